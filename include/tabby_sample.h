@@ -1,0 +1,182 @@
+/*
+ * tabby_sample.h -- C ABI of the B200 token sampler (libtabbysample.so).
+ *
+ * Drop-in for the GPU sampling path of xOAviOx/tabby ("browser-llm"). The reference
+ * splits that path in two:
+ *   - device side: ForwardPass.encodeSampling (src/engine/forward.ts:520-601) records
+ *     reduce_max, reduce_sumexp and k rounds of topk_partial/topk_select
+ *     (src/shaders/*.wgsl) and reads back [maxLogit, sumExp, (value, index) * k]
+ *     (forward.ts:126-157) as a TopKResult (forward.ts:94-103);
+ *   - host side: sampleFromTopK(top, params, random) (src/engine/sampler.ts:147-212)
+ *     turns that block into a SampleOutcome, with the candidate pool sized by the
+ *     worker's rule (src/worker/inference.worker.ts:120-123).
+ * This library runs both halves on the GPU, batched over rows, in one launch.
+ *
+ * Conventions: every function returns a tabby_status; on failure tabby_last_error()
+ * returns a message for the calling thread. Pointers named d_* are device pointers,
+ * h_* host pointers. `stream` is a cudaStream_t passed as void* (NULL = legacy stream).
+ * Nothing here aborts the process. A sampler handle is bound to one device and is not
+ * thread-safe: use one handle per thread or stream.
+ */
+#ifndef TABBY_SAMPLE_H
+#define TABBY_SAMPLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TABBY_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define TABBY_API __attribute__((visibility("default")))
+#else
+#define TABBY_API
+#endif
+
+/* Largest candidate pool the kernels extract. The reference caps k at MAX_TOP_K = 64
+ * (src/engine/kernels.ts:448); this build raises the cap to 1024 and keeps 64 as the
+ * default so an unmodified caller sees the reference's behaviour. */
+#define TABBY_MAX_TOP_K_LIMIT 1024
+#define TABBY_DEFAULT_MAX_TOP_K 64
+/* Local pool each vocab shard contributes in the sharded path. */
+#define TABBY_SHARD_TOP_K 64
+
+typedef enum tabby_status {
+  TABBY_OK = 0,
+  TABBY_EINVAL = 1,    /* bad argument: ForwardError / RangeError in the reference */
+  TABBY_ECUDA = 2,     /* a CUDA runtime call failed */
+  TABBY_ENOMEM = 3,    /* device or pinned allocation failed */
+  TABBY_EINPUT = 4,    /* a logits row held NaN, +-inf or a value <= -3.0e38 */
+  TABBY_ETIMEOUT = 5,  /* a bounded device-side wait gave up; the context stays usable */
+  TABBY_EEMPTY = 6     /* 'sampleFromTopK: empty candidate set' (sampler.ts:153) */
+} tabby_status;
+
+/* SamplingParams (sampler.ts:83-91) minus `seed`: the caller draws one uniform per row
+ * from its SeededRandom and passes it in `uniforms`. */
+typedef struct tabby_sampling_params {
+  double temperature; /* <= 0 selects the argmax (sampler.ts:159-167) */
+  double top_p;       /* nucleus threshold; >= 1 disables it (sampler.ts:175) */
+  int32_t top_k;      /* pool size request; 0 = the sampler's max_top_k (worker :120-123) */
+  int32_t reserved;   /* must be 0 */
+} tabby_sampling_params; /* 24 bytes */
+
+/* SampleOutcome (sampler.ts:121-135) plus the TopKResult statistics it came from. */
+typedef struct tabby_sample_outcome {
+  int32_t id;               /* sampled token id */
+  int32_t considered_count; /* candidates that survived top-p */
+  double probability;       /* full-vocabulary probability of `id` */
+  double pool_mass;         /* full-vocabulary mass held by the pool */
+  int32_t pool_exhausted;   /* 1 when top-p asked for more mass than the pool held */
+  int32_t pool_size;        /* k actually extracted: min(pool rule, vocab) */
+  float max_logit;          /* TopKResult.maxLogit */
+  float sum_exp;            /* TopKResult.sumExp: sum(exp(x - maxLogit)), f32 */
+  int32_t status;           /* tabby_status of this row */
+  int32_t reserved;
+} tabby_sample_outcome; /* 48 bytes */
+
+typedef struct tabby_sampler_config {
+  int32_t device;     /* CUDA device ordinal the handle is bound to */
+  int32_t max_top_k;  /* MAX_TOP_K: 1..TABBY_MAX_TOP_K_LIMIT (0 = default 64) */
+  int32_t max_rows;   /* capacity of the host-buffer entry points (0 = 256) */
+  int32_t max_vocab;  /* capacity of the host-buffer entry points (0 = 151936) */
+} tabby_sampler_config;
+
+typedef struct tabby_sampler tabby_sampler;
+
+/* ABI version of the loaded library (TABBY_ABI_VERSION). */
+TABBY_API int32_t tabby_abi_version(void);
+
+/* Thread-local message for the last failing call on this thread ("" if none). */
+TABBY_API const char *tabby_last_error(void);
+
+/* Creates a handle. Replaces ForwardPass.create's sampling buffers (forward.ts:240-248):
+ * device and pinned staging for the host-buffer entry points are owned by the handle. */
+TABBY_API int tabby_sampler_create(const tabby_sampler_config *config, tabby_sampler **out);
+
+/* Frees everything the handle owns (ForwardPass.destroy, forward.ts:311-317). */
+TABBY_API int tabby_sampler_destroy(tabby_sampler *sampler);
+
+/*
+ * The batched sampler, all buffers on the device, asynchronous on `stream`.
+ * Per row r (logits row at d_logits + r * row_stride, `vocab` floats):
+ *   k = pool rule(params[r].temperature, params[r].top_k, max_top_k), clipped to vocab;
+ *   maxLogit, sumExp, exact top-k by (value desc, index asc) on the raw logits
+ *     (forward.ts:520-601, the four sampling WGSL kernels);
+ *   sampleFromTopK(top, params[r], u = d_uniforms[r]) (sampler.ts:147-212) in float64.
+ * Writes d_out[r]; when d_topk_ids / d_topk_values are non-NULL also the k candidates
+ * (ids int32, raw logits f32) at stride topk_ld (>= max_top_k) in candidate order.
+ * Per-row failures (non-finite logits) are reported in d_out[r].status.
+ * Requirements: d_logits 4-byte aligned, row_stride >= vocab, 1 <= vocab <= 2^30.
+ */
+TABBY_API int tabby_sample_rows_async(tabby_sampler *sampler, const float *d_logits, int64_t row_stride,
+                            int32_t rows, int32_t vocab, const tabby_sampling_params *d_params,
+                            const double *d_uniforms, tabby_sample_outcome *d_out,
+                            int32_t *d_topk_ids, float *d_topk_values, int32_t topk_ld,
+                            void *stream);
+
+/*
+ * Same computation from and to HOST buffers: copies logits/params/uniforms in, runs,
+ * copies outcomes (and candidates when h_topk_ids/h_topk_values are non-NULL) back and
+ * synchronises. Returns the first failing row's status (TABBY_EINPUT, ...) if any.
+ * rows <= max_rows and vocab <= max_vocab of the handle; row_stride is the host stride.
+ * This is the call sampler.ts's sample() reaches through the N-API addon.
+ */
+TABBY_API int tabby_sample_rows(tabby_sampler *sampler, const float *h_logits, int64_t row_stride,
+                      int32_t rows, int32_t vocab, const tabby_sampling_params *h_params,
+                      const double *h_uniforms, tabby_sample_outcome *h_out,
+                      int32_t *h_topk_ids, float *h_topk_values, int32_t topk_ld);
+
+/*
+ * Top-k block only, the TopKResult of ForwardPass.runFull(ids, {topK: k})
+ * (forward.ts:339-350, 430-448): per row writes (2 + 2k) 32-bit words at
+ * d_block + r * block_ld:  [maxLogit, sumExp, (value f32, index u32 bits) * k]
+ * exactly as topk_select.wgsl:60-64 lays them out. 0 <= k <= max_top_k, k <= vocab
+ * (k > max_top_k is rejected like forward.ts:348-351); block_ld >= 2 + 2k.
+ * Row failures set maxLogit to NaN.
+ */
+TABBY_API int tabby_topk_rows_async(tabby_sampler *sampler, const float *d_logits, int64_t row_stride,
+                          int32_t rows, int32_t vocab, int32_t k, float *d_block,
+                          int32_t block_ld, void *stream);
+
+/*
+ * Vocab-sharded sampling, step 1 (new in this build; the reference has no multi-GPU
+ * path). This rank holds columns [vocab_offset, vocab_offset + shard_vocab) of every
+ * row. Writes per row (2 + 2 * TABBY_SHARD_TOP_K) words at d_block + r * block_ld:
+ * [local max, local sum(exp(x - local max)), (value, GLOBAL index bits) * 64], unused
+ * slots padded with (-inf, 0xffffffff). The blocks of all ranks are then all-gathered.
+ */
+TABBY_API int tabby_shard_local_async(tabby_sampler *sampler, const float *d_logits, int64_t row_stride,
+                            int32_t rows, int32_t shard_vocab, int64_t vocab_offset,
+                            float *d_block, int32_t block_ld, void *stream);
+
+/*
+ * Vocab-sharded sampling, step 2: d_gathered holds `shards` blocks per row as
+ * all-gathered rank-major: block of (shard s, row r) at d_gathered + (s*rows + r)*block_ld.
+ * Merges (max, sum-exp) pairs as M = max m_s, S = sum s_s exp(m_s - M), takes the global
+ * top-k of the candidates by (value desc, global index asc), and runs sampleFromTopK
+ * with params[r] and uniforms[r]. Pool sizes above TABBY_SHARD_TOP_K are clipped to it.
+ */
+TABBY_API int tabby_shard_merge_async(tabby_sampler *sampler, const float *d_gathered, int32_t shards,
+                            int32_t rows, int32_t block_ld, const tabby_sampling_params *d_params,
+                            const double *d_uniforms, tabby_sample_outcome *d_out,
+                            int32_t *d_topk_ids, float *d_topk_values, int32_t topk_ld,
+                            void *stream);
+
+/*
+ * Host-side sampleFromTopK on a TopKResult (sampler.ts:147-212) with the same float64
+ * arithmetic the device finalize uses; no GPU involved. For callers that already hold
+ * a TopKResult (e.g. from tabby_topk_rows_async).
+ */
+TABBY_API int tabby_sample_from_topk(const int32_t *ids, const float *logits, int32_t n, float max_logit,
+                           float sum_exp, const tabby_sampling_params *params, double uniform,
+                           tabby_sample_outcome *out);
+
+/* Pool-size rule of the worker (inference.worker.ts:120-123) with the handle's cap. */
+TABBY_API int32_t tabby_pool_size(double temperature, int32_t top_k, int32_t max_top_k);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TABBY_SAMPLE_H */
