@@ -1,0 +1,336 @@
+"""Benchmark of the B200 token sampler (one JSON line on rank 0).
+
+A step is one batched sampling pass -- max, sum-exp, exact top-k, top-p and the seeded
+draw for every row -- over one batch of seeded synthetic logits.
+
+  N=1 workload: B=256 x V=151936 fp32 rows with heterogeneous per-row parameters (the
+  "c4" configuration: bf16(N(0,4^2)) logits, 5% spiked rows, T~U[0.3,1.5],
+  top-k in {0,20,100,1000}, top-p~U[0.5,1]); pool cap MAX_TOP_K = 1024.
+  N>1 (torchrun, one rank per GPU): batch rows split across GPUs, no data-path
+  collective (weak scaling: every rank samples its own 256 rows per step).
+
+  value      rows/s over all ranks, logits already in HBM, device-timed with CUDA events
+             on the launch stream, max over ranks. Inputs rotate over 4 batches (622 MB,
+             larger than the 126 MB L2) so every step reads HBM.
+  e2e        the same metric through the public host-buffer call tabby_sample_rows():
+             pinned host logits -> device, sample, outcomes -> host, every step.
+  roofline   algorithmic bytes = B * V * 4 per launch (each logit read once) / average
+             launch time, against MEASURED_PEAKS.json hbm_gbs.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--profile]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+ROWS = 256
+VOCAB = 151936
+CAP = 1024
+ROTATE = 4
+WORKLOAD = "c4_heterogeneous_B256_V151936"
+METRIC = "sampled rows/s (B=256 x V=151936 fp32 logits, heterogeneous T/top-k/top-p)"
+NOMINAL_HBM_GBS = 8000.0
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
+            int(os.environ.get("WORLD_SIZE", "1")))
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per launch of the dominant kernel on this workload, from the committed
+    ncu summary (a line `traffic_bytes_per_launch: N`)."""
+    path = os.path.join(ROOT, "profiles", "stream_kernel_c4_B256.md")
+    try:
+        with open(path) as f:
+            m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", f.read())
+        return int(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled every 200 ms while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int, enabled: bool = True):
+        self.gpu = gpu
+        self.lines = []
+        self.proc = None
+        self.enabled = enabled
+
+    def __enter__(self):
+        if not self.enabled:
+            return self
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_reference(x, params, u, seconds=10.0):
+    """The reference CPU path (full sort + sampleFromTopK per row, oracle restatement)
+    on all host cores over a bounded sample of the workload's rows."""
+    from oracle import oracle
+
+    threads = os.cpu_count() or 1
+    rows_done, elapsed, reps = 0, 0.0, 0
+    chunk = max(threads * 2, 16)
+    r0 = 0
+    while elapsed < seconds and reps < 1000:
+        sl = slice(r0, r0 + chunk)
+        elapsed += oracle.bench_rows(x[sl], params[sl], u[sl], CAP, threads)
+        rows_done += x[sl].shape[0]
+        r0 = (r0 + chunk) % x.shape[0]
+        reps += 1
+    return rows_done / elapsed, threads, f"{rows_done} rows of the workload in {elapsed:.1f} s"
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    from tabby_b200 import synth
+
+    x, p, u = synth.config("c4", seed=0)
+    vals = []
+    # Bound the whole run to a few minutes whatever --steps/--warmup ask for.
+    per_step = max(0.05, min(2.0, 150.0 / (args.warmup + args.steps)))
+    threads, sample = 1, ""
+    for i in range(args.warmup + args.steps):
+        rate, threads, sample = cpu_reference(x, p, u, seconds=per_step)
+        if i >= args.warmup:
+            vals.append(rate)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * ROWS / value, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32/f64", "data": "synthetic (seeded)",
+        "config": {"workload": WORKLOAD, "rows": ROWS, "vocab": VOCAB, "max_top_k": CAP},
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port",
+                         "sample": sample + " per step (C restatement of sampler.ts topK "
+                         "full sort + sampleFromTopK; Node is absent)"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, rank, local_rank, world):
+    import torch
+
+    from tabby_b200 import Sampler, synth
+    from tabby_b200._lib import OUTCOME_DTYPE, check, lib
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev)
+        pg = dist
+
+    x, p, u = synth.config("c4", seed=rank)
+    sampler = Sampler(local_rank, max_top_k=CAP, max_rows=ROWS, max_vocab=VOCAB)
+    h = sampler.handle
+    # ROTATE resident batches (row-shifted copies) so consecutive steps miss L2.
+    xt = torch.from_numpy(x)
+    batches = [torch.roll(xt, shifts=i, dims=0).to(dev) for i in range(ROTATE)]
+    p_dev = torch.from_numpy(p.view(np.uint8).copy()).to(dev)
+    u_dev = torch.from_numpy(u).to(dev)
+    out = torch.empty(ROWS * OUTCOME_DTYPE.itemsize, dtype=torch.uint8, device=dev)
+    ids = torch.empty((ROWS, CAP), dtype=torch.int32, device=dev)
+    vals = torch.empty((ROWS, CAP), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+    L = lib()
+
+    def step(i):
+        b = batches[i % ROTATE]
+        check(L.tabby_sample_rows_async(h, b.data_ptr(), VOCAB, ROWS, VOCAB, p_dev.data_ptr(),
+                                        u_dev.data_ptr(), out.data_ptr(), ids.data_ptr(),
+                                        vals.data_ptr(), CAP, sptr))
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize(dev)
+
+    with ClockSampler(local_rank, enabled=not args.profile) as clocks:
+        for i in range(args.warmup):
+            step(i)
+        # Keep the GPU loaded ~1 s before timing so the clock record reflects steady state.
+        t_end = time.perf_counter() + (0.0 if args.profile else 1.0)
+        i = 0
+        while time.perf_counter() < t_end:
+            for _ in range(200):
+                step(i)
+                i += 1
+            torch.cuda.synchronize(dev)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+        barrier()
+        ms = e0.elapsed_time(e1)
+    if pg is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = world * ROWS * args.steps / (ms / 1e3)
+
+    # End-to-end through the public host-buffer API: pinned host logits in, outcomes out.
+    e2e_steps = 0 if args.profile else max(3, min(args.steps, 50))
+    e2e_value = None
+    hout = np.zeros(ROWS, OUTCOME_DTYPE)
+    if e2e_steps:
+        host = torch.from_numpy(x).pin_memory()
+        hp = p.copy()
+        hu = u.copy()
+        for _ in range(2):
+            check(L.tabby_sample_rows(h, host.data_ptr(), VOCAB, ROWS, VOCAB, hp.ctypes.data,
+                                      hu.ctypes.data, hout.ctypes.data, None, None, 0))
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            check(L.tabby_sample_rows(h, host.data_ptr(), VOCAB, ROWS, VOCAB, hp.ctypes.data,
+                                      hu.ctypes.data, hout.ctypes.data, None, None, 0))
+        e2e_s = time.perf_counter() - t0
+        if pg is not None:
+            t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            e2e_s = float(t.item())
+        e2e_value = world * ROWS * e2e_steps / e2e_s
+
+    result = None
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        bytes_per_launch = ROWS * VOCAB * 4
+        achieved = bytes_per_launch / (ms_per_step / 1e3) / 1e9
+        result = {
+            "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (selection, sum-exp) / f64 (sampleFromTopK)",
+            "data": "synthetic (seeded bf16-valued N(0,4^2) logits, heterogeneous params)",
+            "config": {"workload": WORKLOAD, "rows_per_gpu": ROWS, "vocab": VOCAB,
+                       "max_top_k": CAP, "parallelism": f"rows split x{world}, no collective",
+                       "l2": f"inputs rotate over {ROTATE} resident batches "
+                             f"({ROTATE * bytes_per_launch / 1e6:.0f} MB > 126 MB L2)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS,
+                         "traffic": profiled_traffic(),
+                         "algorithmic_bytes_per_launch": bytes_per_launch,
+                         "kernel": "stream_kernel"},
+            "e2e": {"value": e2e_value, "unit": "rows/s",
+                    "h2d_bytes_per_step": ROWS * VOCAB * 4 + p.nbytes + u.nbytes,
+                    "d2h_bytes_per_step": hout.nbytes, "steps": e2e_steps,
+                    "call": "tabby_sample_rows (pinned host buffers, synchronous)"},
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(),
+        }
+    if pg is not None:
+        pg.barrier()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline and not args.profile:
+            rate, threads, sample = cpu_reference(x, p, u, seconds=args.cpu_seconds)
+            result["cpu_baseline"] = {
+                "value": rate, "unit": "rows/s", "cores": threads, "kind": "port",
+                "sample": sample + " (C restatement of sampler.ts topK full sort + "
+                "sampleFromTopK, all host threads)"}
+        print(json.dumps(result), flush=True)
+    sampler.close()
+    if pg is not None:
+        pg.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="only warm-up + timed steps (for ncu): no heat loop, e2e or CPU leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank, local_rank, world = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    return run_ours(args, rank, local_rank, world)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -44,14 +44,20 @@ def _stale() -> bool:
     return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and not _stale():
+def build(force: bool = False, verbose: bool = False, out: str | None = None,
+          defines: tuple = ()) -> str:
+    """Compile SOURCES into `out` (default: the in-tree library). `defines` adds -D flags
+    (e.g. TABBY_TRACE=1 for the phase-timestamp build used while tuning)."""
+    lib_path = out or LIB
+    if out is None and not force and not _stale():
         return LIB
-    os.makedirs(LIBDIR, exist_ok=True)
+    libdir = os.path.dirname(lib_path)
+    os.makedirs(libdir, exist_ok=True)
     objs = []
     for src in SOURCES:
-        obj = os.path.join(LIBDIR, os.path.splitext(src)[0] + ".o")
-        cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-I", CSRC,
+        obj = os.path.join(libdir, os.path.splitext(src)[0] + ".o")
+        cmd = [nvcc(), *ARCH, *NVCC_FLAGS, *[f"-D{d}" for d in defines],
+               "-I", os.path.join(ROOT, "include"), "-I", CSRC,
                "-c", os.path.join(CSRC, src), "-o", obj]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
@@ -59,16 +65,16 @@ def build(force: bool = False, verbose: bool = False) -> str:
         if verbose:
             sys.stderr.write(r.stderr)
         objs.append(obj)
-    tmp = LIB + ".tmp"
+    tmp = lib_path + ".tmp"
     cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs,
            "-Xlinker", "--exclude-libs,ALL"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
-    os.replace(tmp, LIB)
+    os.replace(tmp, lib_path)
     for o in objs:
         os.remove(o)
-    return LIB
+    return lib_path
 
 
 if __name__ == "__main__":
