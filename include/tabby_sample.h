@@ -157,6 +157,7 @@ TABBY_API int tabby_shard_local_async(tabby_sampler *sampler, const float *d_log
  * Merges (max, sum-exp) pairs as M = max m_s, S = sum s_s exp(m_s - M), takes the global
  * top-k of the candidates by (value desc, global index asc), and runs sampleFromTopK
  * with params[r] and uniforms[r]. Pool sizes above TABBY_SHARD_TOP_K are clipped to it.
+ * 1 <= shards <= 16.
  */
 TABBY_API int tabby_shard_merge_async(tabby_sampler *sampler, const float *d_gathered, int32_t shards,
                             int32_t rows, int32_t block_ld, const tabby_sampling_params *d_params,

@@ -11,12 +11,15 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
+
 #include "sampler_internal.h"
 #include "tabby_sample.h"
 
+using tabby::MergeLaunch;
 using tabby::RowGeometry;
 using tabby::RowLaunch;
-using tabby::MergeLaunch;
+using tabby::Scratch;
 
 struct tabby_sampler {
   int32_t device;
@@ -24,8 +27,7 @@ struct tabby_sampler {
   int32_t max_rows;
   int32_t max_vocab;
   int32_t sms;
-  int32_t smem_optin;
-  int32_t max_cluster;  // 16 when clusters of 16 CTAs fit, else 8
+  Scratch scratch;  // per-row / per-slice state of the row kernel
   cudaStream_t stream;  // used by the host-buffer entry points
   float *d_logits;
   tabby_sampling_params *d_params;
@@ -89,15 +91,32 @@ int check_params_host(const tabby_sampling_params *p, int32_t rows) {
   return TABBY_OK;
 }
 
-// Picks a geometry and launches; falls back from clusters of 16 to 8 if the former
-// cannot be scheduled.
+// Launches the row kernel over `rows` rows in batches of the scratch capacity.
 cudaError_t plan_and_launch(const tabby_sampler *s, const RowLaunch &l, cudaStream_t stream) {
-  RowGeometry geo;
-  int cap = l.mode == tabby::kModeSample ? l.cap : l.fixed_k;
-  cudaError_t err = tabby::plan_rows(s->sms, s->smem_optin, l.rows, l.vocab, cap, s->max_cluster,
-                                     &geo);
-  if (err != cudaSuccess) return err;
-  return tabby::launch_rows(l, geo, stream);
+  for (int32_t r0 = 0; r0 < l.rows; r0 += s->scratch.max_rows) {
+    RowLaunch b = l;
+    b.rows = std::min(l.rows - r0, s->scratch.max_rows);
+    b.logits = l.logits + (int64_t)r0 * l.row_stride;
+    if (b.params) b.params = l.params + r0;
+    if (b.uniforms) b.uniforms = l.uniforms + r0;
+    if (b.out) b.out = l.out + r0;
+    if (b.topk_ids) b.topk_ids = l.topk_ids + (int64_t)r0 * l.topk_ld;
+    if (b.topk_values) b.topk_values = l.topk_values + (int64_t)r0 * l.topk_ld;
+    if (b.block) b.block = l.block + (int64_t)r0 * l.block_ld;
+    RowGeometry geo;
+    cudaError_t err = tabby::plan_rows(s->sms, b.rows, b.vocab, s->cap, &geo);
+    if (err != cudaSuccess) return err;
+    if (geo.nslices > s->scratch.max_slices) return cudaErrorInvalidValue;
+    err = tabby::launch_rows(b, geo, s->scratch, stream);
+    if (err != cudaSuccess) return err;
+  }
+  return cudaSuccess;
+}
+
+int check_vocab_capacity(const tabby_sampler *s, int32_t vocab) {
+  if (vocab > s->max_vocab)
+    return fail(TABBY_EINVAL, "vocab %d exceeds the handle's max_vocab %d", vocab, s->max_vocab);
+  return TABBY_OK;
 }
 
 }  // namespace
@@ -148,20 +167,14 @@ int tabby_sampler_create(const tabby_sampler_config *config, tabby_sampler **out
   s->max_rows = c.max_rows;
   s->max_vocab = c.max_vocab;
   s->sms = prop.multiProcessorCount;
-  s->smem_optin = (int32_t)prop.sharedMemPerBlockOptin;
-  s->max_cluster = 8;
-  {
-    // Clusters of 16 are a non-portable size; use them only where they schedule.
-    RowGeometry geo;
-    if (tabby::plan_rows(s->sms, s->smem_optin, 1, c.max_vocab, s->cap, 16, &geo) ==
-            cudaSuccess &&
-        geo.cluster == 16) {
-      int n = 0;
-      if (tabby::max_active_clusters(geo, &n) == cudaSuccess && n > 0) s->max_cluster = 16;
-    }
-    cudaGetLastError();
-  }
+  const int32_t cand_ld = std::max(c.max_top_k, (int32_t)TABBY_SHARD_TOP_K);
+  const int32_t nsl = tabby::max_slices(c.max_vocab, c.max_top_k);
   const size_t nlog = (size_t)c.max_rows * (size_t)c.max_vocab;
+  const size_t nsr = (size_t)c.max_rows * (size_t)nsl;
+  Scratch &scr = s->scratch;
+  scr.cand_ld = cand_ld;
+  scr.max_rows = c.max_rows;
+  scr.max_slices = nsl;
   if ((err = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking)) != cudaSuccess ||
       (err = cudaMalloc(&s->d_logits, nlog * sizeof(float))) != cudaSuccess ||
       (err = cudaMalloc(&s->d_params, (size_t)c.max_rows * sizeof(tabby_sampling_params))) !=
@@ -172,7 +185,19 @@ int tabby_sampler_create(const tabby_sampler_config *config, tabby_sampler **out
       (err = cudaMalloc(&s->d_ids, (size_t)c.max_rows * c.max_top_k * sizeof(int32_t))) !=
           cudaSuccess ||
       (err = cudaMalloc(&s->d_values, (size_t)c.max_rows * c.max_top_k * sizeof(float))) !=
-          cudaSuccess) {
+          cudaSuccess ||
+      (err = cudaMalloc(&scr.row_count, (size_t)c.max_rows * sizeof(uint32_t))) != cudaSuccess ||
+      (err = cudaMalloc(&scr.row_tau, (size_t)c.max_rows * sizeof(unsigned long long))) !=
+          cudaSuccess ||
+      (err = cudaMalloc(&scr.slice_stats, nsr * sizeof(float2))) != cudaSuccess ||
+      (err = cudaMalloc(&scr.slice_meta, nsr * sizeof(uint2))) != cudaSuccess ||
+      (err = cudaMalloc(&scr.slice_cand, nsr * cand_ld * sizeof(unsigned long long))) !=
+          cudaSuccess ||
+      (err = cudaMemset(scr.row_count, 0, (size_t)c.max_rows * sizeof(uint32_t))) !=
+          cudaSuccess ||
+      (err = cudaMemset(scr.row_tau, 0, (size_t)c.max_rows * sizeof(unsigned long long))) !=
+          cudaSuccess ||
+      (err = cudaDeviceSynchronize()) != cudaSuccess) {
     tabby_sampler_destroy(s);
     cudaGetLastError();
     return fail(TABBY_ENOMEM, "allocation of sampler buffers failed: %s", cudaGetErrorString(err));
@@ -190,6 +215,11 @@ int tabby_sampler_destroy(tabby_sampler *s) {
   if (s->d_out) cudaFree(s->d_out);
   if (s->d_ids) cudaFree(s->d_ids);
   if (s->d_values) cudaFree(s->d_values);
+  if (s->scratch.row_count) cudaFree(s->scratch.row_count);
+  if (s->scratch.row_tau) cudaFree(s->scratch.row_tau);
+  if (s->scratch.slice_stats) cudaFree(s->scratch.slice_stats);
+  if (s->scratch.slice_meta) cudaFree(s->scratch.slice_meta);
+  if (s->scratch.slice_cand) cudaFree(s->scratch.slice_cand);
   if (s->stream) cudaStreamDestroy(s->stream);
   delete s;
   return TABBY_OK;
@@ -206,6 +236,7 @@ int tabby_sample_rows_async(tabby_sampler *s, const float *d_logits, int64_t row
     return fail(TABBY_EINVAL, "params, uniforms and out must not be NULL");
   if ((d_topk_ids || d_topk_values) && topk_ld < s->cap)
     return fail(TABBY_EINVAL, "topk_ld (%d) must be >= max_top_k (%d)", topk_ld, s->cap);
+  if ((st = check_vocab_capacity(s, vocab))) return st;
   DeviceScope scope(s->device);
   if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
   RowLaunch l;
@@ -223,7 +254,7 @@ int tabby_sample_rows_async(tabby_sampler *s, const float *d_logits, int64_t row
   l.topk_ld = topk_ld;
   cudaError_t err = plan_and_launch(s, l, (cudaStream_t)stream);
   if (err == cudaErrorInvalidValue && vocab > 0)
-    return fail(TABBY_EINVAL, "vocab %d does not fit the row kernel's shared memory", vocab);
+    return fail(TABBY_EINVAL, "vocab %d needs more slices than the handle's scratch holds", vocab);
   if (err != cudaSuccess) return cuda_fail(err, "row_kernel launch");
   return TABBY_OK;
 }
@@ -302,6 +333,7 @@ int tabby_topk_rows_async(tabby_sampler *s, const float *d_logits, int64_t row_s
   if (rows > 0 && !d_block) return fail(TABBY_EINVAL, "block is NULL");
   if (block_ld < 2 + 2 * k)
     return fail(TABBY_EINVAL, "block_ld (%d) must be >= 2 + 2k (%d)", block_ld, 2 + 2 * k);
+  if ((st = check_vocab_capacity(s, vocab))) return st;
   DeviceScope scope(s->device);
   if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
   RowLaunch l;
@@ -316,7 +348,7 @@ int tabby_topk_rows_async(tabby_sampler *s, const float *d_logits, int64_t row_s
   l.block_ld = block_ld;
   cudaError_t err = plan_and_launch(s, l, (cudaStream_t)stream);
   if (err == cudaErrorInvalidValue)
-    return fail(TABBY_EINVAL, "vocab %d does not fit the row kernel's shared memory", vocab);
+    return fail(TABBY_EINVAL, "vocab %d needs more slices than the handle's scratch holds", vocab);
   if (err != cudaSuccess) return cuda_fail(err, "row_kernel launch");
   return TABBY_OK;
 }
@@ -331,6 +363,7 @@ int tabby_shard_local_async(tabby_sampler *s, const float *d_logits, int64_t row
   if (rows > 0 && !d_block) return fail(TABBY_EINVAL, "block is NULL");
   if (block_ld < 2 + 2 * TABBY_SHARD_TOP_K)
     return fail(TABBY_EINVAL, "block_ld (%d) must be >= %d", block_ld, 2 + 2 * TABBY_SHARD_TOP_K);
+  if ((st = check_vocab_capacity(s, shard_vocab))) return st;
   DeviceScope scope(s->device);
   if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
   RowLaunch l;
@@ -346,7 +379,7 @@ int tabby_shard_local_async(tabby_sampler *s, const float *d_logits, int64_t row
   l.block_ld = block_ld;
   cudaError_t err = plan_and_launch(s, l, (cudaStream_t)stream);
   if (err == cudaErrorInvalidValue)
-    return fail(TABBY_EINVAL, "shard vocab %d does not fit the row kernel's shared memory",
+    return fail(TABBY_EINVAL, "shard vocab %d needs more slices than the handle's scratch holds",
                 shard_vocab);
   if (err != cudaSuccess) return cuda_fail(err, "row_kernel launch");
   return TABBY_OK;
@@ -358,7 +391,7 @@ int tabby_shard_merge_async(tabby_sampler *s, const float *d_gathered, int32_t s
                             int32_t *d_topk_ids, float *d_topk_values, int32_t topk_ld,
                             void *stream) {
   if (!s) return fail(TABBY_EINVAL, "sampler is NULL");
-  if (shards < 1 || shards > 64) return fail(TABBY_EINVAL, "shards must be in [1, 64]");
+  if (shards < 1 || shards > 16) return fail(TABBY_EINVAL, "shards must be in [1, 16]");
   if (rows < 0) return fail(TABBY_EINVAL, "rows must be >= 0");
   if (block_ld < 2 + 2 * TABBY_SHARD_TOP_K)
     return fail(TABBY_EINVAL, "block_ld (%d) must be >= %d", block_ld, 2 + 2 * TABBY_SHARD_TOP_K);

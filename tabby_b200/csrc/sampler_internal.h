@@ -47,20 +47,32 @@ struct MergeLaunch {
   int32_t topk_ld = 0;
 };
 
-// Geometry the row kernel will use for (rows, vocab) on `device`: cluster size and
-// shared memory. Returns cudaSuccess or the error that ruled every geometry out.
+// Geometry of one stream_kernel launch: the row is cut into `nslices` slices of
+// `slice` logits, one CTA each.
 struct RowGeometry {
-  int32_t cluster = 1;
-  int32_t slice = 0;       // logits per CTA (multiple of 4)
-  int32_t data_floats = 0; // shared-memory data region, floats
+  int32_t slice = 0;        // logits per CTA (multiple of 4)
+  int32_t nslices = 0;      // CTAs per row
+  int32_t data_floats = 0;  // shared-memory staging region, floats
   size_t smem_bytes = 0;
 };
 
-cudaError_t plan_rows(int32_t sms, int32_t max_smem_optin, int32_t rows, int32_t vocab,
-                      int32_t cap, int32_t max_cluster, RowGeometry *geo);
-// Clusters of this geometry that fit on the device at once (0: cannot launch).
-cudaError_t max_active_clusters(const RowGeometry &geo, int *count);
-cudaError_t launch_rows(const RowLaunch &a, const RowGeometry &geo, cudaStream_t stream);
+// Global scratch of the row kernel, owned by the sampler handle. Row counters and
+// thresholds must be zero before a launch; the kernel leaves them zero again.
+struct Scratch {
+  uint32_t *row_count = nullptr;             // [max_rows] slices finished
+  unsigned long long *row_tau = nullptr;     // [max_rows] exact lower bound of the k-th
+  float2 *slice_stats = nullptr;             // [max_rows * max_slices] (max, sum-exp)
+  uint2 *slice_meta = nullptr;               // [max_rows * max_slices] (count, flags)
+  unsigned long long *slice_cand = nullptr;  // [max_rows * max_slices * cand_ld]
+  int32_t cand_ld = 0;                       // candidates a slice may write (>= k)
+  int32_t max_rows = 0;
+  int32_t max_slices = 0;
+};
+
+int32_t max_slices(int32_t vocab, int32_t cap);
+cudaError_t plan_rows(int32_t sms, int32_t rows, int32_t vocab, int32_t cap, RowGeometry *geo);
+cudaError_t launch_rows(const RowLaunch &a, const RowGeometry &geo, const Scratch &scr,
+                        cudaStream_t stream);
 cudaError_t launch_merge(const MergeLaunch &a, cudaStream_t stream);
 
 // Host float64 finalize with the device's arithmetic (sampler.ts:147-212).

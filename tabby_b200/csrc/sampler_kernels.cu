@@ -2,65 +2,103 @@
 //
 // Replaces the reference's sampling dispatches (xOAviOx/tabby src/engine/forward.ts
 // :520-601): a logits copy, reduce_max x2, reduce_sumexp x2 and k rounds of
-// topk_partial + topk_select, i.e. k+4 passes over the row. Here each row is read from
-// HBM once:
+// topk_partial + topk_select, i.e. k+4 passes over the row. Here every logit is read
+// from HBM once, in one streaming pass:
 //
-//   row_kernel   one thread-block cluster of C CTAs per row. CTA q stages columns
-//                [q*slice, (q+1)*slice) in shared memory with 1-D TMA bulk copies
-//                (cp.async.bulk, mbarrier completion) and, while the chunks land,
-//                takes the max and an 11-bit digit histogram of order-preserving keys.
-//                The cluster merges histograms in rank 0's shared memory over DSMEM
-//                and picks the digit bucket that holds the k-th largest key (radix
-//                select, digits 11/11/10 bits, at most three levels). Later passes run
-//                over shared memory only: sum(exp(x - max)), the next digit histogram,
-//                and finally the gather of the candidates into rank 0, which sorts
-//                them by (value desc, index asc) and runs sampleFromTopK in float64.
-//   merge_kernel the vocab-sharded finish: merges all-gathered per-shard blocks.
+//   stream_kernel  one CTA per (row, slice); a slice is the whole row when the batch
+//                  fills the GPU. The slice streams through an 8-stage shared-memory ring
+//                  (2K logits a stage, 16-byte cp.async copies kept 7 stages ahead) and
+//                  is consumed step by step as it lands: online max and
+//                  sum(exp(x - max)) per thread, and a filter that keeps only logits
+//                  whose 64-bit composite (order-preserving key, inverted index) reaches
+//                  the current threshold. The threshold is an exact lower bound on the
+//                  row's k-th largest composite: a CTA whose candidate buffer fills
+//                  compacts it to its k largest by radix select and publishes that
+//                  bound in global memory, where the row's other slices pick it up.
+//                  Each slice writes its <= k candidates and its (max, sum-exp)
+//                  partial; the last CTA of the row to finish merges them, sorts the k
+//                  winners by (value desc, index asc) and runs sampleFromTopK in
+//                  float64 (finalize.cuh).
+//   merge_kernel   the vocab-sharded finish: merges all-gathered per-shard blocks.
 //
 // Selection works on the raw logits; temperature only enters the float64 finalize,
 // exactly as sampler.ts:144-146 and :170 do. Ties go to the lower index, as
-// topk_partial.wgsl:40-42 and sampler.ts:28 order them.
-#include <cooperative_groups.h>
+// topk_partial.wgsl:40-42 and sampler.ts:28 order them: the composite
+// (key << 32 | ~index) is unique per logit and orders exactly like that.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "finalize.cuh"
 #include "sampler_internal.h"
-
-namespace cg = cooperative_groups;
 
 namespace tabby {
 
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
-constexpr int kBins = 2048;      // widest radix digit: 11 bits
-constexpr int kCandCap = 2048;   // candidates rank 0 can hold and sort
-constexpr int kChunks = 4;       // bulk-copy chunks per CTA, one mbarrier each
-constexpr int kMaxCluster = 16;
-constexpr int kMergeThreads = 256;
+constexpr int kStepElems = kThreads * 4;  // logits consumed per step (one float4 a thread)
+constexpr int kRing = 8;                  // TMA ring stages of kStepElems logits (64 KB)
+constexpr int kRingFloats = kRing * kStepElems;
+constexpr int kCandCap = 4096;            // candidate buffer (composites) per CTA
+constexpr int kBins = 2048;               // radix digit: 11 bits
+constexpr int kMaxSlices = 32;            // slices of one row (one warp merges their stats)
+constexpr int kMinSlice = 8192;           // logits: below this a row is not split further
+constexpr int kMergeThreads = 512;
 constexpr float kNegSentinel = -3.0e38f;  // NEG_INF of reduce_max.wgsl:13
 
-enum Decide : int32_t { kContinue = 0, kGather = 1, kExact = 2, kNone = 3 };
 enum Flags : uint32_t { kFlagBadInput = 1u, kFlagTimeout = 2u, kFlagBadParams = 4u };
 
-// Per-row cluster state. Every CTA has one; rank 0's copy collects the merges.
-struct RowCtrl {
-  uint32_t max_key;
-  uint32_t flags;
-  uint32_t cand_count;
-  int32_t decision;
-  uint32_t prefix;    // digits fixed before the current level
-  int32_t remaining;  // keys still to take from inside the current prefix bucket
-  uint32_t thresh;    // kGather: take key >= thresh; kExact: the tie key
-  int32_t need;       // kExact: how many tie keys to take, lowest index first
-  uint32_t bucket;    // digit chosen at the deciding level
-  int32_t k_eff;
-  float row_max;
-  float sums[kMaxCluster];
-};
+// Opt-in phase timestamps for tuning builds (-DTABBY_TRACE=1); compiled out otherwise.
+#ifdef TABBY_TRACE
+constexpr int kTraceSlots = 16;
+constexpr int kTraceCtas = 16384;
+__device__ unsigned long long g_trace[kTraceCtas * kTraceSlots];
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#define TRACE(ph)                                                  \
+  do {                                                             \
+    if (threadIdx.x == 0 && blockIdx.x < kTraceCtas)               \
+      g_trace[blockIdx.x * kTraceSlots + (ph)] = globaltimer();    \
+  } while (0)
+#define TRACE_VAL(ph, v)                                                    \
+  do {                                                                      \
+    if (threadIdx.x == 0 && blockIdx.x < kTraceCtas)                        \
+      g_trace[blockIdx.x * kTraceSlots + (ph)] = (unsigned long long)(v);   \
+  } while (0)
+#else
+#define TRACE(ph) \
+  do {            \
+  } while (0)
+#define TRACE_VAL(ph, v) \
+  do {                   \
+  } while (0)
+#endif
+
+// Opt-in self-checks for debugging builds (-DTABBY_CHECKS=1): every shared-memory
+// candidate / histogram write and every TMA copy is validated first; a violation is
+// recorded (first one wins) and the access is skipped instead of faulting.
+#ifdef TABBY_CHECKS
+__device__ unsigned long long g_check[4];  // code, blockIdx, a, b
+__device__ __forceinline__ bool check_ok(bool ok, unsigned code, unsigned long long x,
+                                         unsigned long long y) {
+  if (!ok && atomicCAS(&g_check[0], 0ull, (unsigned long long)code) == 0ull) {
+    g_check[1] = blockIdx.x;
+    g_check[2] = x;
+    g_check[3] = y;
+  }
+  return ok;
+}
+#define CHECK(ok, code, x, y) check_ok((ok), (code), (unsigned long long)(x), (unsigned long long)(y))
+#else
+#define CHECK(ok, code, x, y) ((void)0, true)
+#endif
 
 // ------------------------------------------------------------------------------------
-// Small device helpers
+// Keys and small device helpers
 // ------------------------------------------------------------------------------------
 
 // Order-preserving key: larger float -> larger key. -0 is folded onto +0 so equal values
@@ -77,6 +115,11 @@ __device__ __forceinline__ float float_of_key(uint32_t k) {
   return __uint_as_float(k ^ mask);
 }
 
+// Unique, totally ordered candidate: value first, then the lower index.
+__device__ __forceinline__ uint64_t composite(uint32_t key, uint32_t idx) {
+  return ((uint64_t)key << 32) | (uint64_t)(~idx);
+}
+
 __device__ __forceinline__ bool bad_logit(float x) {
   // NaN, +-inf and values at or below the reference's -3.0e38 sentinel
   // (topk_select.wgsl:65 masks with it) have no defined result in the reference.
@@ -87,137 +130,29 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
 
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t cluster_nctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ void cluster_arrive() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void cluster_wait() {
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-  cluster_arrive();
-  cluster_wait();
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+// 16-byte asynchronous global -> shared copy (cp.async, L2 only), tracked per thread by
+// commit groups.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
                : "memory");
 }
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
+// 2^x by the MUFU.EX2 approximation (flush-to-zero).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
-// Bounded wait: gives up after ~2^22 polls (each poll may suspend briefly) and reports
-// failure instead of spinning forever.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
-  for (uint32_t i = 0; i < (1u << 22); i++)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
-}
-
-// 1-D TMA bulk copy global -> this CTA's shared memory (no multicast).
-__device__ __forceinline__ void bulk_copy_g2s(void *dst, const void *src, uint32_t bytes,
-                                              uint64_t *bar, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
-      "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
-      : "memory");
-}
-
-__device__ __forceinline__ uint64_t evict_first_policy() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
-
-// Block-wide sum of one float per thread, fixed order (deterministic).
-__device__ float block_sum_f32(float v, float *red) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
-  if (l == 0) red[w] = v;
-  __syncthreads();
-  float total = 0.f;
-  if (threadIdx.x == 0)
-    for (int i = 0; i < kWarps; i++) total += red[i];
-  return total;  // valid in thread 0 only
-}
-
-// Block-wide exclusive prefix sum of one int per thread in thread order.
-__device__ int block_exclusive_scan(int v, int *red, int *total) {
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  int inc = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int n = __shfl_up_sync(0xffffffffu, inc, o);
-    if (l >= o) inc += n;
-  }
-  __syncthreads();
-  if (l == 31) red[w] = inc;
-  __syncthreads();
-  int before = 0, all = 0;
-  for (int i = 0; i < kWarps; i++) {
-    const int s = red[i];
-    before += (i < w) ? s : 0;
-    all += s;
-  }
-  *total = all;
-  return before + inc - v;
-}
-
-// Bitonic sort of a[0, N) descending, N a power of two, in shared memory.
-__device__ void block_sort_desc(uint64_t *a, int N) {
-  for (int size = 2; size <= N; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = threadIdx.x; i < (N >> 1); i += blockDim.x) {
-        const int lo = 2 * i - (i & (stride - 1));
-        const int hi = lo + stride;
-        const bool desc = (lo & size) == 0;
-        const uint64_t x = a[lo], y = a[hi];
-        if ((x < y) == desc) {
-          a[lo] = y;
-          a[hi] = x;
-        }
-      }
-      __syncthreads();
-    }
-  }
+__device__ __forceinline__ uint64_t ld_cg_u64(const unsigned long long *p) {
+  return (uint64_t)__ldcg(p);
 }
 
 __device__ __forceinline__ int next_pow2(int n) {
@@ -235,99 +170,350 @@ __host__ __device__ __forceinline__ int32_t pool_rule(double temperature, int32_
   return k < cap ? k : cap;
 }
 
-// ------------------------------------------------------------------------------------
-// Candidate push into rank 0's shared memory (warp-aggregated slot reservation).
-// ------------------------------------------------------------------------------------
-__device__ __forceinline__ void push_candidate(bool pred, uint32_t key, uint32_t idx,
-                                               uint32_t *r0_count, uint64_t *r0_cand) {
-  const uint32_t mask = __ballot_sync(0xffffffffu, pred);
-  if (mask == 0) return;
-  const int lane = threadIdx.x & 31;
-  const int leader = __ffs(mask) - 1;
-  uint32_t base = 0;
-  if (lane == leader) base = atomicAdd(r0_count, (uint32_t)__popc(mask));
-  base = __shfl_sync(0xffffffffu, base, leader);
-  if (pred) {
-    const uint32_t slot = base + __popc(mask & ((1u << lane) - 1u));
-    if (slot < (uint32_t)kCandCap) r0_cand[slot] = ((uint64_t)key << 32) | (uint64_t)(~idx);
-  }
-}
+// Shared scalars of a CTA (block-uniform values and reduction scratch).
+struct Shared {
+  uint32_t count;   // candidates in the buffer
+  uint32_t count2;  // compaction write cursor
+  uint32_t bucket;
+  uint32_t above;
+  uint32_t inb;
+  uint32_t last;  // this CTA merges the row
+  int32_t cut_claim;
+  int32_t chosen_claim;
+  int32_t fallback;
+  uint32_t flags;
+  uint64_t tau;  // accept composites >= tau
+  float red_f[kWarps];
+  uint32_t red_u[kWarps];
+  double red_d[kWarps];
+  float merge_max;
+  float merge_sum;
+  int32_t off[32];  // merge: first candidate of each slice
+  int32_t cnt[32];  // merge: candidates of each slice
+};
 
 // ------------------------------------------------------------------------------------
-// Rank 0: pick the digit bucket that holds the k-th largest key.
+// Block primitives (blockDim.x == 512)
 // ------------------------------------------------------------------------------------
-__device__ void decide_level(RowCtrl *ctrl, uint32_t *merged, int level, int *red) {
-  const int width = level == 2 ? 10 : 11;
-  const int shift = level == 0 ? 21 : (level == 1 ? 10 : 0);
+
+// Deterministic block sum of one double per thread (fixed shuffle tree, warps in order).
+__device__ double block_sum_f64(double v, Shared *sh) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = JS_ADD(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) sh->red_d[w] = v;
+  __syncthreads();
+  double total = 0.0;
+  for (int i = 0; i < nw; i++) total = JS_ADD(total, sh->red_d[i]);
+  return total;  // same value in every thread
+}
+
+// Exclusive block scan of one double per thread in thread order.
+__device__ double block_exclusive_scan_f64(double v, Shared *sh) {
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  double inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double n = __shfl_up_sync(0xffffffffu, inc, o);
+    if (l >= o) inc = JS_ADD(inc, n);
+  }
+  __syncthreads();
+  if (l == 31) sh->red_d[w] = inc;
+  __syncthreads();
+  double before = 0.0;
+  for (int i = 0; i < w; i++) before = JS_ADD(before, sh->red_d[i]);
+  return JS_ADD(before, JS_SUB(inc, v));
+}
+
+// Finds the digit bucket b holding the R-th largest element of hist (scanning from the
+// top): above = elements in buckets > b, inb = hist[b]. Results land in sh.
+__device__ void find_bucket(const uint32_t *hist, uint32_t R, Shared *sh) {
   const int tid = threadIdx.x;
-  // Inputs of this level, read before anyone can overwrite them.
-  const uint32_t R = (uint32_t)ctrl->remaining;
-  const uint32_t k_eff = (uint32_t)ctrl->k_eff;
-  const uint32_t prefix = ctrl->prefix;
-  // Thread t owns bins [4t, 4t+4); sum of everything above them (descending order).
+  const int lane = tid & 31, w = tid >> 5;
   uint32_t h[4];
   uint32_t mine = 0;
 #pragma unroll
   for (int j = 0; j < 4; j++) {
-    h[j] = merged[4 * tid + j];
+    h[j] = hist[4 * tid + j];
     mine += h[j];
   }
-  // Suffix sum over threads > tid.
-  const int lane = tid & 31, w = tid >> 5;
-  uint32_t inc = mine;
+  uint32_t inc = mine;  // suffix sum over this lane and the lanes above it
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const uint32_t n = __shfl_down_sync(0xffffffffu, inc, o);
     if (lane + o < 32) inc += n;
   }
   __syncthreads();
-  if (lane == 0) red[w] = (int)inc;
-  // No crossing found (inconsistent counts) ends the selection instead of looping.
-  if (tid == 0) ctrl->decision = kNone;
+  if (lane == 0) sh->red_u[w] = inc;
   __syncthreads();
   uint32_t above = inc - mine;
-  for (int i = w + 1; i < kWarps; i++) above += (uint32_t)red[i];
-
+  for (int i = w + 1; i < kWarps; i++) above += sh->red_u[i];
   if (above < R && above + mine >= R) {
-    // The crossing is in this thread's bins: scan them from the top.
     int b = 3;
     for (; b > 0; b--) {
       if (above + h[b] >= R) break;
       above += h[b];
     }
-    const uint32_t bin = 4 * tid + b;
-    const uint32_t inb = h[b];
-    const uint32_t taken = k_eff - R;
-    const uint32_t n_stop = taken + above + inb;
-    const uint32_t stop_limit = min((uint32_t)kCandCap, max(2u * k_eff, 128u));
-    const uint32_t full = (prefix << width) | bin;
-    ctrl->bucket = bin;
-    if (n_stop <= stop_limit) {
-      ctrl->decision = kGather;
-      ctrl->thresh = full << shift;
-    } else if (level == 2) {
-      ctrl->decision = kExact;
-      ctrl->thresh = full;
-      ctrl->need = (int32_t)(R - above);
-    } else {
-      ctrl->decision = kContinue;
-      ctrl->prefix = full;
-      ctrl->remaining = (int32_t)(R - above);
+    sh->bucket = 4 * tid + b;
+    sh->above = above;
+    sh->inb = h[b];
+  }
+  __syncthreads();
+}
+
+// Keeps the k largest of cand[0, n) (n > k >= 1) in cand[0, k), by radix select over
+// the 64-bit composites (11-bit digits, most significant first). Returns the lower bound
+// of the kept set: every kept composite is >= it and every dropped one is below it.
+__device__ uint64_t select_top(uint64_t *cand, int n, int k, uint32_t *hist, Shared *sh) {
+  const int tid = threadIdx.x;
+  uint64_t prefix = 0;
+  int pbits = 0;
+  uint32_t R = (uint32_t)k;
+  for (;;) {
+    const int w = min(11, 64 - pbits);
+    const int shift = 64 - pbits - w;
+    const uint64_t dmask = (1ull << w) - 1ull;
+    for (int i = tid; i < kBins; i += kThreads) hist[i] = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += kThreads) {
+      const uint64_t c = cand[i];
+      if (pbits == 0 || (c >> (64 - pbits)) == prefix)
+        if (CHECK(((c >> shift) & dmask) < (uint64_t)kBins, 3, pbits, w))
+          atomicAdd(&hist[(uint32_t)((c >> shift) & dmask)], 1u);
+    }
+    __syncthreads();
+    find_bucket(hist, R, sh);
+    const uint32_t b = sh->bucket, above = sh->above, inb = sh->inb;
+    R -= above;
+    prefix = (prefix << w) | b;
+    pbits += w;
+    if (inb == R || pbits == 64) break;  // the bucket is taken whole
+  }
+  const uint64_t thr = pbits == 64 ? prefix : (prefix << (64 - pbits));
+  // Gather the kept composites into registers first, then rewrite the buffer.
+  constexpr int kPer = kCandCap / kThreads;
+  uint64_t held[kPer];
+  int nk = 0;
+#pragma unroll
+  for (int j = 0; j < kPer; j++) {
+    const int i = tid + j * kThreads;
+    held[j] = i < n ? cand[i] : 0ull;
+    nk += (i < n && held[j] >= thr) ? 1 : 0;
+  }
+  if (tid == 0) sh->count2 = 0;
+  __syncthreads();
+  const int lane = tid & 31;
+  int pos;
+  {
+    int incl = nk;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const int wtotal = __shfl_sync(0xffffffffu, incl, 31);
+    uint32_t wbase = 0;
+    if (lane == 31 && wtotal) wbase = atomicAdd(&sh->count2, (uint32_t)wtotal);
+    wbase = __shfl_sync(0xffffffffu, wbase, 31);
+    pos = (int)wbase + incl - nk;
+  }
+#pragma unroll
+  for (int j = 0; j < kPer; j++) {
+    const int i = tid + j * kThreads;
+    if (i < n && held[j] >= thr) {
+      if (CHECK(pos < kCandCap, 4, pos, n)) cand[pos] = held[j];
+      pos++;
     }
   }
   __syncthreads();
-  // Clear the merge area for the next level's histogram.
-  if (ctrl->decision == kContinue)
-    for (int i = tid; i < kBins; i += kThreads) merged[i] = 0;
+  return thr;
+}
+
+// Sorts a[0, n) descending, n <= 2 * blockDim.x, by a bitonic network held in registers
+// (two elements a thread): strides below 64 exchange through warp shuffles, larger ones
+// through shared memory.
+__device__ void block_sort_desc(uint64_t *a, int n) {
+  const int tid = threadIdx.x;
+  const int N = next_pow2(n);
+  const int j0 = 2 * tid, j1 = 2 * tid + 1;
+  uint64_t v0 = j0 < n ? a[j0] : 0ull;
+  uint64_t v1 = j1 < n ? a[j1] : 0ull;
+  for (int size = 2; size <= N; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      uint64_t p0, p1;
+      if (stride == 1) {
+        p0 = v1;
+        p1 = v0;
+      } else if (stride <= 32) {
+        p0 = __shfl_xor_sync(0xffffffffu, v0, stride >> 1);
+        p1 = __shfl_xor_sync(0xffffffffu, v1, stride >> 1);
+      } else {
+        __syncthreads();
+        if (j0 < N) {
+          a[j0] = v0;
+          a[j1] = v1;
+        }
+        __syncthreads();
+        p0 = j0 < N ? a[j0 ^ stride] : 0ull;
+        p1 = j1 < N ? a[j1 ^ stride] : 0ull;
+      }
+      const bool lower0 = (j0 & stride) == 0, desc0 = (j0 & size) == 0;
+      const bool lower1 = (j1 & stride) == 0, desc1 = (j1 & size) == 0;
+      v0 = (lower0 == desc0) ? (v0 > p0 ? v0 : p0) : (v0 < p0 ? v0 : p0);
+      v1 = (lower1 == desc1) ? (v1 > p1 ? v1 : p1) : (v1 < p1 ? v1 : p1);
+    }
+  }
+  __syncthreads();
+  if (j0 < n) a[j0] = v0;
+  if (j1 < n) a[j1] = v1;
+  __syncthreads();
 }
 
 // ------------------------------------------------------------------------------------
-// The row kernel.
+// sampleFromTopK on the device (sampler.ts:147-212).
+//
+// The exponentials and the divisions by the pool sums are per candidate, so all threads
+// compute them. The reference then makes three decisions from left-to-right float64
+// sums: the top-p cut, the drawn candidate and poolExhausted. Here those sums come from
+// a parallel tree / scan, whose results differ from the sequential ones by at most
+// (2n + 2*log2(n) + 3) * 2^-53 (n <= 1024 candidates, all terms positive, every sum
+// <= 1 + n * 2^-53). A decision is taken from the parallel sums only when its margin
+// exceeds 4x that bound; otherwise thread 0 replays the reference's sequential
+// arithmetic (decide_sequential). The token id, considered count and poolExhausted
+// therefore always equal the reference's; poolMass is the parallel sum unless the
+// replay ran (it stays within 1e-12 relative of the left-to-right value).
 // ------------------------------------------------------------------------------------
-struct RowArgs {
+__device__ void finalize_sample(const int32_t *ids, const float *vals, int n, float max_logit,
+                                float sum_exp, tabby_sampling_params p, double u, double *exact,
+                                double *scaled, double *cum, Shared *sh,
+                                tabby_sample_outcome *out, uint32_t status) {
+  const int tid = threadIdx.x;
+  if (status != TABBY_OK || n == 0) {
+    if (tid == 0) {
+      tabby_sample_outcome o;
+      o.id = -1;
+      o.considered_count = 0;
+      o.probability = 0.0;
+      o.pool_mass = 0.0;
+      o.pool_exhausted = 0;
+      o.pool_size = n;
+      o.max_logit = max_logit;
+      o.sum_exp = sum_exp;
+      o.status = status != TABBY_OK ? (int32_t)status : (int32_t)TABBY_EEMPTY;
+      o.reserved = 0;
+      *out = o;
+    }
+    return;
+  }
+  const bool sample = p.temperature > 0;
+  // Two consecutive candidates a thread (n <= 2 * blockDim.x).
+  const int i0 = 2 * tid, i1 = 2 * tid + 1;
+  double e0 = 0.0, e1 = 0.0, s0 = 0.0, s1 = 0.0;
+  if (i0 < n) {
+    e0 = exact_prob(vals[i0], max_logit, sum_exp);
+    exact[i0] = e0;
+    if (sample) s0 = scaled_weight(vals[i0], max_logit, p.temperature);
+    scaled[i0] = s0;
+  }
+  if (i1 < n) {
+    e1 = exact_prob(vals[i1], max_logit, sum_exp);
+    exact[i1] = e1;
+    if (sample) s1 = scaled_weight(vals[i1], max_logit, p.temperature);
+    scaled[i1] = s1;
+  }
+  const double pool_mass = block_sum_f64(JS_ADD(e0, e1), sh);
+  const double bound = 4.0 * (double)(2 * n + 2 * 11 + 3) * 1.1102230246251565e-16;
+
+  int32_t cut = 1, chosen = 0, exhausted = 0;
+  bool fallback = false;
+  if (sample) {
+    const double st = block_sum_f64(JS_ADD(s0, s1), sh);
+    const double w0 = i0 < n ? JS_DIV(s0, st) : 0.0;
+    const double w1 = i1 < n ? JS_DIV(s1, st) : 0.0;
+    const double before = block_exclusive_scan_f64(JS_ADD(w0, w1), sh);
+    const double c0 = JS_ADD(before, w0);
+    const double c1 = JS_ADD(c0, w1);
+    if (i0 < n) cum[i0] = c0;
+    if (i1 < n) cum[i1] = c1;
+    if (tid == 0) {
+      sh->cut_claim = n;
+      sh->chosen_claim = n;
+      sh->fallback = 0;
+    }
+    __syncthreads();
+    cut = n;
+    if (p.top_p < 1) {
+      // First i with cumulative >= top_p (sampler.ts:175-189).
+      if (i0 < n && c0 >= p.top_p)
+        atomicMin(&sh->cut_claim, i0);
+      else if (i1 < n && c1 >= p.top_p)
+        atomicMin(&sh->cut_claim, i1);
+      if (pool_mass < p.top_p) exhausted = 1;
+      __syncthreads();
+      const int ci = sh->cut_claim;
+      if (tid == 0) {
+        bool ok = fabs(pool_mass - p.top_p) > bound;
+        if (ci < n)
+          ok = ok && (cum[ci] - p.top_p > bound) && (ci == 0 || p.top_p - cum[ci - 1] > bound);
+        else
+          ok = ok && (p.top_p - cum[n - 1] > bound);
+        if (!ok) sh->fallback = 1;
+      }
+      cut = ci < n ? ci + 1 : n;
+    }
+    // target = u * total; first i < cut with target < cumulative (sampler.ts:191-203).
+    const double total = cum[cut - 1];
+    const double target = JS_MUL(u, total);
+    if (i0 < cut && target < c0)
+      atomicMin(&sh->chosen_claim, i0);
+    else if (i1 < cut && target < c1)
+      atomicMin(&sh->chosen_claim, i1);
+    __syncthreads();
+    const int ch = sh->chosen_claim;
+    if (tid == 0) {
+      bool ok = ch < cut;
+      if (ok)
+        ok = (cum[ch] - target > 2 * bound) && (ch == 0 || target - cum[ch - 1] > 2 * bound);
+      if (!ok) sh->fallback = 1;
+    }
+    __syncthreads();
+    chosen = ch < cut ? ch : cut - 1;
+    fallback = sh->fallback != 0;
+  }
+  if (tid == 0) {
+    tabby_sample_outcome o;
+    double pm = pool_mass;
+    if (fallback) {
+      // Exact replay of the reference's left-to-right float64 arithmetic.
+      const Decision d = decide_sequential(exact, scaled, cum, n, p.temperature, p.top_p, u);
+      chosen = d.chosen;
+      cut = d.cut;
+      exhausted = d.pool_exhausted;
+      pm = d.pool_mass;
+    }
+    o.id = ids[chosen];
+    o.considered_count = cut;
+    o.probability = exact[chosen];
+    o.pool_mass = pm;
+    o.pool_exhausted = exhausted;
+    o.pool_size = n;
+    o.max_logit = max_logit;
+    o.sum_exp = sum_exp;
+    o.status = TABBY_OK;
+    o.reserved = fallback ? 1 : 0;  // 1 when the sequential replay decided
+    *out = o;
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// The streaming kernel.
+// ------------------------------------------------------------------------------------
+struct StreamArgs {
   const float *logits;
   int64_t row_stride;
-  int32_t rows, vocab, slice, data_floats;
+  int32_t rows, vocab, slice, nslices;
   int32_t mode, cap, fixed_k;
   int64_t index_offset;
   const tabby_sampling_params *params;
@@ -338,291 +524,296 @@ struct RowArgs {
   int32_t topk_ld;
   float *block;
   int32_t block_ld;
+  uint32_t *row_count;
+  unsigned long long *row_tau;
+  float2 *slice_stats;
+  uint2 *slice_meta;
+  unsigned long long *slice_cand;
+  int32_t cand_ld;
 };
 
-// One pass over the staged slice: optional sum(exp(x - M)), optional digit histogram of
-// the keys inside `prefix`, optional gather of keys >= thresh into rank 0.
-template <bool kSum, bool kHist, bool kGather>
-__device__ float slice_pass(const float *data, int mis, int n, int lo, float row_max,
-                            uint32_t *hist, int level, uint32_t prefix, uint32_t thresh,
-                            uint32_t *r0_count, uint64_t *r0_cand) {
-  const int width = level == 2 ? 10 : 11;
-  const int shift = level == 0 ? 21 : (level == 1 ? 10 : 0);
-  const uint32_t dmask = (1u << width) - 1u;
-  const float4 *d4 = reinterpret_cast<const float4 *>(data);
-  const int G = (mis + n + 3) >> 2;
-  float s = 0.f;
-  for (int base = 0; base < G; base += kThreads) {
-    const int g = base + threadIdx.x;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (g < G) v = d4[g];
-    const float xs[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-      const int idx = 4 * g + e;
-      const bool valid = g < G && idx >= mis && idx < mis + n;
-      const float x = xs[e];
-      const uint32_t key = key_of(x);
-      if (kSum) {
-        if (valid) s += __expf(x - row_max);
-      }
-      if (kHist) {
-        if (valid && (key >> (shift + width)) == prefix)
-          atomicAdd(&hist[(key >> shift) & dmask], 1u);
-      }
-      if (kGather) {
-        push_candidate(valid && key >= thresh, key, (uint32_t)(lo + idx - mis), r0_count,
-                       r0_cand);
-      }
-    }
-  }
-  return s;
+__device__ __forceinline__ void insert_candidate(bool pred, uint64_t c, uint64_t *cand,
+                                                 uint32_t *count) {
+  const uint32_t mask = __ballot_sync(0xffffffffu, pred);
+  if (mask == 0) return;
+  const int lane = threadIdx.x & 31;
+  const int leader = __ffs(mask) - 1;
+  uint32_t base = 0;
+  if (lane == leader) base = atomicAdd(count, (uint32_t)__popc(mask));
+  base = __shfl_sync(0xffffffffu, base, leader);
+  const uint32_t slot = base + __popc(mask & ((1u << lane) - 1u));
+  if (pred && CHECK(slot < (uint32_t)kCandCap, 2, slot, base)) cand[slot] = c;
 }
 
-__global__ void __launch_bounds__(kThreads, 2) row_kernel(RowArgs a) {
+__global__ void __launch_bounds__(kThreads, 2) stream_kernel(StreamArgs a) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  float *data = reinterpret_cast<float *>(smem_raw);
-  uint32_t *hist = reinterpret_cast<uint32_t *>(smem_raw + (size_t)a.data_floats * 4);
-  uint64_t *cand = reinterpret_cast<uint64_t *>(hist + kBins);  // also the merged histogram
-  uint32_t *merged = reinterpret_cast<uint32_t *>(cand);
-  uint64_t *bars = cand + kCandCap;
-  RowCtrl *ctrl = reinterpret_cast<RowCtrl *>(bars + kChunks);
-  int *red = reinterpret_cast<int *>(ctrl + 1);
+  float *ring = reinterpret_cast<float *>(smem_raw);  // kRing stages of kStepElems logits
+  uint64_t *cand = reinterpret_cast<uint64_t *>(smem_raw + (size_t)kRingFloats * 4);
+  uint32_t *hist = reinterpret_cast<uint32_t *>(cand + kCandCap);
+  Shared *sh = reinterpret_cast<Shared *>(hist + kBins);
 
-  cg::cluster_group cluster = cg::this_cluster();
-  const uint32_t rank = cluster_ctarank();
-  const uint32_t csize = cluster_nctarank();
-  const int row = (int)cluster_id_x();
   const int tid = threadIdx.x;
-
-  RowCtrl *r0 = cluster.map_shared_rank(ctrl, 0);
-  uint32_t *r0_merged = cluster.map_shared_rank(merged, 0);
-  uint64_t *r0_cand = cluster.map_shared_rank(cand, 0);
-
+  const int row = blockIdx.x / a.nslices;
+  const int sl = blockIdx.x - row * a.nslices;
   const float *rowp = a.logits + (int64_t)row * a.row_stride;
-  const int lo = (int)rank * a.slice;
+  const int lo = sl * a.slice;
   const int hi = min(lo + a.slice, a.vocab);
-  const int n = max(hi - lo, 0);
-  const int mis = n > 0 ? (int)((reinterpret_cast<uintptr_t>(rowp + lo) >> 2) & 3) : 0;
+  // [a0, a1) is the 16-byte aligned middle of the slice, moved by TMA; the ragged ends
+  // (fewer than 4 logits each) come in through plain loads.
+  const int mis = (int)((reinterpret_cast<uintptr_t>(rowp + lo) >> 2) & 3);
   int a0 = lo + ((4 - mis) & 3);
   if (a0 > hi) a0 = hi;
-  const int a1 = a0 + ((hi - a0) & ~3);
-  const int ng = (a1 - a0) >> 2;  // 16-byte groups moved by TMA
-  const int gb0 = (a0 - lo + mis) >> 2;
+  const int a1 = a0 + ((max(hi - a0, 0)) & ~3);
+  const int ngroups = (a1 - a0) >> 2;  // float4 groups in the aligned middle
+  const int nsteps = (ngroups + kThreads - 1) / kThreads;
+  TRACE(0);
 
-  // ---- set-up: local state, mbarriers, then start the bulk copies at once ----
-  for (int i = tid; i < kBins; i += kThreads) hist[i] = 0;
-  if (rank == 0)
-    for (int i = tid; i < kBins; i += kThreads) merged[i] = 0;
+  // ---- set-up: start the first kRing-1 steps of the ring ----
   if (tid == 0) {
-    RowCtrl c = {};
-    c.max_key = 0;
-    c.decision = kContinue;
-    *ctrl = c;
-    for (int c2 = 0; c2 < kChunks; c2++) mbar_init(&bars[c2], 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    sh->count = 0;
+    sh->flags = 0;
   }
   __syncthreads();
-  if (tid == 0 && ng > 0) {
-    const uint64_t policy = evict_first_policy();
-    for (int c2 = 0; c2 < kChunks; c2++) {
-      const int g0 = (ng * c2) / kChunks, g1 = (ng * (c2 + 1)) / kChunks;
-      const uint32_t bytes = (uint32_t)(g1 - g0) * 16u;
-      mbar_expect_tx(&bars[c2], bytes);
-      if (bytes) bulk_copy_g2s(data + 4 * (gb0 + g0), rowp + a0 + 4 * g0, bytes, &bars[c2], policy);
-    }
+  // Step j's float4 group of thread t is group j*kThreads + t of the aligned middle and
+  // lands in stage j % kRing at the same position.
+  auto issue_step = [&](int jj) {
+    const int gg = jj * kThreads + tid;
+    if (jj < nsteps && gg < ngroups)
+      cp_async16(ring + (size_t)(jj % kRing) * kStepElems + 4 * tid, rowp + a0 + 4 * gg);
+    cp_async_commit();  // one group per step, empty or not, keeps the counting uniform
+  };
+#pragma unroll
+  for (int jj = 0; jj < kRing - 1; jj++) issue_step(jj);
+  // Pool size of this row.
+  int32_t k;
+  uint32_t pflags = 0;
+  if (a.mode == kModeSample) {
+    const tabby_sampling_params p = a.params[row];
+    k = pool_rule(p.temperature, p.top_k, a.cap);
+    if (isnan(p.temperature) || isnan(p.top_p)) pflags = kFlagBadParams;
+  } else {
+    k = a.fixed_k;
   }
-  // Every CTA of the cluster must be running before any DSMEM access: arrive now, wait
-  // just before the first remote operation.
-  cluster_arrive();
+  k = min(k, a.vocab);
+  TRACE(1);
 
-  // ---- pass A: max, bad-input check and level-0 histogram as chunks arrive ----
-  uint32_t kmax = 0;
-  bool bad = false;
-  // Ragged head/tail elements (fewer than 4 at each end) come in through plain loads.
-  if (tid < 8) {
+  // Per-thread online statistics: s = sum exp(x - m) as 2^((x - m) * log2(e)).
+  constexpr float kLog2e = 1.44269504088896341f;
+  float m = -3.40282347e38f, s = 0.f;
+  float mn = 3.40282347e38f;  // running min: catches -inf and the -3e38 sentinel
+  uint64_t tau = 0;  // accept composites >= tau (an exact lower bound of the row's k-th)
+  float tf = -__int_as_float(0x7f800000);  // value of tau's key: a cheap superset filter
+
+  // Ragged ends: at most 3 logits before a0 and 3 after a1, one per thread of warp 0.
+  if (tid < 32) {
     const int e = tid < 4 ? lo + tid : a1 + (tid - 4);
-    const bool in = tid < 4 ? (e < a0) : (e < hi);
+    const bool in = tid < 8 && (tid < 4 ? (e < a0) : (e < hi));
+    float x = 0.f;
     if (in) {
-      const float x = __ldg(rowp + e);
-      data[e - lo + mis] = x;
-      const uint32_t key = key_of(x);
-      kmax = max(kmax, key);
-      bad |= bad_logit(x);
-      atomicAdd(&hist[key >> 21], 1u);
+      x = __ldg(rowp + e);
+      m = x;
+      s = 1.f;
+      mn = x;
     }
+    insert_candidate(in && k > 0, composite(key_of(x), (uint32_t)e), cand, &sh->count);
   }
-  bool timed_out = false;
-  const float4 *d4 = reinterpret_cast<const float4 *>(data);
-  for (int c2 = 0; c2 < kChunks && ng > 0; c2++) {
-    if (!mbar_wait_bounded(&bars[c2], 0)) timed_out = true;
-    const int g0 = gb0 + (ng * c2) / kChunks, g1 = gb0 + (ng * (c2 + 1)) / kChunks;
-    for (int g = g0 + tid; g < g1; g += kThreads) {
-      const float4 v = d4[g];
+
+  // ---- one pass: online max / sum-exp and the threshold filter ----
+  const float4 *r4 = reinterpret_cast<const float4 *>(ring);
+  for (int j = 0; j < nsteps; j++) {
+    cp_async_wait<kRing - 2>();  // this thread's copies of step j have landed
+    __syncthreads();             // ... and every other thread's, and step j-1 is consumed
+    issue_step(j + kRing - 1);   // refills the stage step j-1 used
+    if (k > 0 && sh->count > (uint32_t)(kCandCap - kStepElems)) {
+      // Buffer nearly full: keep the k best and raise the threshold (block-uniform).
+      const uint64_t thr = select_top(cand, (int)sh->count, k, hist, sh);
+      if (tid == 0) {
+        sh->count = (uint32_t)k;
+        uint64_t t = thr;
+        if (a.nslices > 1) {
+          atomicMax(&a.row_tau[row], (unsigned long long)thr);
+          const uint64_t g = ld_cg_u64(&a.row_tau[row]);
+          t = thr > g ? thr : g;
+        }
+        sh->tau = t;
+      }
+      __syncthreads();
+      tau = sh->tau;
+      tf = float_of_key((uint32_t)(tau >> 32));
+    }
+    const int stage = j % kRing;
+    const int g = j * kThreads + tid;
+    const bool gin = g < ngroups;
+    float4 v = make_float4(-3.40282347e38f, -3.40282347e38f, -3.40282347e38f, -3.40282347e38f);
+    if (gin) v = r4[stage * kThreads + tid];
+    if (gin) {
+      const float gm = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+      mn = fminf(mn, fminf(fminf(v.x, v.y), fminf(v.z, v.w)));
+      if (gm > m) {
+        s *= ex2_approx((m - gm) * kLog2e);
+        m = gm;
+      }
+      s += ex2_approx((v.x - m) * kLog2e) + ex2_approx((v.y - m) * kLog2e) +
+           ex2_approx((v.z - m) * kLog2e) + ex2_approx((v.w - m) * kLog2e);
+    }
+    const bool hit = gin && k > 0 && (v.x >= tf || v.y >= tf || v.z >= tf || v.w >= tf);
+    if (__any_sync(0xffffffffu, hit)) {
+      // Rare path: exact composite test and insertion (every lane of the warp is here).
       const float xs[4] = {v.x, v.y, v.z, v.w};
+      const int base_idx = a0 + 4 * g;
 #pragma unroll
       for (int e = 0; e < 4; e++) {
-        const uint32_t key = key_of(xs[e]);
-        kmax = max(kmax, key);
-        bad |= bad_logit(xs[e]);
-        atomicAdd(&hist[key >> 21], 1u);
+        const uint64_t c = composite(key_of(xs[e]), (uint32_t)(base_idx + e));
+        insert_candidate(hit && c >= tau, c, cand, &sh->count);
       }
     }
   }
-  kmax = __reduce_max_sync(0xffffffffu, kmax);
-  const int any_bad = __syncthreads_or(bad ? 1 : 0);
-  const int any_timeout = __syncthreads_or(timed_out ? 1 : 0);
+  cp_async_wait<0>();
+  __syncthreads();
+  TRACE(2);
+  // NaN or +inf logits leave s or m non-finite; -inf and values at or below the
+  // reference's -3.0e38 sentinel show in the running min.
+  const bool bad = !(s == s) || !(m <= 3.40282347e38f) || !(mn > kNegSentinel) ||
+                   !(s <= 3.40282347e38f);
 
-  cluster_wait();  // peers are alive; rank 0's merge area is cleared
-
-  // ---- level loop: merge histograms in rank 0, decide, maybe refine ----
-  int level = 0;
-  float row_max = 0.f;
-  bool sum_done = false;
-  float my_sum = 0.f;
-  RowCtrl c;
-  for (;;) {
-    for (int i = tid; i < kBins; i += kThreads) {
-      const uint32_t v = hist[i];
-      if (v) atomicAdd(&r0_merged[i], v);
-    }
-    if (level == 0) {
-      if ((tid & 31) == 0) atomicMax(&r0->max_key, kmax);
-      if (tid == 0 && (any_bad || any_timeout))
-        atomicOr(&r0->flags, (any_bad ? kFlagBadInput : 0u) | (any_timeout ? kFlagTimeout : 0u));
-    }
-    cluster_sync_all();
-    if (rank == 0) {
-      if (level == 0) {
-        if (tid == 0) {
-          int32_t k;
-          if (a.mode == kModeSample) {
-            const tabby_sampling_params p = a.params[row];
-            k = pool_rule(p.temperature, p.top_k, a.cap);
-            if (isnan(p.temperature) || isnan(p.top_p)) ctrl->flags |= kFlagBadParams;
-          } else {
-            k = a.fixed_k;
-          }
-          k = min(k, a.vocab);
-          ctrl->k_eff = k;
-          ctrl->remaining = k;
-          ctrl->prefix = 0;
-          ctrl->row_max = float_of_key(ctrl->max_key);
-          if (k <= 0) ctrl->decision = kNone;
-        }
-        __syncthreads();
-      }
-      if (ctrl->decision != kNone) decide_level(ctrl, merged, level, red);
-      __syncthreads();
-    }
-    cluster_sync_all();
-    // Decision of this level; rank 0 writes no decision field again before the next
-    // cluster barrier. One thread fetches it over DSMEM for the whole CTA.
-    if (rank != 0 && tid == 0) *ctrl = *r0;
-    __syncthreads();
-    c = *ctrl;
-    if (level == 0) row_max = c.row_max;
-    if (c.decision != kContinue) break;
-    level++;
-    for (int i = tid; i < kBins; i += kThreads) hist[i] = 0;
-    __syncthreads();
-    if (!sum_done) {
-      my_sum = slice_pass<true, true, false>(data, mis, n, lo, row_max, hist, level, c.prefix, 0,
-                                             nullptr, nullptr);
-      sum_done = true;
-    } else {
-      slice_pass<false, true, false>(data, mis, n, lo, row_max, hist, level, c.prefix, 0, nullptr,
-                                     nullptr);
-    }
-    __syncthreads();
+  // ---- this slice's <= k best and its (max, sum-exp) partial ----
+  int cnt = (int)sh->count;
+  if (k > 0 && cnt > k) {
+    const uint64_t thr = select_top(cand, cnt, k, hist, sh);
+    if (tid == 0 && a.nslices > 1) atomicMax(&a.row_tau[row], (unsigned long long)thr);
+    cnt = k;
   }
-
-  // ---- final pass: gather candidates into rank 0 ----
-  uint32_t *r0_count = &r0->cand_count;
-  if (c.decision == kGather) {
-    if (!sum_done) {
-      my_sum = slice_pass<true, false, true>(data, mis, n, lo, row_max, hist, 0, 0, c.thresh,
-                                             r0_count, r0_cand);
-      sum_done = true;
-    } else {
-      slice_pass<false, false, true>(data, mis, n, lo, row_max, hist, 0, 0, c.thresh, r0_count,
-                                     r0_cand);
-    }
-  } else {
-    if (!sum_done) {
-      my_sum = slice_pass<true, false, false>(data, mis, n, lo, row_max, hist, 0, 0, 0, nullptr,
-                                              nullptr);
-      sum_done = true;
-    }
-    if (c.decision == kExact) {
-      // Keys above the tie key all go; of the keys equal to it, the `need` lowest
-      // indices go. CTAs cover ascending column ranges, so this CTA's first tie has rank
-      // (ties held by lower ranks).
-      int offset = 0;
-      for (uint32_t p = 0; p < rank; p++) offset += (int)*cluster.map_shared_rank(&hist[c.bucket], p);
-      const int G = (mis + n + 3) >> 2;
-      int running = 0;
-      for (int base = 0; base < G; base += kThreads) {
-        const int g = base + tid;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (g < G) v = d4[g];
-        const float xs[4] = {v.x, v.y, v.z, v.w};
-        int ties = 0;
-        bool is_tie[4], is_above[4];
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const int idx = 4 * g + e;
-          const bool valid = g < G && idx >= mis && idx < mis + n;
-          const uint32_t key = key_of(xs[e]);
-          is_tie[e] = valid && key == c.thresh;
-          is_above[e] = valid && key > c.thresh;
-          ties += is_tie[e] ? 1 : 0;
-        }
-        int tile_total;
-        const int before = block_exclusive_scan(ties, red, &tile_total);
-        int r = offset + running + before;
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const uint32_t idx = (uint32_t)(lo + 4 * g + e - mis);
-          const bool take_tie = is_tie[e] && r < c.need;
-          r += is_tie[e] ? 1 : 0;
-          push_candidate(is_above[e] || take_tie, key_of(xs[e]), idx, r0_count, r0_cand);
-        }
-        running += tile_total;
-      }
-    }
-  }
+  float M, S;
+  uint32_t flags;
   {
-    const float total = block_sum_f32(my_sum, reinterpret_cast<float *>(red));
-    if (tid == 0) r0->sums[rank] = total;
-  }
-  cluster_sync_all();  // every candidate and partial sum is in rank 0
-  if (rank != 0) return;
-
-  // ---- rank 0: sort the candidates, then the epilogue of the mode ----
-  const RowCtrl fin = *ctrl;
-  const int k = fin.k_eff;
-  int nc = (int)min(fin.cand_count, (uint32_t)kCandCap);
-  if (fin.decision == kNone) nc = 0;
-  double sum_d = 0.0;
-  for (uint32_t q = 0; q < csize; q++) sum_d += (double)fin.sums[q];
-  const float sum_exp = (float)sum_d;
-  const uint32_t status = (fin.flags & kFlagBadInput)    ? (uint32_t)TABBY_EINPUT
-                          : (fin.flags & kFlagBadParams) ? (uint32_t)TABBY_EINVAL
-                          : (fin.flags & kFlagTimeout)   ? (uint32_t)TABBY_ETIMEOUT
-                                                         : (uint32_t)TABBY_OK;
-  if (nc > 0) {
-    const int N = next_pow2(nc);
-    for (int i = nc + tid; i < N; i += kThreads) cand[i] = 0ull;
+    // Block merge of the per-thread online pairs, in a fixed order.
+    float bm = m;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+    if ((tid & 31) == 0) sh->red_f[tid >> 5] = bm;
     __syncthreads();
-    block_sort_desc(cand, N);
+    M = sh->red_f[0];
+    for (int i = 1; i < kWarps; i++) M = fmaxf(M, sh->red_f[i]);
+    float contrib = s > 0.f ? s * __expf(m - M) : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) contrib += __shfl_xor_sync(0xffffffffu, contrib, o);
+    const int any_bad = __syncthreads_or(bad ? 1 : 0);
+    if ((tid & 31) == 0) sh->red_f[tid >> 5] = contrib;
+    __syncthreads();
+    S = 0.f;
+    for (int i = 0; i < kWarps; i++) S += sh->red_f[i];
+    flags = pflags | (any_bad ? kFlagBadInput : 0u);
   }
-  const int kk = min(k, nc);
-  // Unpack the first kk candidates into (id, value); the finalize arrays reuse the
-  // (no longer needed) data region.
-  double *exact = reinterpret_cast<double *>(data);
+  TRACE(3);
+
+  int kk;
+  float sum_exp, row_max;
+  if (a.nslices == 1) {
+    // The whole row was this CTA's: no merge.
+    kk = cnt;
+    sum_exp = S;
+    row_max = M;
+  } else {
+    // Publish the slice, then count it in; the row's last slice merges them all.
+    const int64_t sidx = (int64_t)row * a.nslices + sl;
+    if (tid == 0) {
+      a.slice_stats[sidx] = make_float2(M, S);
+      a.slice_meta[sidx] = make_uint2((uint32_t)cnt, flags);
+    }
+    unsigned long long *dst = a.slice_cand + sidx * a.cand_ld;
+    for (int i = tid; i < cnt; i += kThreads) dst[i] = cand[i];
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const uint32_t done = atomicAdd(&a.row_count[row], 1u);
+      sh->last = done == (uint32_t)(a.nslices - 1);
+    }
+    __syncthreads();
+    if (!sh->last) return;
+    __threadfence();
+    TRACE(4);
+    // Statistics of every slice, loaded in parallel and merged in slice order.
+    const int64_t sbase = (int64_t)row * a.nslices;
+    float2 mine = make_float2(-3.40282347e38f, 0.f);
+    uint2 meta = make_uint2(0u, 0u);
+    if (tid < a.nslices) {
+      (void)CHECK(a.nslices <= kMaxSlices, 6, a.nslices, 0);
+      mine = __ldcg(&a.slice_stats[sbase + tid]);
+      meta = __ldcg(&a.slice_meta[sbase + tid]);
+    }
+    float wm = mine.x;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, o));
+    uint32_t wf = meta.y;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) wf |= __shfl_xor_sync(0xffffffffu, wf, o);
+    // a.nslices <= 32: warp 0 holds everything.
+    double part = (mine.y > 0.f) ? (double)mine.y * (double)__expf(mine.x - wm) : 0.0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    // Candidate offsets: exclusive scan of the slice counts.
+    int c = (int)meta.x, incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if ((tid & 31) >= o) incl += t;
+    }
+    if (tid < 32) {
+      sh->off[tid] = incl - c;
+      sh->cnt[tid] = c;
+    }
+    if (tid == 0) {
+      sh->merge_max = wm;
+      sh->merge_sum = (float)part;
+      sh->flags = wf;
+    }
+    __syncthreads();
+    flags = sh->flags;
+    row_max = sh->merge_max;
+    sum_exp = sh->merge_sum;
+    // Gather the slices' candidates, compacting whenever the buffer would overflow.
+    int total = 0;
+    int q0 = 0;
+    while (q0 < a.nslices) {
+      int q1 = q0, add = 0;
+      while (q1 < a.nslices && total + add + sh->cnt[q1] <= kCandCap) add += sh->cnt[q1++];
+      for (int q = q0; q < q1; q++) {
+        const unsigned long long *src = a.slice_cand + (sbase + q) * a.cand_ld;
+        const int base = total + sh->off[q] - sh->off[q0];
+        for (int i = tid; i < sh->cnt[q]; i += kThreads) cand[base + i] = ld_cg_u64(src + i);
+      }
+      total += add;
+      q0 = q1;
+      __syncthreads();
+      if (q0 < a.nslices && total > k) {
+        select_top(cand, total, k, hist, sh);
+        total = k;
+      }
+    }
+    if (k > 0 && total > k) {
+      select_top(cand, total, k, hist, sh);
+      total = k;
+    }
+    kk = min(k, total);
+    if (tid == 0) {
+      // Leave the row's counters clean for the next launch.
+      a.row_count[row] = 0;
+      a.row_tau[row] = 0;
+    }
+  }
+  TRACE(5);
+  block_sort_desc(cand, kk);
+  TRACE(6);
+
+  const uint32_t status = (flags & kFlagBadInput)    ? (uint32_t)TABBY_EINPUT
+                          : (flags & kFlagBadParams) ? (uint32_t)TABBY_EINVAL
+                          : (flags & kFlagTimeout)   ? (uint32_t)TABBY_ETIMEOUT
+                                                     : (uint32_t)TABBY_OK;
+  // Unpack into (id, value); the finalize arrays reuse the (drained) ring.
+  double *exact = reinterpret_cast<double *>(ring);
   double *scaled = exact + kk;
-  int32_t *ids = reinterpret_cast<int32_t *>(scaled + kk);
+  double *cum = scaled + kk;
+  int32_t *ids = reinterpret_cast<int32_t *>(cum + kk);
   float *vals = reinterpret_cast<float *>(ids + kk);
   for (int i = tid; i < kk; i += kThreads) {
     const uint64_t e = cand[i];
@@ -634,7 +825,7 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(RowArgs a) {
     vals[i] = v;
   }
   __syncthreads();
-  const float max_logit = kk > 0 ? vals[0] : fin.row_max;
+  const float max_logit = kk > 0 ? vals[0] : row_max;
 
   if (a.mode == kModeTopK || a.mode == kModeShard) {
     float *blk = a.block + (int64_t)row * a.block_ld;
@@ -653,45 +844,17 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(RowArgs a) {
       blk[2 + 2 * i] = v;
       blk[3 + 2 * i] = __uint_as_float(gi);
     }
+    TRACE(7);
     return;
   }
 
-  // kModeSample
   if (a.topk_ids)
     for (int i = tid; i < kk; i += kThreads) a.topk_ids[(int64_t)row * a.topk_ld + i] = ids[i];
   if (a.topk_values)
     for (int i = tid; i < kk; i += kThreads) a.topk_values[(int64_t)row * a.topk_ld + i] = vals[i];
-  const tabby_sampling_params p = a.params[row];
-  const double u = a.uniforms[row];
-  for (int i = tid; i < kk; i += kThreads) {
-    exact[i] = exact_prob(vals[i], max_logit, sum_exp);
-    scaled[i] = p.temperature > 0 ? scaled_weight(vals[i], max_logit, p.temperature) : 0.0;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    tabby_sample_outcome o;
-    o.pool_size = kk;
-    o.max_logit = max_logit;
-    o.sum_exp = sum_exp;
-    o.reserved = 0;
-    if (status != TABBY_OK || kk == 0) {
-      o.id = -1;
-      o.considered_count = 0;
-      o.probability = 0.0;
-      o.pool_mass = 0.0;
-      o.pool_exhausted = 0;
-      o.status = status != TABBY_OK ? (int32_t)status : (int32_t)TABBY_EEMPTY;
-    } else {
-      const Decision d = decide_sequential(exact, scaled, scaled, kk, p.temperature, p.top_p, u);
-      o.id = ids[d.chosen];
-      o.considered_count = d.cut;
-      o.probability = exact[d.chosen];
-      o.pool_mass = d.pool_mass;
-      o.pool_exhausted = d.pool_exhausted;
-      o.status = TABBY_OK;
-    }
-    a.out[row] = o;
-  }
+  finalize_sample(ids, vals, kk, max_logit, sum_exp, a.params[row], a.uniforms[row], exact,
+                  scaled, cum, sh, &a.out[row], status);
+  TRACE(7);
 }
 
 // ------------------------------------------------------------------------------------
@@ -699,58 +862,52 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(RowArgs a) {
 // ------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch a) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ Shared sh_s;
+  Shared *sh = &sh_s;
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
   const int total = a.shards * TABBY_SHARD_TOP_K;
-  const int N = next_pow2(total);
   uint64_t *cand = reinterpret_cast<uint64_t *>(smem_raw);
-  double *exact = reinterpret_cast<double *>(cand + N);
+  double *exact = reinterpret_cast<double *>(cand + 2 * kMergeThreads);
   double *scaled = exact + TABBY_SHARD_TOP_K;
-  int32_t *ids = reinterpret_cast<int32_t *>(scaled + TABBY_SHARD_TOP_K);
+  double *cum = scaled + TABBY_SHARD_TOP_K;
+  int32_t *ids = reinterpret_cast<int32_t *>(cum + TABBY_SHARD_TOP_K);
   float *vals = reinterpret_cast<float *>(ids + TABBY_SHARD_TOP_K);
-  __shared__ float s_max;
-  __shared__ float s_sum;
-  __shared__ int s_bad;
-  __shared__ int s_count;
+  const tabby_sampling_params p = a.params[row];
 
   if (tid == 0) {
     // M = max m_s; S = sum s_s * exp(m_s - M), shards in rank order.
-    float m = -3.40282347e38f;
-    int bad = 0;
+    float mx = -3.40282347e38f;
+    uint32_t bad = 0;
     for (int s = 0; s < a.shards; s++) {
       const float ms = a.gathered[((int64_t)s * a.rows + row) * a.block_ld];
-      if (ms != ms) bad = 1;
-      m = fmaxf(m, ms);
+      if (ms != ms) bad = kFlagBadInput;
+      mx = fmaxf(mx, ms);
     }
     double S = 0.0;
     for (int s = 0; s < a.shards; s++) {
       const float *b = a.gathered + ((int64_t)s * a.rows + row) * a.block_ld;
-      S = JS_ADD(S, JS_MUL((double)b[1], js_exp(JS_SUB((double)b[0], (double)m))));
+      if (b[1] > 0.f)
+        S = JS_ADD(S, JS_MUL((double)b[1], js_exp(JS_SUB((double)b[0], (double)mx))));
     }
-    s_max = m;
-    s_sum = (float)S;
-    const tabby_sampling_params p0 = a.params[row];
-    if (isnan(p0.temperature) || isnan(p0.top_p)) bad = 2;
-    s_bad = bad;
-    s_count = 0;
+    if (isnan(p.temperature) || isnan(p.top_p)) bad |= kFlagBadParams;
+    sh->merge_max = mx;
+    sh->merge_sum = (float)S;
+    sh->flags = bad;
+    sh->count = 0;
   }
   __syncthreads();
-  for (int i = tid; i < N; i += kMergeThreads) {
-    uint64_t e = 0;
-    if (i < total) {
-      const int s = i / TABBY_SHARD_TOP_K, j = i % TABBY_SHARD_TOP_K;
-      const float *b = a.gathered + ((int64_t)s * a.rows + row) * a.block_ld;
-      const uint32_t gi = __float_as_uint(b[3 + 2 * j]);
-      if (gi != 0xffffffffu) e = ((uint64_t)key_of(b[2 + 2 * j]) << 32) | (uint64_t)(~gi);
-      if (gi != 0xffffffffu) atomicAdd(&s_count, 1);
-    }
-    cand[i] = e;
+  for (int i = tid; i < total; i += kMergeThreads) {
+    const int s = i / TABBY_SHARD_TOP_K, j = i % TABBY_SHARD_TOP_K;
+    const float *b = a.gathered + ((int64_t)s * a.rows + row) * a.block_ld;
+    const uint32_t gi = __float_as_uint(b[3 + 2 * j]);
+    if (gi != 0xffffffffu) cand[atomicAdd(&sh->count, 1u)] = composite(key_of(b[2 + 2 * j]), gi);
   }
   __syncthreads();
-  block_sort_desc(cand, N);
-  const tabby_sampling_params p = a.params[row];
-  int k = pool_rule(p.temperature, p.top_k, TABBY_SHARD_TOP_K);
-  const int kk = min(k, s_count);
+  const int nc = (int)sh->count;
+  block_sort_desc(cand, nc);
+  const int k = pool_rule(p.temperature, p.top_k, TABBY_SHARD_TOP_K);
+  const int kk = min(k, nc);
   for (int i = tid; i < kk; i += kMergeThreads) {
     const uint64_t e = cand[i];
     const uint32_t key = (uint32_t)(e >> 32);
@@ -768,129 +925,71 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch a) {
     vals[i] = v;
   }
   __syncthreads();
-  const float max_logit = kk > 0 ? vals[0] : s_max;
-  const float sum_exp = s_sum;
+  const float max_logit = kk > 0 ? vals[0] : sh->merge_max;
+  const uint32_t flags = sh->flags;
+  const uint32_t status = (flags & kFlagBadInput)    ? (uint32_t)TABBY_EINPUT
+                          : (flags & kFlagBadParams) ? (uint32_t)TABBY_EINVAL
+                                                     : (uint32_t)TABBY_OK;
   if (a.topk_ids)
     for (int i = tid; i < kk; i += kMergeThreads) a.topk_ids[(int64_t)row * a.topk_ld + i] = ids[i];
   if (a.topk_values)
     for (int i = tid; i < kk; i += kMergeThreads)
       a.topk_values[(int64_t)row * a.topk_ld + i] = vals[i];
-  const double u = a.uniforms[row];
-  for (int i = tid; i < kk; i += kMergeThreads) {
-    exact[i] = exact_prob(vals[i], max_logit, sum_exp);
-    scaled[i] = p.temperature > 0 ? scaled_weight(vals[i], max_logit, p.temperature) : 0.0;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    tabby_sample_outcome o;
-    o.pool_size = kk;
-    o.max_logit = max_logit;
-    o.sum_exp = sum_exp;
-    o.reserved = 0;
-    if (s_bad || kk == 0) {
-      o.id = -1;
-      o.considered_count = 0;
-      o.probability = 0.0;
-      o.pool_mass = 0.0;
-      o.pool_exhausted = 0;
-      o.status = s_bad == 1 ? TABBY_EINPUT : s_bad == 2 ? TABBY_EINVAL : TABBY_EEMPTY;
-    } else {
-      const Decision d = decide_sequential(exact, scaled, scaled, kk, p.temperature, p.top_p, u);
-      o.id = ids[d.chosen];
-      o.considered_count = d.cut;
-      o.probability = exact[d.chosen];
-      o.pool_mass = d.pool_mass;
-      o.pool_exhausted = d.pool_exhausted;
-      o.status = TABBY_OK;
-    }
-    a.out[row] = o;
-  }
+  finalize_sample(ids, vals, kk, max_logit, sh->merge_sum, p, a.uniforms[row], exact, scaled, cum,
+                  sh, &a.out[row], status);
 }
 
 // ------------------------------------------------------------------------------------
 // Host side: geometry and launches.
 // ------------------------------------------------------------------------------------
-static size_t row_smem_bytes(int data_floats) {
-  return (size_t)data_floats * 4 + (size_t)kBins * 4 + (size_t)kCandCap * 8 +
-         (size_t)kChunks * 8 + sizeof(RowCtrl) + (size_t)kWarps * 4 + 64;
-}
-
 static int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
-cudaError_t plan_rows(int32_t sms, int32_t max_smem_optin, int32_t rows, int32_t vocab,
-                      int32_t cap, int32_t max_cluster, RowGeometry *geo) {
-  // Shared memory per CTA that still lets two CTAs share an SM (one streams its slice in
-  // while the other works on shared memory), and the hard per-CTA limit beyond that.
-  const size_t two_per_sm = 112 * 1024;
-  const size_t one_per_sm = (size_t)max_smem_optin;
-  const int finalize_floats = 6 * min(max(cap, (int32_t)TABBY_SHARD_TOP_K), vocab) + 16;
-  auto geometry = [&](int C) {
-    RowGeometry g;
-    g.cluster = C;
-    g.slice = round_up((vocab + C - 1) / C, 4);
-    g.data_floats = round_up(max(g.slice + 8, finalize_floats), 32);
-    g.smem_bytes = row_smem_bytes(g.data_floats);
-    return g;
-  };
-  if (max_cluster > kMaxCluster) max_cluster = kMaxCluster;
-  int C = 1;
-  while (C < max_cluster && geometry(C).smem_bytes > two_per_sm) C <<= 1;
-  if (geometry(C).smem_bytes > one_per_sm) return cudaErrorInvalidValue;
-  // Spread small batches over more SMs: aim for >= 2 CTAs per SM in flight, but keep
-  // at least ~4K logits per CTA.
-  while (C < max_cluster && (int64_t)rows * C < 2 * (int64_t)sms &&
-         geometry(2 * C).slice >= 4096)
-    C <<= 1;
-  *geo = geometry(C);
+static size_t stream_smem_bytes() {
+  return (size_t)kRingFloats * 4 + (size_t)kCandCap * 8 + (size_t)kBins * 4 +
+         sizeof(Shared) + 64;
+}
+
+int32_t max_slices(int32_t vocab, int32_t cap) {
+  (void)cap;
+  return std::max(1, std::min(kMaxSlices, (vocab + kMinSlice - 1) / kMinSlice));
+}
+
+cudaError_t plan_rows(int32_t sms, int32_t rows, int32_t vocab, int32_t cap, RowGeometry *geo) {
+  // One CTA streams a whole row when there are enough rows to fill two CTAs per SM;
+  // smaller batches split rows into up to 32 slices of >= kMinSlice logits, merged by
+  // the row's last slice. Two CTAs share an SM (shared memory ~107 KB each).
+  int S = (int)std::min<int64_t>(kMaxSlices, (2LL * sms) / std::max(rows, 1));
+  S = std::max(1, std::min(S, max_slices(vocab, cap)));
+  RowGeometry g;
+  g.slice = round_up((vocab + S - 1) / S, 4);
+  g.nslices = (vocab + g.slice - 1) / g.slice;
+  g.data_floats = kRingFloats;
+  g.smem_bytes = stream_smem_bytes();
+  *geo = g;
   return cudaSuccess;
 }
 
-// Raises the kernel's dynamic shared-memory limit once per process to the largest size
-// ever asked for, and allows clusters of 16 CTAs.
-static cudaError_t prepare_row_kernel(size_t smem_bytes) {
+static cudaError_t prepare_stream_kernel(size_t smem_bytes) {
   static size_t configured = 0;
-  static bool nonportable = false;
-  if (!nonportable) {
-    cudaError_t err =
-        cudaFuncSetAttribute(row_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (err != cudaSuccess) return err;
-    nonportable = true;
-  }
   if (smem_bytes > configured) {
     cudaError_t err = cudaFuncSetAttribute(
-        row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes);
+        stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes);
     if (err != cudaSuccess) return err;
     configured = smem_bytes;
   }
   return cudaSuccess;
 }
 
-cudaError_t max_active_clusters(const RowGeometry &geo, int *count) {
-  cudaError_t err = prepare_row_kernel(geo.smem_bytes);
-  if (err != cudaSuccess) return err;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)geo.cluster, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = geo.smem_bytes;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)geo.cluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaOccupancyMaxActiveClusters(count, row_kernel, &cfg);
-}
-
-cudaError_t launch_rows(const RowLaunch &l, const RowGeometry &geo, cudaStream_t stream) {
+cudaError_t launch_rows(const RowLaunch &l, const RowGeometry &geo, const Scratch &scr,
+                        cudaStream_t stream) {
   if (l.rows == 0) return cudaSuccess;
-  RowArgs a;
+  StreamArgs a;
   a.logits = l.logits;
   a.row_stride = l.row_stride;
   a.rows = l.rows;
   a.vocab = l.vocab;
   a.slice = geo.slice;
-  a.data_floats = geo.data_floats;
+  a.nslices = geo.nslices;
   a.mode = l.mode;
   a.cap = l.cap;
   a.fixed_k = l.fixed_k;
@@ -903,33 +1002,23 @@ cudaError_t launch_rows(const RowLaunch &l, const RowGeometry &geo, cudaStream_t
   a.topk_ld = l.topk_ld;
   a.block = l.block;
   a.block_ld = l.block_ld;
-
-  cudaError_t err = prepare_row_kernel(geo.smem_bytes);
+  a.row_count = scr.row_count;
+  a.row_tau = scr.row_tau;
+  a.slice_stats = scr.slice_stats;
+  a.slice_meta = scr.slice_meta;
+  a.slice_cand = scr.slice_cand;
+  a.cand_ld = scr.cand_ld;
+  cudaError_t err = prepare_stream_kernel(geo.smem_bytes);
   if (err != cudaSuccess) return err;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(l.rows * geo.cluster), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = geo.smem_bytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)geo.cluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, row_kernel, a);
+  const unsigned grid = (unsigned)((int64_t)l.rows * geo.nslices);
+  stream_kernel<<<grid, kThreads, geo.smem_bytes, stream>>>(a);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_merge(const MergeLaunch &l, cudaStream_t stream) {
   if (l.rows == 0) return cudaSuccess;
-  const int total = l.shards * TABBY_SHARD_TOP_K;
-  int N = 2;
-  while (N < total) N <<= 1;
-  const size_t smem = (size_t)N * 8 + (size_t)TABBY_SHARD_TOP_K * (8 + 8 + 4 + 4);
-  cudaError_t err =
-      cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (err != cudaSuccess) return err;
+  const size_t smem =
+      (size_t)2 * kMergeThreads * 8 + (size_t)TABBY_SHARD_TOP_K * (3 * 8 + 4 + 4);
   merge_kernel<<<l.rows, kMergeThreads, smem, stream>>>(l);
   return cudaGetLastError();
 }
@@ -961,3 +1050,16 @@ int host_sample_from_topk(const int32_t *ids, const float *logits, int32_t n, fl
 }
 
 }  // namespace tabby
+
+#ifdef TABBY_TRACE
+extern "C" __attribute__((visibility("default"))) int tabby_debug_trace(unsigned long long *host,
+                                                                        int n) {
+  return (int)cudaMemcpyFromSymbol(host, tabby::g_trace, (size_t)n * 8);
+}
+#endif
+
+#ifdef TABBY_CHECKS
+extern "C" __attribute__((visibility("default"))) int tabby_debug_checks(unsigned long long *host) {
+  return (int)cudaMemcpyFromSymbol(host, tabby::g_check, sizeof(unsigned long long) * 4);
+}
+#endif

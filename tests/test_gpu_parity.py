@@ -88,7 +88,8 @@ def assert_parity(oracle, x, params, u, cap, got, check_finalize=True):
             assert fo["id"] == int(o["id"])
             assert fo["consideredCount"] == int(o["considered_count"])
             assert fo["probability"] == float(o["probability"])
-            assert fo["poolMass"] == float(o["pool_mass"])
+            # poolMass comes from a parallel float64 sum unless the sequential replay ran.
+            assert abs(fo["poolMass"] - float(o["pool_mass"])) <= 1e-12 * fo["poolMass"]
             assert fo["poolExhausted"] == bool(o["pool_exhausted"])
 
 
