@@ -174,6 +174,32 @@ TABBY_API int tabby_sample_from_topk(const int32_t *ids, const float *logits, in
                            float sum_exp, const tabby_sampling_params *params, double uniform,
                            tabby_sample_outcome *out);
 
+/* Largest max_top_k tabby_sample_rows_noalloc accepts (its scratch array is fixed). */
+#define TABBY_NOALLOC_MAX_TOP_K 256
+
+/*
+ * tabby_sample_rows_async without a sampler handle and without any device allocation.
+ * No counterpart in the reference: it exists for callers that cannot call cudaMalloc
+ * (code running under an allocator that owns all device memory, plug-in hosts that
+ * forbid allocation on their request path, callers that must not add allocations
+ * between steps). The row kernel's global scratch -- per-row counters and per-slice
+ * candidate lists, about 2 MB -- lives in a file-scope __device__ array that every GPU
+ * loading the library keeps until the process exits. Same inputs, outputs and results
+ * as tabby_sample_rows_async with max_top_k as the pool cap; max_top_k must be
+ * 1..TABBY_NOALLOC_MAX_TOP_K, larger values are rejected with TABBY_EINVAL.
+ * Runs on the current device. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress): make that first call before any stream capture.
+ * All calls on a device share the one array (each call first clears the counters it
+ * needs at zero), so calls that overlap on the GPU -- concurrent streams or threads --
+ * race and must be serialised by the caller.
+ */
+TABBY_API int tabby_sample_rows_noalloc(const float *d_logits, int64_t row_stride, int32_t rows,
+                                        int32_t vocab, int32_t max_top_k,
+                                        const tabby_sampling_params *d_params,
+                                        const double *d_uniforms, tabby_sample_outcome *d_out,
+                                        int32_t *d_topk_ids, float *d_topk_values,
+                                        int32_t topk_ld, void *stream);
+
 /* Pool-size rule of the worker (inference.worker.ts:120-123) with the handle's cap. */
 TABBY_API int32_t tabby_pool_size(double temperature, int32_t top_k, int32_t max_top_k);
 

@@ -23,6 +23,7 @@ TABBY_EEMPTY = 6
 TABBY_MAX_TOP_K_LIMIT = 1024
 TABBY_DEFAULT_MAX_TOP_K = 64
 TABBY_SHARD_TOP_K = 64
+TABBY_NOALLOC_MAX_TOP_K = 256
 SHARD_BLOCK_WORDS = 2 + 2 * TABBY_SHARD_TOP_K
 
 # tabby_sampling_params (24 bytes) and tabby_sample_outcome (48 bytes).
@@ -75,6 +76,8 @@ SIGNATURES = {
     "tabby_shard_merge_async": (
         [_P, _P, _I32, _I32, _I32, _P, _P, _P, _P, _P, _I32, _P], ctypes.c_int),
     "tabby_sample_from_topk": ([_P, _P, _I32, _F32, _F32, _P, _F64, _P], ctypes.c_int),
+    "tabby_sample_rows_noalloc": (
+        [_P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _P, _I32, _P], ctypes.c_int),
 }
 
 _lib = None

@@ -121,6 +121,8 @@ int check_vocab_capacity(const tabby_sampler *s, int32_t vocab) {
 
 }  // namespace
 
+int tabby::set_error(int status, const char *msg) { return fail(status, "%s", msg); }
+
 extern "C" {
 
 int32_t tabby_abi_version(void) { return TABBY_ABI_VERSION; }

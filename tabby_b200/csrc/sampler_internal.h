@@ -75,6 +75,9 @@ cudaError_t launch_rows(const RowLaunch &a, const RowGeometry &geo, const Scratc
                         cudaStream_t stream);
 cudaError_t launch_merge(const MergeLaunch &a, cudaStream_t stream);
 
+// Records `msg` as the calling thread's tabby_last_error() and returns `status`.
+int set_error(int status, const char *msg);
+
 // Host float64 finalize with the device's arithmetic (sampler.ts:147-212).
 int host_sample_from_topk(const int32_t *ids, const float *logits, int32_t n, float max_logit,
                           float sum_exp, double temperature, double top_p, double u,
