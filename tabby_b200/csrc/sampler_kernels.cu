@@ -6,9 +6,9 @@
 // from HBM once, in one streaming pass:
 //
 //   stream_kernel  one CTA per (row, slice); a slice is the whole row when the batch
-//                  fills the GPU. The slice streams through an 8-stage shared-memory ring
-//                  (2K logits a stage, 16-byte cp.async copies kept 7 stages ahead) and
-//                  is consumed step by step as it lands: online max and
+//                  fills the GPU. Every thread streams its own float4 groups straight
+//                  into registers (four 16-byte loads in flight a thread, 8K logits an
+//                  iteration per CTA, one barrier an iteration): online max and
 //                  sum(exp(x - max)) per thread, and a filter that keeps only logits
 //                  whose 64-bit composite (order-preserving key, inverted index) reaches
 //                  the current threshold. The threshold is an exact lower bound on the
@@ -37,10 +37,9 @@ namespace tabby {
 
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
-constexpr int kStepElems = kThreads * 4;  // logits consumed per step (one float4 a thread)
-constexpr int kRing = 8;                  // TMA ring stages of kStepElems logits (64 KB)
-constexpr int kRingFloats = kRing * kStepElems;
-constexpr int kCandCap = 4096;            // candidate buffer (composites) per CTA
+constexpr int kVec = 4;                   // float4 loads in flight per thread per iteration
+constexpr int kIterGroups = kThreads * kVec;  // float4 groups per iteration (8K logits)
+constexpr int kCandCap = 8192;            // candidate buffer (composites) per CTA
 constexpr int kBins = 2048;               // radix digit: 11 bits
 constexpr int kMaxSlices = 32;            // slices of one row (one warp merges their stats)
 constexpr int kMinSlice = 8192;           // logits: below this a row is not split further
@@ -139,9 +138,8 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 // 2^x by the MUFU.EX2 approximation (flush-to-zero).
@@ -182,12 +180,15 @@ struct Shared {
   int32_t chosen_claim;
   int32_t fallback;
   uint32_t flags;
+  uint32_t overflow;  // an insert found the candidate buffer full
+  uint32_t snap;      // candidate count at the start of the current iteration
   uint64_t tau;  // accept composites >= tau
   float red_f[kWarps];
   uint32_t red_u[kWarps];
   double red_d[kWarps];
   float merge_max;
   float merge_sum;
+  uint64_t samp[64];  // sorted sample of the candidate buffer
   int32_t off[32];  // merge: first candidate of each slice
   int32_t cnt[32];  // merge: candidates of each slice
 };
@@ -263,25 +264,37 @@ __device__ void find_bucket(const uint32_t *hist, uint32_t R, Shared *sh) {
   __syncthreads();
 }
 
-// Keeps the k largest of cand[0, n) (n > k >= 1) in cand[0, k), by radix select over
-// the 64-bit composites (11-bit digits, most significant first). Returns the lower bound
-// of the kept set: every kept composite is >= it and every dropped one is below it.
-__device__ uint64_t select_top(uint64_t *cand, int n, int k, uint32_t *hist, Shared *sh) {
+// Keeps the k largest of cand[0, n) (n > k >= 1, k <= 1024) in cand[0, k), by radix
+// select over the 64-bit composites (11-bit digits, most significant first). Histogram
+// increments are aggregated per warp over equal digits (__match_any_sync), so runs of equal
+// logits do not serialise on one counter. Returns the lower bound of the kept set: every
+// kept composite is >= it and every dropped one is below it.
+__device__ __noinline__ uint64_t select_top(uint64_t *cand, int n, int k, uint32_t *hist, Shared *sh) {
   const int tid = threadIdx.x;
+  const int lane = tid & 31;
   uint64_t prefix = 0;
   int pbits = 0;
   uint32_t R = (uint32_t)k;
+  const int nround = (n + kThreads - 1) / kThreads * kThreads;  // warp-uniform trip count
   for (;;) {
     const int w = min(11, 64 - pbits);
     const int shift = 64 - pbits - w;
     const uint64_t dmask = (1ull << w) - 1ull;
     for (int i = tid; i < kBins; i += kThreads) hist[i] = 0;
     __syncthreads();
-    for (int i = tid; i < n; i += kThreads) {
-      const uint64_t c = cand[i];
-      if (pbits == 0 || (c >> (64 - pbits)) == prefix)
-        if (CHECK(((c >> shift) & dmask) < (uint64_t)kBins, 3, pbits, w))
-          atomicAdd(&hist[(uint32_t)((c >> shift) & dmask)], 1u);
+    for (int i = tid; i < nround; i += kThreads) {
+      bool in = false;
+      uint32_t digit = 0;
+      if (i < n) {
+        const uint64_t c = cand[i];
+        in = pbits == 0 || (c >> (64 - pbits)) == prefix;
+        digit = (uint32_t)((c >> shift) & dmask);
+      }
+      const uint32_t act = __ballot_sync(0xffffffffu, in);
+      if (in) {
+        const uint32_t peers = __match_any_sync(act, digit);
+        if (lane == __ffs(peers) - 1) atomicAdd(&hist[digit], (uint32_t)__popc(peers));
+      }
     }
     __syncthreads();
     find_bucket(hist, R, sh);
@@ -292,55 +305,63 @@ __device__ uint64_t select_top(uint64_t *cand, int n, int k, uint32_t *hist, Sha
     if (inb == R || pbits == 64) break;  // the bucket is taken whole
   }
   const uint64_t thr = pbits == 64 ? prefix : (prefix << (64 - pbits));
-  // Gather the kept composites into registers first, then rewrite the buffer.
-  constexpr int kPer = kCandCap / kThreads;
-  uint64_t held[kPer];
-  int nk = 0;
-#pragma unroll
-  for (int j = 0; j < kPer; j++) {
-    const int i = tid + j * kThreads;
-    held[j] = i < n ? cand[i] : 0ull;
-    nk += (i < n && held[j] >= thr) ? 1 : 0;
-  }
+  // Exactly k composites are >= thr: collect them in the histogram space (1024 slots),
+  // then copy them to the front of the buffer.
+  uint64_t *tmp = reinterpret_cast<uint64_t *>(hist);
   if (tid == 0) sh->count2 = 0;
   __syncthreads();
-  const int lane = tid & 31;
-  int pos;
-  {
-    int incl = nk;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    const int wtotal = __shfl_sync(0xffffffffu, incl, 31);
-    uint32_t wbase = 0;
-    if (lane == 31 && wtotal) wbase = atomicAdd(&sh->count2, (uint32_t)wtotal);
-    wbase = __shfl_sync(0xffffffffu, wbase, 31);
-    pos = (int)wbase + incl - nk;
-  }
-#pragma unroll
-  for (int j = 0; j < kPer; j++) {
-    const int i = tid + j * kThreads;
-    if (i < n && held[j] >= thr) {
-      if (CHECK(pos < kCandCap, 4, pos, n)) cand[pos] = held[j];
-      pos++;
+  for (int i = tid; i < nround; i += kThreads) {
+    const uint64_t c = i < n ? cand[i] : 0ull;
+    const bool keep = i < n && c >= thr;
+    const uint32_t mask = __ballot_sync(0xffffffffu, keep);
+    if (mask) {
+      const int leader = __ffs(mask) - 1;
+      uint32_t base = 0;
+      if (lane == leader) base = atomicAdd(&sh->count2, (uint32_t)__popc(mask));
+      base = __shfl_sync(0xffffffffu, base, leader);
+      const uint32_t slot = base + __popc(mask & ((1u << lane) - 1u));
+      if (keep && CHECK(slot < (uint32_t)(kBins / 2), 4, slot, n)) tmp[slot] = c;
     }
   }
+  __syncthreads();
+  for (int i = tid; i < k; i += kThreads) cand[i] = tmp[i];
   __syncthreads();
   return thr;
 }
 
-// Sorts a[0, n) descending, n <= 2 * blockDim.x, by a bitonic network held in registers
-// (two elements a thread): strides below 64 exchange through warp shuffles, larger ones
-// through shared memory.
-__device__ void block_sort_desc(uint64_t *a, int n) {
-  const int tid = threadIdx.x;
-  const int N = next_pow2(n);
-  const int j0 = 2 * tid, j1 = 2 * tid + 1;
-  uint64_t v0 = j0 < n ? a[j0] : 0ull;
-  uint64_t v1 = j1 < n ? a[j1] : 0ull;
+// Bitonic sort of 64 values held two per lane (lane l holds elements 2l, 2l+1), descending.
+__device__ __forceinline__ void warp_sort64_desc(uint64_t &v0, uint64_t &v1) {
+  const int lane = threadIdx.x & 31;
+  const int j0 = 2 * lane, j1 = j0 + 1;
+#pragma unroll
+  for (int size = 2; size <= 64; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      uint64_t p0, p1;
+      if (stride == 1) {
+        p0 = v1;
+        p1 = v0;
+      } else {
+        p0 = __shfl_xor_sync(0xffffffffu, v0, stride >> 1);
+        p1 = __shfl_xor_sync(0xffffffffu, v1, stride >> 1);
+      }
+      const bool lower0 = (j0 & stride) == 0, desc0 = (j0 & size) == 0;
+      const bool lower1 = (j1 & stride) == 0, desc1 = (j1 & size) == 0;
+      v0 = (lower0 == desc0) ? (v0 > p0 ? v0 : p0) : (v0 < p0 ? v0 : p0);
+      v1 = (lower1 == desc1) ? (v1 > p1 ? v1 : p1) : (v1 < p1 ? v1 : p1);
+    }
+  }
+}
+
+// Bitonic network for N (a power of two, 128..1024) values held two per thread of a
+// 512-thread block (elements 2t, 2t+1), descending. Fully unrolled: strides up to 32
+// exchange through warp shuffles, larger ones through shared memory `a`.
+template <int N>
+__device__ __forceinline__ void sort_pow2_desc(uint64_t *a, uint64_t &v0, uint64_t &v1) {
+  const int j0 = 2 * threadIdx.x, j1 = j0 + 1;
+#pragma unroll
   for (int size = 2; size <= N; size <<= 1) {
+#pragma unroll
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
       uint64_t p0, p1;
       if (stride == 1) {
@@ -365,10 +386,174 @@ __device__ void block_sort_desc(uint64_t *a, int n) {
       v1 = (lower1 == desc1) ? (v1 > p1 ? v1 : p1) : (v1 < p1 ? v1 : p1);
     }
   }
+}
+
+// Sorts a[0, n) descending, n <= 1024 (block-uniform call, 512 threads): one warp for
+// n <= 64, otherwise the smallest unrolled network that holds n.
+__device__ __noinline__ void block_sort_desc(uint64_t *a, int n) {
+  const int tid = threadIdx.x;
+  if (n <= 1) {
+    __syncthreads();
+    return;
+  }
+  if (n <= 64) {
+    if (tid < 32) {
+      uint64_t v0 = 2 * tid < n ? a[2 * tid] : 0ull;
+      uint64_t v1 = 2 * tid + 1 < n ? a[2 * tid + 1] : 0ull;
+      warp_sort64_desc(v0, v1);
+      if (2 * tid < n) a[2 * tid] = v0;
+      if (2 * tid + 1 < n) a[2 * tid + 1] = v1;
+    }
+    __syncthreads();
+    return;
+  }
+  const int j0 = 2 * tid, j1 = j0 + 1;
+  uint64_t v0 = j0 < n ? a[j0] : 0ull;
+  uint64_t v1 = j1 < n ? a[j1] : 0ull;
+  if (n <= 128)
+    sort_pow2_desc<128>(a, v0, v1);
+  else if (n <= 256)
+    sort_pow2_desc<256>(a, v0, v1);
+  else if (n <= 512)
+    sort_pow2_desc<512>(a, v0, v1);
+  else
+    sort_pow2_desc<1024>(a, v0, v1);
   __syncthreads();
   if (j0 < n) a[j0] = v0;
   if (j1 < n) a[j1] = v1;
   __syncthreads();
+}
+
+// 2048-element variant: four values a thread (elements 4t..4t+3), unrolled.
+__device__ __forceinline__ void sort2048_desc(uint64_t *a, uint64_t (&v)[4]) {
+  const int jb = 4 * threadIdx.x;
+#pragma unroll
+  for (int size = 2; size <= 2048; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      uint64_t p[4];
+      if (stride <= 2) {
+#pragma unroll
+        for (int e = 0; e < 4; e++) p[e] = v[e ^ stride];
+      } else if (stride <= 64) {
+#pragma unroll
+        for (int e = 0; e < 4; e++) p[e] = __shfl_xor_sync(0xffffffffu, v[e], stride >> 2);
+      } else {
+        __syncthreads();
+#pragma unroll
+        for (int e = 0; e < 4; e++) a[jb + e] = v[e];
+        __syncthreads();
+#pragma unroll
+        for (int e = 0; e < 4; e++) p[e] = a[(jb + e) ^ stride];
+      }
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int j = jb + e;
+        const bool lower = (j & stride) == 0, desc = (j & size) == 0;
+        v[e] = (lower == desc) ? (v[e] > p[e] ? v[e] : p[e]) : (v[e] < p[e] ? v[e] : p[e]);
+      }
+    }
+  }
+}
+
+// Sorts a[0, n) descending for n <= 2048 (block-uniform call).
+__device__ __noinline__ void block_sort_desc_2k(uint64_t *a, int n) {
+  if (n <= 1024) {
+    block_sort_desc(a, n);
+    return;
+  }
+  const int jb = 4 * threadIdx.x;
+  uint64_t v[4];
+#pragma unroll
+  for (int e = 0; e < 4; e++) v[e] = jb + e < n ? a[jb + e] : 0ull;
+  sort2048_desc(a, v);
+  __syncthreads();
+#pragma unroll
+  for (int e = 0; e < 4; e++)
+    if (jb + e < n) a[jb + e] = v[e];
+  __syncthreads();
+}
+
+// Number of composites >= t in cand[0, n), the same in every thread.
+__device__ __noinline__ int block_count_ge(const uint64_t *cand, int n, uint64_t t, Shared *sh) {
+  int c = 0;
+  for (int i = threadIdx.x; i < n; i += kThreads) c += cand[i] >= t ? 1 : 0;
+  c = __reduce_add_sync(0xffffffffu, c);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh->red_u[threadIdx.x >> 5] = (uint32_t)c;
+  __syncthreads();
+  int total = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; w++) total += (int)sh->red_u[w];
+  return total;
+}
+
+// Keeps the composites >= t of cand[0, n) at the front, in order, in place: chunk by chunk
+// every thread reads its element, a block scan gives the new positions (never past the
+// chunk being read), then the kept elements are written. Returns how many were kept.
+__device__ __noinline__ int block_keep_ge(uint64_t *cand, int n, uint64_t t, Shared *sh) {
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  int out = 0;
+  for (int base = 0; base < n; base += kThreads) {
+    const int i = base + tid;
+    const uint64_t c = i < n ? cand[i] : 0ull;
+    const bool keep = i < n && c >= t;
+    const uint32_t mask = __ballot_sync(0xffffffffu, keep);
+    __syncthreads();  // everyone has read this chunk (and the previous red_u is consumed)
+    if (lane == 0) sh->red_u[w] = (uint32_t)__popc(mask);
+    __syncthreads();
+    int before = 0, all = 0;
+#pragma unroll
+    for (int q = 0; q < kWarps; q++) {
+      const int cq = (int)sh->red_u[q];
+      before += q < w ? cq : 0;
+      all += cq;
+    }
+    if (keep) cand[out + before + __popc(mask & ((1u << lane) - 1u))] = c;
+    out += all;
+  }
+  __syncthreads();
+  return out;
+}
+
+// Shrinks cand[0, n) (n > limit >= k) to between k and `limit` composites that include its
+// k largest. A sorted sample of 64 candidates proposes actual candidates as thresholds; a
+// block count accepts one or moves the sample rank. Returns the threshold (a valid lower
+// bound of the k-th largest: at least k composites are >= it); falls back to the exact
+// radix select when no sampled rank fits.
+__device__ __noinline__ uint64_t shrink_to(uint64_t *cand, int n, int k, int limit, uint32_t *hist,
+                              Shared *sh, int *kept) {
+  const int tid = threadIdx.x;
+  if (tid < 32) {
+    uint64_t v0 = cand[(int)(((int64_t)(2 * tid) * n) >> 6)];
+    uint64_t v1 = cand[(int)(((int64_t)(2 * tid + 1) * n) >> 6)];
+    warp_sort64_desc(v0, v1);
+    sh->samp[2 * tid] = v0;
+    sh->samp[2 * tid + 1] = v1;
+  }
+  __syncthreads();
+  // Sample rank r stands for about (r + 1) * n / 64 candidates; aim between k and limit.
+  const int target = (k + limit) / 2;
+  int r = (int)(((int64_t)target * 64) / n) - 1;
+  r = min(max(r, 0), 63);
+  for (int round = 0; round < 6; round++) {
+    const uint64_t t = sh->samp[r];
+    const int c = block_count_ge(cand, n, t, sh);
+    if (c >= k && c <= limit) {
+      *kept = block_keep_ge(cand, n, t, sh);
+      return t;
+    }
+    if (c < k) {
+      if (r == 63) break;
+      r = min(63, r + max(1, (int)(((int64_t)(k - c) * 64 + n - 1) / n)));
+    } else {
+      if (r == 0) break;
+      r = max(0, r - max(1, (int)(((int64_t)(c - limit) * 64 + n - 1) / n)));
+    }
+  }
+  const uint64_t thr = select_top(cand, n, k, hist, sh);
+  *kept = k;
+  return thr;
 }
 
 // ------------------------------------------------------------------------------------
@@ -385,7 +570,7 @@ __device__ void block_sort_desc(uint64_t *a, int n) {
 // therefore always equal the reference's; poolMass is the parallel sum unless the
 // replay ran (it stays within 1e-12 relative of the left-to-right value).
 // ------------------------------------------------------------------------------------
-__device__ void finalize_sample(const int32_t *ids, const float *vals, int n, float max_logit,
+__device__ __noinline__ void finalize_sample(const int32_t *ids, const float *vals, int n, float max_logit,
                                 float sum_exp, tabby_sampling_params p, double u, double *exact,
                                 double *scaled, double *cum, Shared *sh,
                                 tabby_sample_outcome *out, uint32_t status) {
@@ -532,8 +717,10 @@ struct StreamArgs {
   int32_t cand_ld;
 };
 
+// Appends c to the candidate buffer when pred holds (warp-uniform call). Slots past
+// kCandCap are not written; the overflow flag tells the block to redo the iteration.
 __device__ __forceinline__ void insert_candidate(bool pred, uint64_t c, uint64_t *cand,
-                                                 uint32_t *count) {
+                                                 uint32_t *count, uint32_t *overflow) {
   const uint32_t mask = __ballot_sync(0xffffffffu, pred);
   if (mask == 0) return;
   const int lane = threadIdx.x & 31;
@@ -542,15 +729,23 @@ __device__ __forceinline__ void insert_candidate(bool pred, uint64_t c, uint64_t
   if (lane == leader) base = atomicAdd(count, (uint32_t)__popc(mask));
   base = __shfl_sync(0xffffffffu, base, leader);
   const uint32_t slot = base + __popc(mask & ((1u << lane) - 1u));
-  if (pred && CHECK(slot < (uint32_t)kCandCap, 2, slot, base)) cand[slot] = c;
+  if (pred) {
+    if (slot < (uint32_t)kCandCap)
+      cand[slot] = c;
+    else
+      *overflow = 1u;
+  }
 }
 
-__global__ void __launch_bounds__(kThreads, 2) stream_kernel(StreamArgs a) {
+#ifndef TABBY_MIN_BLOCKS
+#define TABBY_MIN_BLOCKS 2
+#endif
+__global__ void __launch_bounds__(kThreads, TABBY_MIN_BLOCKS) stream_kernel(StreamArgs a) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  float *ring = reinterpret_cast<float *>(smem_raw);  // kRing stages of kStepElems logits
-  uint64_t *cand = reinterpret_cast<uint64_t *>(smem_raw + (size_t)kRingFloats * 4);
+  uint64_t *cand = reinterpret_cast<uint64_t *>(smem_raw);
   uint32_t *hist = reinterpret_cast<uint32_t *>(cand + kCandCap);
-  Shared *sh = reinterpret_cast<Shared *>(hist + kBins);
+  float4 *stage = reinterpret_cast<float4 *>(hist + kBins);  // [kVec][kThreads] prefetch slots
+  Shared *sh = reinterpret_cast<Shared *>(stage + kVec * kThreads);
 
   const int tid = threadIdx.x;
   const int row = blockIdx.x / a.nslices;
@@ -558,32 +753,30 @@ __global__ void __launch_bounds__(kThreads, 2) stream_kernel(StreamArgs a) {
   const float *rowp = a.logits + (int64_t)row * a.row_stride;
   const int lo = sl * a.slice;
   const int hi = min(lo + a.slice, a.vocab);
-  // [a0, a1) is the 16-byte aligned middle of the slice, moved by TMA; the ragged ends
-  // (fewer than 4 logits each) come in through plain loads.
+  // [a0, a1) is the 16-byte aligned middle of the slice, read as float4; the ragged ends
+  // (fewer than 4 logits each) come in through scalar loads.
   const int mis = (int)((reinterpret_cast<uintptr_t>(rowp + lo) >> 2) & 3);
   int a0 = lo + ((4 - mis) & 3);
   if (a0 > hi) a0 = hi;
   const int a1 = a0 + ((max(hi - a0, 0)) & ~3);
   const int ngroups = (a1 - a0) >> 2;  // float4 groups in the aligned middle
-  const int nsteps = (ngroups + kThreads - 1) / kThreads;
+  const int niters = (ngroups + kIterGroups - 1) / kIterGroups;
+  const float4 *p4 = reinterpret_cast<const float4 *>(rowp + a0);
   TRACE(0);
+#ifdef TABBY_TRACE
+  {
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    TRACE_VAL(12, smid);
+  }
+#endif
 
-  // ---- set-up: start the first kRing-1 steps of the ring ----
   if (tid == 0) {
     sh->count = 0;
     sh->flags = 0;
+    sh->overflow = 0;
+    sh->snap = 0;
   }
-  __syncthreads();
-  // Step j's float4 group of thread t is group j*kThreads + t of the aligned middle and
-  // lands in stage j % kRing at the same position.
-  auto issue_step = [&](int jj) {
-    const int gg = jj * kThreads + tid;
-    if (jj < nsteps && gg < ngroups)
-      cp_async16(ring + (size_t)(jj % kRing) * kStepElems + 4 * tid, rowp + a0 + 4 * gg);
-    cp_async_commit();  // one group per step, empty or not, keeps the counting uniform
-  };
-#pragma unroll
-  for (int jj = 0; jj < kRing - 1; jj++) issue_step(jj);
   // Pool size of this row.
   int32_t k;
   uint32_t pflags = 0;
@@ -595,11 +788,14 @@ __global__ void __launch_bounds__(kThreads, 2) stream_kernel(StreamArgs a) {
     k = a.fixed_k;
   }
   k = min(k, a.vocab);
+  __syncthreads();
   TRACE(1);
 
   // Per-thread online statistics: s = sum exp(x - m) as 2^((x - m) * log2(e)).
   constexpr float kLog2e = 1.44269504088896341f;
   float m = -3.40282347e38f, s = 0.f;
+  float mL = 0.f;      // rn(m * log2(e)) for the FFMA form of the exponent argument
+  bool small = false;  // |m| small enough for the FFMA form
   float mn = 3.40282347e38f;  // running min: catches -inf and the -3e38 sentinel
   uint64_t tau = 0;  // accept composites >= tau (an exact lower bound of the row's k-th)
   float tf = -__int_as_float(0x7f800000);  // value of tau's key: a cheap superset filter
@@ -612,77 +808,308 @@ __global__ void __launch_bounds__(kThreads, 2) stream_kernel(StreamArgs a) {
     if (in) {
       x = __ldg(rowp + e);
       m = x;
+      mL = m * kLog2e;
+      small = fabsf(m) <= 16.f;
       s = 1.f;
       mn = x;
     }
-    insert_candidate(in && k > 0, composite(key_of(x), (uint32_t)e), cand, &sh->count);
+    insert_candidate(in && k > 0, composite(key_of(x), (uint32_t)e), cand, &sh->count,
+                     &sh->overflow);
   }
+  __syncthreads();
+  if (tid == 0) sh->snap = sh->count;
+  __syncthreads();
 
-  // ---- one pass: online max / sum-exp and the threshold filter ----
-  const float4 *r4 = reinterpret_cast<const float4 *>(ring);
-  for (int j = 0; j < nsteps; j++) {
-    cp_async_wait<kRing - 2>();  // this thread's copies of step j have landed
-    __syncthreads();             // ... and every other thread's, and step j-1 is consumed
-    issue_step(j + kRing - 1);   // refills the stage step j-1 used
-    if (k > 0 && sh->count > (uint32_t)(kCandCap - kStepElems)) {
-      // Buffer nearly full: keep the k best and raise the threshold (block-uniform).
-      const uint64_t thr = select_top(cand, (int)sh->count, k, hist, sh);
-      if (tid == 0) {
-        sh->count = (uint32_t)k;
-        uint64_t t = thr;
-        if (a.nslices > 1) {
-          atomicMax(&a.row_tau[row], (unsigned long long)thr);
-          const uint64_t g = ld_cg_u64(&a.row_tau[row]);
-          t = thr > g ? thr : g;
-        }
-        sh->tau = t;
+  // Keeps the k best candidates and raises the threshold (block-uniform call).
+  auto compact = [&]() {
+#ifdef TABBY_TRACE
+    if (tid == 0) g_trace[blockIdx.x * kTraceSlots + 9] += 1;
+#endif
+    int kept;
+    const uint64_t thr = shrink_to(cand, (int)sh->count, k, max(2 * k, 1024), hist, sh, &kept);
+    if (tid == 0) {
+      sh->count = (uint32_t)kept;
+      uint64_t t = thr;
+      if (a.nslices > 1) {
+        atomicMax(&a.row_tau[row], (unsigned long long)thr);
+        const uint64_t g = ld_cg_u64(&a.row_tau[row]);
+        t = thr > g ? thr : g;
       }
-      __syncthreads();
-      tau = sh->tau;
-      tf = float_of_key((uint32_t)(tau >> 32));
+      sh->tau = t;
     }
-    const int stage = j % kRing;
-    const int g = j * kThreads + tid;
-    const bool gin = g < ngroups;
-    float4 v = make_float4(-3.40282347e38f, -3.40282347e38f, -3.40282347e38f, -3.40282347e38f);
-    if (gin) v = r4[stage * kThreads + tid];
-    if (gin) {
-      const float gm = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
-      mn = fminf(mn, fminf(fminf(v.x, v.y), fminf(v.z, v.w)));
-      if (gm > m) {
-        s *= ex2_approx((m - gm) * kLog2e);
-        m = gm;
-      }
-      s += ex2_approx((v.x - m) * kLog2e) + ex2_approx((v.y - m) * kLog2e) +
-           ex2_approx((v.z - m) * kLog2e) + ex2_approx((v.w - m) * kLog2e);
-    }
-    const bool hit = gin && k > 0 && (v.x >= tf || v.y >= tf || v.z >= tf || v.w >= tf);
+    __syncthreads();
+    tau = sh->tau;
+    tf = float_of_key((uint32_t)(tau >> 32));
+  };
+  // Inserts the candidates of float4 group g (warp-uniform call; groups past the end
+  // of the slice insert nothing).
+  auto filter_group = [&](const float4 v, const float gm, int g) {
+    const bool hit = k > 0 && g < ngroups && gm >= tf;
     if (__any_sync(0xffffffffu, hit)) {
-      // Rare path: exact composite test and insertion (every lane of the warp is here).
       const float xs[4] = {v.x, v.y, v.z, v.w};
       const int base_idx = a0 + 4 * g;
 #pragma unroll
       for (int e = 0; e < 4; e++) {
         const uint64_t c = composite(key_of(xs[e]), (uint32_t)(base_idx + e));
-        insert_candidate(hit && c >= tau, c, cand, &sh->count);
+        insert_candidate(hit && c >= tau, c, cand, &sh->count, &sh->overflow);
       }
     }
+  };
+
+  // Inserts this thread's candidates among the iteration's kVec groups (warp-uniform
+  // call): one float compare a logit, the exact composite test only for values equal to
+  // the threshold's, one warp-aggregated reservation.
+  auto filter_iter = [&](const float4 *v, const float *gm, int g0) {
+#ifdef TABBY_KNOB_NOFILTER
+    return;
+#endif
+    uint32_t hm = 0;
+#pragma unroll
+    for (int q = 0; q < kVec; q++) {
+      if (k > 0 && g0 + q * kThreads < ngroups && gm[q] >= tf) {
+        hm |= (v[q].x >= tf ? 1u : 0u) << (4 * q);
+        hm |= (v[q].y >= tf ? 2u : 0u) << (4 * q);
+        hm |= (v[q].z >= tf ? 4u : 0u) << (4 * q);
+        hm |= (v[q].w >= tf ? 8u : 0u) << (4 * q);
+      }
+    }
+    if (!__any_sync(0xffffffffu, hm != 0)) return;
+#ifdef TABBY_TRACE
+    if ((tid & 31) == 0) atomicAdd(&g_trace[blockIdx.x * kTraceSlots + 10], 1ull);
+    atomicAdd(&g_trace[blockIdx.x * kTraceSlots + 11], (unsigned long long)__popc(hm));
+#endif
+#pragma unroll
+    for (int q = 0; q < kVec; q++) {
+      if ((hm >> (4 * q)) & 15u) {
+        const float xs[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+        const int base_idx = a0 + 4 * (g0 + q * kThreads);
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+          if (xs[e] == tf && composite(key_of(xs[e]), (uint32_t)(base_idx + e)) < tau)
+            hm &= ~(1u << (4 * q + e));
+      }
+    }
+    const int lane = tid & 31;
+    const int nh = __popc(hm);
+    int incl = nh;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const int wtotal = __shfl_sync(0xffffffffu, incl, 31);
+    if (wtotal == 0) return;
+    uint32_t wbase = 0;
+    if (lane == 31) wbase = atomicAdd(&sh->count, (uint32_t)wtotal);
+    wbase = __shfl_sync(0xffffffffu, wbase, 31);
+    uint32_t slot = wbase + (uint32_t)(incl - nh);
+#pragma unroll
+    for (int q = 0; q < kVec; q++) {
+      const uint32_t gb = (hm >> (4 * q)) & 15u;
+      if (gb) {
+        const float xs[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+        const int base_idx = a0 + 4 * (g0 + q * kThreads);
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          if ((gb >> e) & 1u) {
+            if (slot < (uint32_t)kCandCap)
+              cand[slot] = composite(key_of(xs[e]), (uint32_t)(base_idx + e));
+            else
+              sh->overflow = 1u;
+            slot++;
+          }
+        }
+      }
+    }
+  };
+
+  // ---- one pass: online max / sum-exp and the threshold filter ----
+  // Iteration it: thread t reads groups it*kIterGroups + q*kThreads + t (q < kVec), four
+  // independent 16-byte streaming loads in flight per thread.
+  const float4 kPast = make_float4(-3.40282347e38f, -3.40282347e38f, -3.40282347e38f,
+                                   -3.40282347e38f);
+  // Register double buffering: iteration it+1's loads are in flight while it is used.
+  float4 v[kVec];
+#pragma unroll
+  for (int q = 0; q < kVec; q++) {
+    const int g = tid + q * kThreads;
+    v[q] = g < ngroups ? __ldcs(p4 + g) : kPast;
   }
-  cp_async_wait<0>();
-  __syncthreads();
+  // The next iteration's groups go to this thread's own shared-memory slots by cp.async
+  // (one commit group an iteration), so they stay in flight while this one is worked on.
+  auto prefetch = [&](int itn) {
+#pragma unroll
+    for (int q = 0; q < kVec; q++) {
+      const int g = itn * kIterGroups + tid + q * kThreads;
+      if (itn < niters && g < ngroups) cp_async16(stage + q * kThreads + tid, p4 + g);
+    }
+    cp_async_commit();
+  };
+  prefetch(1);
+#ifdef TABBY_TRACE
+  long long tc_stats = 0, tc_filter = 0, tc_bar = 0, tc_end = 0, tc_t;
+#define TCLK(var) do { const long long _n = clock64(); var += _n - tc_t; tc_t = _n; } while (0)
+#else
+#define TCLK(var) do { } while (0)
+#endif
+  for (int it = 0; it < niters; it++) {
+#ifdef TABBY_TRACE
+    tc_t = clock64();
+#endif
+    const int g0 = it * kIterGroups + tid;
+    // Past-the-end groups hold -FLT_MAX: they never raise the max and add exp(-huge) = 0
+    // to the sum; the filter skips them by index.
+    float gm[kVec];
+#pragma unroll
+    for (int q = 0; q < kVec; q++) {
+      gm[q] = fmaxf(fmaxf(v[q].x, v[q].y), fmaxf(v[q].z, v[q].w));
+      const float lo4 = fminf(fminf(v[q].x, v[q].y), fminf(v[q].z, v[q].w));
+      if (g0 + q * kThreads < ngroups) mn = fminf(mn, lo4);
+    }
+#ifdef TABBY_KNOB_NOSTATS
+    if (0) {
+#else
+    const float im = fmaxf(fmaxf(gm[0], gm[1]), fmaxf(gm[2], gm[3]));
+    if (im > m) {
+#endif
+      s *= ex2_approx((m - im) * kLog2e);
+      m = im;
+      mL = m * kLog2e;
+      // fma(x, L, -rn(m*L)) differs from (x - m)*L by the rounding of m*L, at most
+      // 2^-20 for |m| <= 16: every term then carries a factor within 7e-7 of 1 (well
+      // inside the 1e-5 budget). Larger |m| uses the subtraction form.
+      small = fabsf(m) <= 16.f;
+    }
+#ifdef TABBY_KNOB_NOSTATS
+    if (0) {
+#else
+    if (small) {
+#endif
+#pragma unroll
+      for (int q = 0; q < kVec; q++)
+        s += (ex2_approx(fmaf(v[q].x, kLog2e, -mL)) + ex2_approx(fmaf(v[q].y, kLog2e, -mL))) +
+             (ex2_approx(fmaf(v[q].z, kLog2e, -mL)) + ex2_approx(fmaf(v[q].w, kLog2e, -mL)));
+    } else
+#ifndef TABBY_KNOB_NOSTATS
+    {
+#else
+    if (0) {
+#endif
+#pragma unroll
+      for (int q = 0; q < kVec; q++)
+        s += (ex2_approx((v[q].x - m) * kLog2e) + ex2_approx((v[q].y - m) * kLog2e)) +
+             (ex2_approx((v[q].z - m) * kLog2e) + ex2_approx((v[q].w - m) * kLog2e));
+    }
+    TCLK(tc_stats);
+#ifdef TABBY_KNOB_NOBOOT
+    if (0) {
+#else
+    if (it == 0 && k > 0) {
+#endif
+      // Bootstrap threshold from this first iteration (registers): the per-thread maxima of
+      // every 8th thread form a 64-value sample; the highest sample value with at least k
+      // logits of the iteration at or above it is a valid lower bound of the k-th largest.
+      float tmax = fmaxf(fmaxf(gm[0], gm[1]), fmaxf(gm[2], gm[3]));
+      if ((tid & 7) == 0) sh->samp[tid >> 3] = (uint64_t)key_of(tmax) << 32;
+      __syncthreads();
+      if (tid < 32) {
+        uint64_t s0 = sh->samp[2 * tid], s1 = sh->samp[2 * tid + 1];
+        warp_sort64_desc(s0, s1);
+        sh->samp[2 * tid] = s0;
+        sh->samp[2 * tid + 1] = s1;
+      }
+      __syncthreads();
+      for (int r = 0; r < 64; r = 2 * r + 1) {
+        const float t = float_of_key((uint32_t)(sh->samp[r] >> 32));
+        int c = 0;
+#pragma unroll
+        for (int q = 0; q < kVec; q++)
+          if (g0 + q * kThreads < ngroups)
+            c += (v[q].x >= t) + (v[q].y >= t) + (v[q].z >= t) + (v[q].w >= t);
+        c = __reduce_add_sync(0xffffffffu, c);
+        __syncthreads();
+        if ((tid & 31) == 0) sh->red_u[tid >> 5] = (uint32_t)c;
+        __syncthreads();
+        int total = 0;
+#pragma unroll
+        for (int w = 0; w < kWarps; w++) total += (int)sh->red_u[w];
+        if (total >= k) {
+          tf = t;
+          tau = sh->samp[r];  // key(t) << 32: every logit >= t has a composite >= it
+          break;
+        }
+      }
+      __syncthreads();
+    }
+    filter_iter(v, gm, g0);
+    TCLK(tc_filter);
+    __syncthreads();
+    TCLK(tc_bar);
+    // Move to the next iteration: this thread's slots hold its groups of iteration it+1.
+    cp_async_wait_all();
+#pragma unroll
+    for (int q = 0; q < kVec; q++) {
+      const int g = g0 + kIterGroups + q * kThreads;
+      v[q] = g < ngroups ? stage[q * kThreads + tid] : kPast;
+    }
+    prefetch(it + 2);  // reuses the slots just read (same thread, values already in registers)
+    if (sh->overflow) {
+#ifdef TABBY_TRACE
+      (void)0;
+#endif
+      // The buffer filled during this iteration (only before the threshold settles):
+      // drop the iteration's inserts and filter it again from L2 one float4 a thread at
+      // a time, compacting between the sub-steps.
+      __syncthreads();
+      if (tid == 0) {
+        sh->count = sh->snap;
+        sh->overflow = 0;
+      }
+      __syncthreads();
+      for (int q = 0; q < kVec; q++) {
+        if (sh->count > (uint32_t)(kCandCap - kThreads * 4)) compact();
+        const int g = g0 + q * kThreads;
+        const float4 w = g < ngroups ? __ldcg(p4 + g) : kPast;
+        filter_group(w, fmaxf(fmaxf(w.x, w.y), fmaxf(w.z, w.w)), g);
+        __syncthreads();
+      }
+    }
+    if (k > 0 && sh->count > (uint32_t)(kCandCap / 2)) compact();
+    if (tid == 0) sh->snap = sh->count;
+#ifndef TABBY_KNOB_ONEBAR
+    __syncthreads();
+#endif
+    TCLK(tc_end);
+    if (it == 0) TRACE(8);
+  }
   TRACE(2);
+#ifdef TABBY_TRACE
+  TRACE_VAL(13, tc_stats);
+  TRACE_VAL(14, tc_filter);
+  TRACE_VAL(15, tc_bar);
+  TRACE_VAL(4, tc_end);
+#endif
+#ifdef TABBY_KNOB_NOEPI
+  if (s == 12345.f && tid == 0) a.out[row].id = (int)m;
+  return;
+#endif
   // NaN or +inf logits leave s or m non-finite; -inf and values at or below the
   // reference's -3.0e38 sentinel show in the running min.
   const bool bad = !(s == s) || !(m <= 3.40282347e38f) || !(mn > kNegSentinel) ||
                    !(s <= 3.40282347e38f);
 
   // ---- this slice's <= k best and its (max, sum-exp) partial ----
+  // The slice's k best, sorted by (value desc, index asc): cut to at most 2048 that
+  // include them, sort, keep the first min(k, cnt).
   int cnt = (int)sh->count;
-  if (k > 0 && cnt > k) {
-    const uint64_t thr = select_top(cand, cnt, k, hist, sh);
+  if (k > 0 && cnt > 2048) {
+    int kept;
+    const uint64_t thr = shrink_to(cand, cnt, k, 2048, hist, sh, &kept);
     if (tid == 0 && a.nslices > 1) atomicMax(&a.row_tau[row], (unsigned long long)thr);
-    cnt = k;
+    cnt = kept;
   }
+  block_sort_desc_2k(cand, cnt);
+  cnt = min(cnt, k);
   float M, S;
   uint32_t flags;
   {
@@ -785,15 +1212,18 @@ __global__ void __launch_bounds__(kThreads, 2) stream_kernel(StreamArgs a) {
       total += add;
       q0 = q1;
       __syncthreads();
-      if (q0 < a.nslices && total > k) {
-        select_top(cand, total, k, hist, sh);
-        total = k;
+      if (q0 < a.nslices && total > kCandCap / 2) {
+        int kept;
+        shrink_to(cand, total, k, 2048, hist, sh, &kept);
+        total = kept;
       }
     }
-    if (k > 0 && total > k) {
-      select_top(cand, total, k, hist, sh);
-      total = k;
+    if (k > 0 && total > 2048) {
+      int kept;
+      shrink_to(cand, total, k, 2048, hist, sh, &kept);
+      total = kept;
     }
+    block_sort_desc_2k(cand, total);
     kk = min(k, total);
     if (tid == 0) {
       // Leave the row's counters clean for the next launch.
@@ -802,19 +1232,19 @@ __global__ void __launch_bounds__(kThreads, 2) stream_kernel(StreamArgs a) {
     }
   }
   TRACE(5);
-  block_sort_desc(cand, kk);
   TRACE(6);
 
   const uint32_t status = (flags & kFlagBadInput)    ? (uint32_t)TABBY_EINPUT
                           : (flags & kFlagBadParams) ? (uint32_t)TABBY_EINVAL
                           : (flags & kFlagTimeout)   ? (uint32_t)TABBY_ETIMEOUT
                                                      : (uint32_t)TABBY_OK;
-  // Unpack into (id, value); the finalize arrays reuse the (drained) ring.
-  double *exact = reinterpret_cast<double *>(ring);
+  // Unpack into (id, value) in the histogram space; once that is done the candidate
+  // buffer holds the float64 finalize arrays.
+  int32_t *ids = reinterpret_cast<int32_t *>(hist);
+  float *vals = reinterpret_cast<float *>(ids + kk);
+  double *exact = reinterpret_cast<double *>(cand);
   double *scaled = exact + kk;
   double *cum = scaled + kk;
-  int32_t *ids = reinterpret_cast<int32_t *>(cum + kk);
-  float *vals = reinterpret_cast<float *>(ids + kk);
   for (int i = tid; i < kk; i += kThreads) {
     const uint64_t e = cand[i];
     const uint32_t key = (uint32_t)(e >> 32);
@@ -945,7 +1375,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch a) {
 static int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
 static size_t stream_smem_bytes() {
-  return (size_t)kRingFloats * 4 + (size_t)kCandCap * 8 + (size_t)kBins * 4 +
+  return (size_t)kCandCap * 8 + (size_t)kBins * 4 + (size_t)kVec * kThreads * 16 +
          sizeof(Shared) + 64;
 }
 
@@ -963,7 +1393,7 @@ cudaError_t plan_rows(int32_t sms, int32_t rows, int32_t vocab, int32_t cap, Row
   RowGeometry g;
   g.slice = round_up((vocab + S - 1) / S, 4);
   g.nslices = (vocab + g.slice - 1) / g.slice;
-  g.data_floats = kRingFloats;
+  g.data_floats = 0;
   g.smem_bytes = stream_smem_bytes();
   *geo = g;
   return cudaSuccess;
