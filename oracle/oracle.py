@@ -200,3 +200,72 @@ def bench_rows(logits: np.ndarray, params: np.ndarray, uniforms: np.ndarray, cap
     return lib().or_bench_rows(
         _ptr(logits), vocab, rows, vocab, _ptr(params), _ptr(uniforms), cap, threads
     )
+
+
+# ---------------------------------------------------------------------------------------
+# Vocab-sharded sampling (a multi-GPU protocol new in this build; the reference samples
+# one row on one device). The restatement below defines what the sharded path must equal:
+# local (max, sum-exp, top-64) per shard, then M = max m_s, S = sum s_s * exp(m_s - M),
+# the global top-k by (value desc, index asc) and sampleFromTopK (sampler.ts:147-212).
+# ---------------------------------------------------------------------------------------
+SHARD_TOP_K = 64
+
+
+def shard_local_block(x: np.ndarray, offset: int) -> np.ndarray:
+    """[rows, 2 + 2*64] float32 blocks for the columns [offset, offset + x.shape[1])."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows = x.shape[0]
+    blk = np.zeros((rows, 2 + 2 * SHARD_TOP_K), np.float32)
+    u = blk.view(np.uint32)
+    for r in range(rows):
+        m = row_max(x[r])
+        blk[r, 0] = m
+        blk[r, 1] = np.float32(sum_exp_f64(x[r], m))
+        ids, vals = topk(x[r], SHARD_TOP_K)
+        blk[r, 2::2] = -np.inf
+        u[r, 3::2] = 0xFFFFFFFF
+        blk[r, 2:2 + 2 * ids.size:2] = vals
+        u[r, 3:3 + 2 * ids.size:2] = (ids.astype(np.int64) + offset).astype(np.uint32)
+    return blk
+
+
+def shard_merge(blocks: np.ndarray, shards: int, params: np.ndarray, uniforms: np.ndarray):
+    """blocks: [shards * rows, 130] rank-major. Returns (outcomes, topk_ids, topk_values)."""
+    import math
+
+    blocks = np.ascontiguousarray(blocks, dtype=np.float32)
+    rows = blocks.shape[0] // shards
+    u32 = blocks.view(np.uint32)
+    out = np.zeros(rows, OUTCOME_DTYPE)
+    tids = np.full((rows, SHARD_TOP_K), -1, np.int32)
+    tvals = np.zeros((rows, SHARD_TOP_K), np.float32)
+    for r in range(rows):
+        b = [blocks[s * rows + r] for s in range(shards)]
+        bu = [u32[s * rows + r] for s in range(shards)]
+        M = max(float(x[0]) for x in b)
+        S = 0.0
+        for x in b:
+            if x[1] > 0:
+                S += float(x[1]) * js_exp(float(x[0]) - M)
+        cand = []
+        for x, xu in zip(b, bu):
+            for j in range(SHARD_TOP_K):
+                if xu[3 + 2 * j] != 0xFFFFFFFF:
+                    v = float(x[2 + 2 * j])
+                    cand.append((-(v + 0.0), int(xu[3 + 2 * j]), x[2 + 2 * j]))
+        cand.sort(key=lambda c: (c[0], c[1]))
+        p = params[r]
+        k = min(pool_size(p["temperature"], p["top_k"], SHARD_TOP_K), len(cand))
+        ids = np.array([c[1] for c in cand[:k]], np.int32)
+        vals = np.array([c[2] for c in cand[:k]], np.float32)
+        o = np.zeros(1, OUTCOME_DTYPE)
+        rc = lib().or_sample_from_topk(
+            _ptr(ids), _ptr(vals), k, float(vals[0]) if k else M, float(np.float32(S)),
+            float(p["temperature"]), float(p["top_p"]), float(uniforms[r]), _ptr(o))
+        if rc != 0:
+            raise ValueError("sampleFromTopK: empty candidate set")
+        o["pool_size"] = k
+        out[r] = o[0]
+        tids[r, :k] = ids
+        tvals[r, :k] = vals
+    return out, tids, tvals
