@@ -38,7 +38,7 @@ namespace tabby {
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kVec = 4;                   // float4 loads in flight per thread per iteration
-constexpr int kIterGroups = kThreads * kVec;  // float4 groups per iteration (8K logits)
+constexpr int kWarpIter = 32 * kVec;      // float4 groups a warp reads per iteration (2 KB)
 constexpr int kCandCap = 8192;            // candidate buffer (composites) per CTA
 constexpr int kBins = 2048;               // radix digit: 11 bits
 constexpr int kMaxSlices = 32;            // slices of one row (one warp merges their stats)
@@ -142,6 +142,18 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
+// Three-input float max / min (sm_100 max.f32 / min.f32 with three sources).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // 2^x by the MUFU.EX2 approximation (flush-to-zero).
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -181,7 +193,6 @@ struct Shared {
   int32_t fallback;
   uint32_t flags;
   uint32_t overflow;  // an insert found the candidate buffer full
-  uint32_t snap;      // candidate count at the start of the current iteration
   uint64_t tau;  // accept composites >= tau
   float red_f[kWarps];
   uint32_t red_u[kWarps];
@@ -692,6 +703,234 @@ __device__ __noinline__ void finalize_sample(const int32_t *ids, const float *va
   }
 }
 
+// Merges the sorted 64-list (w0, w1) into the sorted 64-list (v0, v1) (both descending,
+// lane l holding elements 2l and 2l+1), keeping the 64 largest, sorted. The elementwise
+// max of one list and the other reversed holds exactly the 64 largest of both and is
+// bitonic; a bitonic merge sorts it.
+__device__ __forceinline__ void warp_merge64_desc(uint64_t &v0, uint64_t &v1, uint64_t w0,
+                                                  uint64_t w1) {
+  const int lane = threadIdx.x & 31;
+  const uint64_t r0 = __shfl_sync(0xffffffffu, w1, 31 - lane);
+  const uint64_t r1 = __shfl_sync(0xffffffffu, w0, 31 - lane);
+  v0 = v0 > r0 ? v0 : r0;
+  v1 = v1 > r1 ? v1 : r1;
+#pragma unroll
+  for (int stride = 32; stride >= 2; stride >>= 1) {
+    const uint64_t p0 = __shfl_xor_sync(0xffffffffu, v0, stride >> 1);
+    const uint64_t p1 = __shfl_xor_sync(0xffffffffu, v1, stride >> 1);
+    const bool lower = ((2 * lane) & stride) == 0;
+    v0 = lower ? (v0 > p0 ? v0 : p0) : (v0 < p0 ? v0 : p0);
+    v1 = lower ? (v1 > p1 ? v1 : p1) : (v1 < p1 ? v1 : p1);
+  }
+  const uint64_t hi = v0 > v1 ? v0 : v1;
+  v1 = v0 > v1 ? v1 : v0;
+  v0 = hi;
+}
+
+// The min(64, n) largest of cand[0, n), sorted descending, into cand[0, 64) (zeros past
+// n). Block-uniform call. Every warp keeps a running top 64 of its share in registers
+// (sort 64, merge); a four-level tree then merges the 16 lists through tmp (960 slots),
+// one barrier a level.
+__device__ __noinline__ void top64_sorted(uint64_t *cand, int n, uint64_t *tmp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int per = ((n + kWarps - 1) / kWarps + 63) & ~63;
+  const int b0 = min(n, warp * per), b1 = min(n, b0 + per);
+  uint64_t a0 = 0, a1 = 0;
+  for (int base = b0; base < b1; base += 64) {
+    uint64_t c0 = base + 2 * lane < b1 ? cand[base + 2 * lane] : 0ull;
+    uint64_t c1 = base + 2 * lane + 1 < b1 ? cand[base + 2 * lane + 1] : 0ull;
+    warp_sort64_desc(c0, c1);
+    if (base == b0) {
+      a0 = c0;
+      a1 = c1;
+    } else {
+      warp_merge64_desc(a0, a1, c0, c1);
+    }
+  }
+  int off = 0;
+#pragma unroll
+  for (int h = kWarps / 2; h >= 1; h >>= 1) {
+    if (warp >= h && warp < 2 * h) {
+      tmp[off + (warp - h) * 64 + 2 * lane] = a0;
+      tmp[off + (warp - h) * 64 + 2 * lane + 1] = a1;
+    }
+    __syncthreads();
+    if (warp < h)
+      warp_merge64_desc(a0, a1, tmp[off + warp * 64 + 2 * lane], tmp[off + warp * 64 + 2 * lane + 1]);
+    off += h * 64;
+  }
+  if (warp == 0) {
+    cand[2 * lane] = a0;
+    cand[2 * lane + 1] = a1;
+  }
+  __syncthreads();
+}
+
+// sampleFromTopK for n <= 64 candidates in one warp (lane l holds candidates 2l, 2l+1:
+// logits x0, x1), with warp shuffles only. Same float64 arithmetic, the same error bound
+// on the parallel sums and the same sequential replay as finalize_sample; `scratch`
+// holds 192 doubles for the replay.
+__device__ __noinline__ void finalize_warp(int32_t id0, int32_t id1, float x0, float x1, int n,
+                                           float max_logit, float sum_exp,
+                                           tabby_sampling_params p, double u, double *scratch,
+                                           tabby_sample_outcome *out, uint32_t status) {
+  const unsigned kAll = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  if (status != TABBY_OK || n == 0) {
+    if (lane == 0) {
+      tabby_sample_outcome o;
+      o.id = -1;
+      o.considered_count = 0;
+      o.probability = 0.0;
+      o.pool_mass = 0.0;
+      o.pool_exhausted = 0;
+      o.pool_size = n;
+      o.max_logit = max_logit;
+      o.sum_exp = sum_exp;
+      o.status = status != TABBY_OK ? (int32_t)status : (int32_t)TABBY_EEMPTY;
+      o.reserved = 0;
+      *out = o;
+    }
+    return;
+  }
+  const bool sample = p.temperature > 0;
+  const int i0 = 2 * lane, i1 = i0 + 1;
+  const double e0 = i0 < n ? exact_prob(x0, max_logit, sum_exp) : 0.0;
+  const double e1 = i1 < n ? exact_prob(x1, max_logit, sum_exp) : 0.0;
+  const double s0 = (sample && i0 < n) ? scaled_weight(x0, max_logit, p.temperature) : 0.0;
+  const double s1 = (sample && i1 < n) ? scaled_weight(x1, max_logit, p.temperature) : 0.0;
+  double pm = JS_ADD(e0, e1);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) pm = JS_ADD(pm, __shfl_xor_sync(kAll, pm, o));
+  const double bound = 4.0 * (double)(2 * n + 2 * 11 + 3) * 1.1102230246251565e-16;
+
+  int32_t cut = 1, chosen = 0, exhausted = 0;
+  bool fallback = false;
+  double c0 = 0.0, c1 = 0.0;
+  // cum[i] from the lane that holds it (i warp-uniform).
+  auto cum_at = [&](int i) -> double {
+    const double a = __shfl_sync(kAll, c0, (i >> 1) & 31);
+    const double b = __shfl_sync(kAll, c1, (i >> 1) & 31);
+    return (i & 1) ? b : a;
+  };
+  if (sample) {
+    double st = JS_ADD(s0, s1);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) st = JS_ADD(st, __shfl_xor_sync(kAll, st, o));
+    const double w0 = i0 < n ? JS_DIV(s0, st) : 0.0;
+    const double w1 = i1 < n ? JS_DIV(s1, st) : 0.0;
+    double incl = JS_ADD(w0, w1);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double t = __shfl_up_sync(kAll, incl, o);
+      if (lane >= o) incl = JS_ADD(t, incl);
+    }
+    double excl = __shfl_up_sync(kAll, incl, 1);
+    if (lane == 0) excl = 0.0;
+    c0 = JS_ADD(excl, w0);
+    c1 = JS_ADD(c0, w1);
+    cut = n;
+    if (p.top_p < 1) {
+      // First i with cumulative >= top_p (sampler.ts:175-189).
+      const bool h0 = i0 < n && c0 >= p.top_p, h1 = i1 < n && c1 >= p.top_p;
+      const unsigned bal = __ballot_sync(kAll, h0 || h1);
+      int ci = n;
+      if (bal) {
+        const int L = __ffs(bal) - 1;
+        ci = __shfl_sync(kAll, h0 ? 1 : 0, L) ? 2 * L : 2 * L + 1;
+      }
+      exhausted = pm < p.top_p ? 1 : 0;
+      bool ok = fabs(pm - p.top_p) > bound;
+      if (ci < n) {
+        const double here = cum_at(ci), prev = cum_at(ci > 0 ? ci - 1 : 0);
+        ok = ok && (here - p.top_p > bound) && (ci == 0 || p.top_p - prev > bound);
+      } else {
+        ok = ok && (p.top_p - cum_at(n - 1) > bound);
+      }
+      fallback = !ok;
+      cut = ci < n ? ci + 1 : n;
+    }
+    // target = u * total; first i < cut with target < cumulative (sampler.ts:191-203).
+    const double target = JS_MUL(u, cum_at(cut - 1));
+    const bool g0 = i0 < cut && target < c0, g1 = i1 < cut && target < c1;
+    const unsigned bal = __ballot_sync(kAll, g0 || g1);
+    int ch = cut;
+    if (bal) {
+      const int L = __ffs(bal) - 1;
+      ch = __shfl_sync(kAll, g0 ? 1 : 0, L) ? 2 * L : 2 * L + 1;
+    }
+    bool ok = ch < cut;
+    if (ok) {
+      const double here = cum_at(ch), prev = cum_at(ch > 0 ? ch - 1 : 0);
+      ok = (here - target > 2 * bound) && (ch == 0 || target - prev > 2 * bound);
+    }
+    fallback = fallback || !ok;
+    chosen = ch < cut ? ch : cut - 1;
+  }
+  if (fallback) {
+    // Exact replay of the reference's left-to-right float64 arithmetic.
+    double *ex = scratch, *sc = scratch + 64, *wt = scratch + 128;
+    ex[i0] = e0;
+    ex[i1] = e1;
+    sc[i0] = s0;
+    sc[i1] = s1;
+    __syncwarp();
+    int32_t dv[4] = {0, 0, 0, 0};
+    double dpm = 0.0;
+    if (lane == 0) {
+      const Decision d = decide_sequential(ex, sc, wt, n, p.temperature, p.top_p, u);
+      dv[0] = d.chosen;
+      dv[1] = d.cut;
+      dv[2] = d.pool_exhausted;
+      dpm = d.pool_mass;
+    }
+    chosen = __shfl_sync(kAll, dv[0], 0);
+    cut = __shfl_sync(kAll, dv[1], 0);
+    exhausted = __shfl_sync(kAll, dv[2], 0);
+    pm = __shfl_sync(kAll, dpm, 0);
+  }
+  const int32_t cid = __shfl_sync(kAll, (chosen & 1) ? id1 : id0, (chosen >> 1) & 31);
+  const double cprob = __shfl_sync(kAll, (chosen & 1) ? e1 : e0, (chosen >> 1) & 31);
+  if (lane == 0) {
+    tabby_sample_outcome o;
+    o.id = cid;
+    o.considered_count = cut;
+    o.probability = cprob;
+    o.pool_mass = pm;
+    o.pool_exhausted = exhausted;
+    o.pool_size = n;
+    o.max_logit = max_logit;
+    o.sum_exp = sum_exp;
+    o.status = TABBY_OK;
+    o.reserved = fallback ? 1 : 0;  // 1 when the sequential replay decided
+    *out = o;
+  }
+}
+
+// The min(k, n) largest of cand[0, n) (k <= 1024), sorted descending, at cand[0, ...);
+// returns how many. Block-uniform call. Pools of at most 64 go through the per-warp
+// top-64 tree; larger ones through the exact radix select, then a sort of the k kept.
+__device__ __forceinline__ int top_sorted(uint64_t *cand, int n, int k, uint32_t *hist,
+                                          Shared *sh) {
+  if (k <= 0 || n <= 0) {
+    __syncthreads();
+    return 0;
+  }
+  if (k <= 64) {
+    if (n <= 64)
+      block_sort_desc(cand, n);
+    else
+      top64_sorted(cand, n, reinterpret_cast<uint64_t *>(hist));
+    return min(k, n);
+  }
+  if (n > k) {
+    select_top(cand, n, k, hist, sh);
+    n = k;
+  }
+  block_sort_desc(cand, n);
+  return n;
+}
+
 // ------------------------------------------------------------------------------------
 // The streaming kernel.
 // ------------------------------------------------------------------------------------
@@ -744,8 +983,7 @@ __global__ void __launch_bounds__(kThreads, TABBY_MIN_BLOCKS) stream_kernel(Stre
   extern __shared__ __align__(128) unsigned char smem_raw[];
   uint64_t *cand = reinterpret_cast<uint64_t *>(smem_raw);
   uint32_t *hist = reinterpret_cast<uint32_t *>(cand + kCandCap);
-  float4 *stage = reinterpret_cast<float4 *>(hist + kBins);  // [kVec][kThreads] prefetch slots
-  Shared *sh = reinterpret_cast<Shared *>(stage + kVec * kThreads);
+  Shared *sh = reinterpret_cast<Shared *>(hist + kBins);
 
   const int tid = threadIdx.x;
   const int row = blockIdx.x / a.nslices;
@@ -760,7 +998,6 @@ __global__ void __launch_bounds__(kThreads, TABBY_MIN_BLOCKS) stream_kernel(Stre
   if (a0 > hi) a0 = hi;
   const int a1 = a0 + ((max(hi - a0, 0)) & ~3);
   const int ngroups = (a1 - a0) >> 2;  // float4 groups in the aligned middle
-  const int niters = (ngroups + kIterGroups - 1) / kIterGroups;
   const float4 *p4 = reinterpret_cast<const float4 *>(rowp + a0);
   TRACE(0);
 #ifdef TABBY_TRACE
@@ -775,7 +1012,6 @@ __global__ void __launch_bounds__(kThreads, TABBY_MIN_BLOCKS) stream_kernel(Stre
     sh->count = 0;
     sh->flags = 0;
     sh->overflow = 0;
-    sh->snap = 0;
   }
   // Pool size of this row.
   int32_t k;
@@ -797,34 +1033,136 @@ __global__ void __launch_bounds__(kThreads, TABBY_MIN_BLOCKS) stream_kernel(Stre
   float mL = 0.f;      // rn(m * log2(e)) for the FFMA form of the exponent argument
   bool small = false;  // |m| small enough for the FFMA form
   float mn = 3.40282347e38f;  // running min: catches -inf and the -3e38 sentinel
-  uint64_t tau = 0;  // accept composites >= tau (an exact lower bound of the row's k-th)
+  uint64_t tau = 0;  // accept composites >= tau
   float tf = -__int_as_float(0x7f800000);  // value of tau's key: a cheap superset filter
+  const int warp = tid >> 5, lane = tid & 31;
+  const int slice_len = hi - lo;
+  const int need = min(k, slice_len);  // candidates >= tau the slice must end with
 
   // Ragged ends: at most 3 logits before a0 and 3 after a1, one per thread of warp 0.
-  if (tid < 32) {
+  // Their statistics count now; they join the candidates once the threshold is known.
+  float rx = 0.f;
+  int re = -1;
+  if (tid < 8) {
     const int e = tid < 4 ? lo + tid : a1 + (tid - 4);
-    const bool in = tid < 8 && (tid < 4 ? (e < a0) : (e < hi));
-    float x = 0.f;
-    if (in) {
-      x = __ldg(rowp + e);
-      m = x;
+    if (tid < 4 ? (e < a0) : (e < hi)) {
+      rx = __ldg(rowp + e);
+      re = e;
+      m = rx;
       mL = m * kLog2e;
       small = fabsf(m) <= 16.f;
       s = 1.f;
-      mn = x;
+      mn = rx;
     }
-    insert_candidate(in && k > 0, composite(key_of(x), (uint32_t)e), cand, &sh->count,
-                     &sh->overflow);
   }
-  __syncthreads();
-  if (tid == 0) sh->snap = sh->count;
-  __syncthreads();
+
+  // Warp segments: warp w streams the float4 groups [sg0, sg0 + wn) of the aligned
+  // middle, 128 groups (2 KB, four 512-byte coalesced loads) an iteration.
+  const int seg = (ngroups + kWarps - 1) / kWarps;
+  const int sg0 = min(warp * seg, ngroups);
+  const int wn = min(sg0 + seg, ngroups) - sg0;
+  const int wit = (wn + kWarpIter - 1) / kWarpIter;
+  const float4 *wp = p4 + sg0;
+  const int gbase = a0 + 4 * sg0;  // logit index of this warp's first group
+  const float4 kPast = make_float4(-3.40282347e38f, -3.40282347e38f, -3.40282347e38f,
+                                   -3.40282347e38f);
+
+  auto load_iter = [&](float4 (&dst)[kVec], int it) {
+#pragma unroll
+    for (int q = 0; q < kVec; q++) {
+      const int g = it * kWarpIter + q * 32 + lane;
+      dst[q] = g < wn ? __ldcs(wp + g) : kPast;
+    }
+  };
+  // Online max / sum-exp over one iteration's 16 values. Groups past the segment hold
+  // -FLT_MAX: they never raise the max and add exp(-huge) = 0 to the sum.
+  auto stats_iter = [&](const float4 (&v)[kVec], int it) -> float {
+    float im = max3f(max3f(v[0].x, v[0].y, v[0].z), max3f(v[0].w, v[1].x, v[1].y),
+                     max3f(v[1].z, v[1].w, v[2].x));
+    im = max3f(im, max3f(v[2].y, v[2].z, v[2].w), max3f(v[3].x, v[3].y, max3f(v[3].z, v[3].w, im)));
+    if (it + 1 < wit) {
+      float l = min3f(min3f(v[0].x, v[0].y, v[0].z), min3f(v[0].w, v[1].x, v[1].y),
+                      min3f(v[1].z, v[1].w, v[2].x));
+      l = min3f(l, min3f(v[2].y, v[2].z, v[2].w), min3f(v[3].x, v[3].y, min3f(v[3].z, v[3].w, l)));
+      mn = fminf(mn, l);
+    } else {
+#pragma unroll
+      for (int q = 0; q < kVec; q++)
+        if (it * kWarpIter + q * 32 + lane < wn)
+          mn = min3f(mn, min3f(v[q].x, v[q].y, v[q].z), v[q].w);
+    }
+    if (im > m) {
+      s *= ex2_approx((m - im) * kLog2e);
+      m = im;
+      mL = m * kLog2e;
+      // fma(x, L, -rn(m*L)) differs from (x - m)*L by the rounding of m*L, at most
+      // 2^-20 for |m| <= 16: every term then carries a factor within 7e-7 of 1 (well
+      // inside the 1e-5 budget). Larger |m| uses the subtraction form.
+      small = fabsf(m) <= 16.f;
+    }
+    if (small) {
+#pragma unroll
+      for (int q = 0; q < kVec; q++)
+        s += (ex2_approx(fmaf(v[q].x, kLog2e, -mL)) + ex2_approx(fmaf(v[q].y, kLog2e, -mL))) +
+             (ex2_approx(fmaf(v[q].z, kLog2e, -mL)) + ex2_approx(fmaf(v[q].w, kLog2e, -mL)));
+    } else {
+#pragma unroll
+      for (int q = 0; q < kVec; q++)
+        s += (ex2_approx((v[q].x - m) * kLog2e) + ex2_approx((v[q].y - m) * kLog2e)) +
+             (ex2_approx((v[q].z - m) * kLog2e) + ex2_approx((v[q].w - m) * kLog2e));
+    }
+    return im;
+  };
+  // Appends this iteration's logits >= tf (warp-uniform call). On this path tau carries
+  // no index bits, so the float compare is the whole test. Slots past kCandCap are not
+  // written; the overflow flag sends the slice to the re-filter at the end.
+  auto filter_iter = [&](const float4 (&v)[kVec], int it, float im) {
+    if (!__any_sync(0xffffffffu, im >= tf)) return;
+    uint32_t hm = 0;
+#pragma unroll
+    for (int q = 0; q < kVec; q++) {
+      if (it * kWarpIter + q * 32 + lane < wn) {
+        hm |= (v[q].x >= tf ? 1u : 0u) << (4 * q);
+        hm |= (v[q].y >= tf ? 2u : 0u) << (4 * q);
+        hm |= (v[q].z >= tf ? 4u : 0u) << (4 * q);
+        hm |= (v[q].w >= tf ? 8u : 0u) << (4 * q);
+      }
+    }
+    const int nh = __popc(hm);
+    int incl = nh;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const int wtotal = __shfl_sync(0xffffffffu, incl, 31);
+    if (wtotal == 0) return;
+    uint32_t wb = 0;
+    if (lane == 31) wb = atomicAdd(&sh->count, (uint32_t)wtotal);
+    wb = __shfl_sync(0xffffffffu, wb, 31);
+    uint32_t slot = wb + (uint32_t)(incl - nh);
+#pragma unroll
+    for (int q = 0; q < kVec; q++) {
+      const uint32_t gb = (hm >> (4 * q)) & 15u;
+      if (gb) {
+        const float xs[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+        const int base_idx = gbase + 4 * (it * kWarpIter + q * 32 + lane);
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          if ((gb >> e) & 1u) {
+            if (slot < (uint32_t)kCandCap)
+              cand[slot] = composite(key_of(xs[e]), (uint32_t)(base_idx + e));
+            else
+              sh->overflow = 1u;
+            slot++;
+          }
+        }
+      }
+    }
+  };
 
   // Keeps the k best candidates and raises the threshold (block-uniform call).
   auto compact = [&]() {
-#ifdef TABBY_TRACE
-    if (tid == 0) g_trace[blockIdx.x * kTraceSlots + 9] += 1;
-#endif
     int kept;
     const uint64_t thr = shrink_to(cand, (int)sh->count, k, max(2 * k, 1024), hist, sh, &kept);
     if (tid == 0) {
@@ -841,12 +1179,12 @@ __global__ void __launch_bounds__(kThreads, TABBY_MIN_BLOCKS) stream_kernel(Stre
     tau = sh->tau;
     tf = float_of_key((uint32_t)(tau >> 32));
   };
-  // Inserts the candidates of float4 group g (warp-uniform call; groups past the end
-  // of the slice insert nothing).
-  auto filter_group = [&](const float4 v, const float gm, int g) {
-    const bool hit = k > 0 && g < ngroups && gm >= tf;
+  // Inserts the candidates of float4 group g of the aligned middle (warp-uniform call;
+  // groups past the end of the slice insert nothing).
+  auto filter_group = [&](const float4 w, const float gm, int g) {
+    const bool hit = g < ngroups && gm >= tf;
     if (__any_sync(0xffffffffu, hit)) {
-      const float xs[4] = {v.x, v.y, v.z, v.w};
+      const float xs[4] = {w.x, w.y, w.z, w.w};
       const int base_idx = a0 + 4 * g;
 #pragma unroll
       for (int e = 0; e < 4; e++) {
@@ -856,243 +1194,106 @@ __global__ void __launch_bounds__(kThreads, TABBY_MIN_BLOCKS) stream_kernel(Stre
     }
   };
 
-  // Inserts this thread's candidates among the iteration's kVec groups (warp-uniform
-  // call): one float compare a logit, the exact composite test only for values equal to
-  // the threshold's, one warp-aggregated reservation.
-  auto filter_iter = [&](const float4 *v, const float *gm, int g0) {
-#ifdef TABBY_KNOB_NOFILTER
-    return;
-#endif
-    uint32_t hm = 0;
+  // ---- iteration 0 of every warp, then the threshold estimate ----
+  float4 v[kVec], nx[kVec];
+  load_iter(v, 0);
+  if (wit > 1) load_iter(nx, 1);
+  const float im0 = wit > 0 ? stats_iter(v, 0) : -3.40282347e38f;
+  if (k > 0) {
+    // The 16 first iterations (one per warp, spread over the slice) are the sample. The
+    // threshold is a logit with about rr sample logits at or above it, rr set so that
+    // the slice holds at least k logits above it with near certainty (rr = mu +
+    // 3 sqrt(mu) + 4, mu the expected sample count above the slice's k-th largest). The
+    // end of the pass checks it; a failed estimate (fewer than k above it, or more than
+    // the buffer holds) re-filters the slice.
+    uint64_t t1 = 0, t2 = 0;
+    if (wit > 0) {
 #pragma unroll
-    for (int q = 0; q < kVec; q++) {
-      if (k > 0 && g0 + q * kThreads < ngroups && gm[q] >= tf) {
-        hm |= (v[q].x >= tf ? 1u : 0u) << (4 * q);
-        hm |= (v[q].y >= tf ? 2u : 0u) << (4 * q);
-        hm |= (v[q].z >= tf ? 4u : 0u) << (4 * q);
-        hm |= (v[q].w >= tf ? 8u : 0u) << (4 * q);
-      }
-    }
-    if (!__any_sync(0xffffffffu, hm != 0)) return;
-#ifdef TABBY_TRACE
-    if ((tid & 31) == 0) atomicAdd(&g_trace[blockIdx.x * kTraceSlots + 10], 1ull);
-    atomicAdd(&g_trace[blockIdx.x * kTraceSlots + 11], (unsigned long long)__popc(hm));
-#endif
+      for (int q = 0; q < kVec; q++) {
+        if (q * 32 + lane < wn) {
+          const float xs[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
 #pragma unroll
-    for (int q = 0; q < kVec; q++) {
-      if ((hm >> (4 * q)) & 15u) {
-        const float xs[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
-        const int base_idx = a0 + 4 * (g0 + q * kThreads);
-#pragma unroll
-        for (int e = 0; e < 4; e++)
-          if (xs[e] == tf && composite(key_of(xs[e]), (uint32_t)(base_idx + e)) < tau)
-            hm &= ~(1u << (4 * q + e));
-      }
-    }
-    const int lane = tid & 31;
-    const int nh = __popc(hm);
-    int incl = nh;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += t;
-    }
-    const int wtotal = __shfl_sync(0xffffffffu, incl, 31);
-    if (wtotal == 0) return;
-    uint32_t wbase = 0;
-    if (lane == 31) wbase = atomicAdd(&sh->count, (uint32_t)wtotal);
-    wbase = __shfl_sync(0xffffffffu, wbase, 31);
-    uint32_t slot = wbase + (uint32_t)(incl - nh);
-#pragma unroll
-    for (int q = 0; q < kVec; q++) {
-      const uint32_t gb = (hm >> (4 * q)) & 15u;
-      if (gb) {
-        const float xs[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
-        const int base_idx = a0 + 4 * (g0 + q * kThreads);
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          if ((gb >> e) & 1u) {
-            if (slot < (uint32_t)kCandCap)
-              cand[slot] = composite(key_of(xs[e]), (uint32_t)(base_idx + e));
-            else
-              sh->overflow = 1u;
-            slot++;
+          for (int e = 0; e < 4; e++) {
+            const uint64_t c = composite(key_of(xs[e]), (uint32_t)(gbase + 4 * (q * 32 + lane) + e));
+            if (c > t1) {
+              t2 = t1;
+              t1 = c;
+            } else if (c > t2) {
+              t2 = c;
+            }
           }
         }
       }
     }
-  };
-
-  // ---- one pass: online max / sum-exp and the threshold filter ----
-  // Iteration it: thread t reads groups it*kIterGroups + q*kThreads + t (q < kVec), four
-  // independent 16-byte streaming loads in flight per thread.
-  const float4 kPast = make_float4(-3.40282347e38f, -3.40282347e38f, -3.40282347e38f,
-                                   -3.40282347e38f);
-  // Register double buffering: iteration it+1's loads are in flight while it is used.
-  float4 v[kVec];
+    // ns: logits in the sample; nw: warps that read any; rr: sample rank wanted.
+    int ns = 0, nw = 0;
+    for (int w = 0; w < kWarps; w++) {
+      const int b0 = min(w * seg, ngroups);
+      const int gw = min(kWarpIter, min(b0 + seg, ngroups) - b0);
+      ns += 4 * gw;
+      nw += gw > 0 ? 1 : 0;
+    }
+    const float mu = (float)k * (float)ns / (float)max(slice_len, 1);
+    const int rr = (int)ceilf(mu + 3.f * sqrtf(mu) + 4.f);
+    // Each warp sorts its 64 top-two slots and offers its j-th largest (j = rr / nw
+    // rounded up); the smallest offer has at least j logits of every offering warp at
+    // or above it, so about rr of the sample.
+    const int j = nw > 0 ? (rr + nw - 1) / nw : 65;
+    warp_sort64_desc(t1, t2);
+    const uint64_t jth = __shfl_sync(0xffffffffu, ((j - 1) & 1) ? t2 : t1, ((j - 1) >> 1) & 31);
+    if (lane == 0) sh->samp[warp] = (j <= 2 * min(32, wn)) ? jth : ~0ull;
+    __syncthreads();
+    uint64_t thr = ~0ull;
 #pragma unroll
-  for (int q = 0; q < kVec; q++) {
-    const int g = tid + q * kThreads;
-    v[q] = g < ngroups ? __ldcs(p4 + g) : kPast;
+    for (int w = 0; w < kWarps; w++) thr = min(thr, (uint64_t)sh->samp[w]);
+    if (rr <= 256 && j <= 64 && thr != ~0ull && (thr >> 32) != 0ull) {
+      tau = thr & 0xffffffff00000000ull;
+      tf = float_of_key((uint32_t)(thr >> 32));
+    }
+    if (warp == 0)
+      insert_candidate(re >= 0 && composite(key_of(rx), (uint32_t)re) >= tau,
+                       composite(key_of(rx), (uint32_t)max(re, 0)), cand, &sh->count,
+                       &sh->overflow);
+    if (wit > 0) filter_iter(v, 0, im0);
   }
-  // The next iteration's groups go to this thread's own shared-memory slots by cp.async
-  // (one commit group an iteration), so they stay in flight while this one is worked on.
-  auto prefetch = [&](int itn) {
+  TRACE(8);
+
+  // ---- the rest of each warp's segment: no block barrier until the end ----
+  for (int it = 1; it < wit; it++) {
 #pragma unroll
-    for (int q = 0; q < kVec; q++) {
-      const int g = itn * kIterGroups + tid + q * kThreads;
-      if (itn < niters && g < ngroups) cp_async16(stage + q * kThreads + tid, p4 + g);
-    }
-    cp_async_commit();
-  };
-  prefetch(1);
-#ifdef TABBY_TRACE
-  long long tc_stats = 0, tc_filter = 0, tc_bar = 0, tc_end = 0, tc_t;
-#define TCLK(var) do { const long long _n = clock64(); var += _n - tc_t; tc_t = _n; } while (0)
-#else
-#define TCLK(var) do { } while (0)
-#endif
-  for (int it = 0; it < niters; it++) {
-#ifdef TABBY_TRACE
-    tc_t = clock64();
-#endif
-    const int g0 = it * kIterGroups + tid;
-    // Past-the-end groups hold -FLT_MAX: they never raise the max and add exp(-huge) = 0
-    // to the sum; the filter skips them by index.
-    float gm[kVec];
-#pragma unroll
-    for (int q = 0; q < kVec; q++) {
-      gm[q] = fmaxf(fmaxf(v[q].x, v[q].y), fmaxf(v[q].z, v[q].w));
-      const float lo4 = fminf(fminf(v[q].x, v[q].y), fminf(v[q].z, v[q].w));
-      if (g0 + q * kThreads < ngroups) mn = fminf(mn, lo4);
-    }
-#ifdef TABBY_KNOB_NOSTATS
-    if (0) {
-#else
-    const float im = fmaxf(fmaxf(gm[0], gm[1]), fmaxf(gm[2], gm[3]));
-    if (im > m) {
-#endif
-      s *= ex2_approx((m - im) * kLog2e);
-      m = im;
-      mL = m * kLog2e;
-      // fma(x, L, -rn(m*L)) differs from (x - m)*L by the rounding of m*L, at most
-      // 2^-20 for |m| <= 16: every term then carries a factor within 7e-7 of 1 (well
-      // inside the 1e-5 budget). Larger |m| uses the subtraction form.
-      small = fabsf(m) <= 16.f;
-    }
-#ifdef TABBY_KNOB_NOSTATS
-    if (0) {
-#else
-    if (small) {
-#endif
-#pragma unroll
-      for (int q = 0; q < kVec; q++)
-        s += (ex2_approx(fmaf(v[q].x, kLog2e, -mL)) + ex2_approx(fmaf(v[q].y, kLog2e, -mL))) +
-             (ex2_approx(fmaf(v[q].z, kLog2e, -mL)) + ex2_approx(fmaf(v[q].w, kLog2e, -mL)));
-    } else
-#ifndef TABBY_KNOB_NOSTATS
-    {
-#else
-    if (0) {
-#endif
-#pragma unroll
-      for (int q = 0; q < kVec; q++)
-        s += (ex2_approx((v[q].x - m) * kLog2e) + ex2_approx((v[q].y - m) * kLog2e)) +
-             (ex2_approx((v[q].z - m) * kLog2e) + ex2_approx((v[q].w - m) * kLog2e));
-    }
-    TCLK(tc_stats);
-#ifdef TABBY_KNOB_NOBOOT
-    if (0) {
-#else
-    if (it == 0 && k > 0) {
-#endif
-      // Bootstrap threshold from this first iteration (registers): the per-thread maxima of
-      // every 8th thread form a 64-value sample; the highest sample value with at least k
-      // logits of the iteration at or above it is a valid lower bound of the k-th largest.
-      float tmax = fmaxf(fmaxf(gm[0], gm[1]), fmaxf(gm[2], gm[3]));
-      if ((tid & 7) == 0) sh->samp[tid >> 3] = (uint64_t)key_of(tmax) << 32;
-      __syncthreads();
-      if (tid < 32) {
-        uint64_t s0 = sh->samp[2 * tid], s1 = sh->samp[2 * tid + 1];
-        warp_sort64_desc(s0, s1);
-        sh->samp[2 * tid] = s0;
-        sh->samp[2 * tid + 1] = s1;
-      }
-      __syncthreads();
-      for (int r = 0; r < 64; r = 2 * r + 1) {
-        const float t = float_of_key((uint32_t)(sh->samp[r] >> 32));
-        int c = 0;
-#pragma unroll
-        for (int q = 0; q < kVec; q++)
-          if (g0 + q * kThreads < ngroups)
-            c += (v[q].x >= t) + (v[q].y >= t) + (v[q].z >= t) + (v[q].w >= t);
-        c = __reduce_add_sync(0xffffffffu, c);
-        __syncthreads();
-        if ((tid & 31) == 0) sh->red_u[tid >> 5] = (uint32_t)c;
-        __syncthreads();
-        int total = 0;
-#pragma unroll
-        for (int w = 0; w < kWarps; w++) total += (int)sh->red_u[w];
-        if (total >= k) {
-          tf = t;
-          tau = sh->samp[r];  // key(t) << 32: every logit >= t has a composite >= it
-          break;
-        }
-      }
-      __syncthreads();
-    }
-    filter_iter(v, gm, g0);
-    TCLK(tc_filter);
-    __syncthreads();
-    TCLK(tc_bar);
-    // Move to the next iteration: this thread's slots hold its groups of iteration it+1.
-    cp_async_wait_all();
-#pragma unroll
-    for (int q = 0; q < kVec; q++) {
-      const int g = g0 + kIterGroups + q * kThreads;
-      v[q] = g < ngroups ? stage[q * kThreads + tid] : kPast;
-    }
-    prefetch(it + 2);  // reuses the slots just read (same thread, values already in registers)
-    if (sh->overflow) {
-#ifdef TABBY_TRACE
-      (void)0;
-#endif
-      // The buffer filled during this iteration (only before the threshold settles):
-      // drop the iteration's inserts and filter it again from L2 one float4 a thread at
-      // a time, compacting between the sub-steps.
-      __syncthreads();
-      if (tid == 0) {
-        sh->count = sh->snap;
-        sh->overflow = 0;
-      }
-      __syncthreads();
-      for (int q = 0; q < kVec; q++) {
-        if (sh->count > (uint32_t)(kCandCap - kThreads * 4)) compact();
-        const int g = g0 + q * kThreads;
-        const float4 w = g < ngroups ? __ldcg(p4 + g) : kPast;
-        filter_group(w, fmaxf(fmaxf(w.x, w.y), fmaxf(w.z, w.w)), g);
-        __syncthreads();
-      }
-    }
-    if (k > 0 && sh->count > (uint32_t)(kCandCap / 2)) compact();
-    if (tid == 0) sh->snap = sh->count;
-#ifndef TABBY_KNOB_ONEBAR
-    __syncthreads();
-#endif
-    TCLK(tc_end);
-    if (it == 0) TRACE(8);
+    for (int q = 0; q < kVec; q++) v[q] = nx[q];
+    if (it + 1 < wit) load_iter(nx, it + 1);
+    const float im = stats_iter(v, it);
+    if (k > 0) filter_iter(v, it, im);
   }
   TRACE(2);
-#ifdef TABBY_TRACE
-  TRACE_VAL(13, tc_stats);
-  TRACE_VAL(14, tc_filter);
-  TRACE_VAL(15, tc_bar);
-  TRACE_VAL(4, tc_end);
-#endif
-#ifdef TABBY_KNOB_NOEPI
-  if (s == 12345.f && tid == 0) a.out[row].id = (int)m;
-  return;
-#endif
+  __syncthreads();
+  TRACE_VAL(11, sh->count);
+
+  if (k > 0 && (sh->overflow != 0u || (int)sh->count < need)) {
+    // The estimate failed: filter the slice again from memory, block-synchronously,
+    // with every logit a candidate at first and compaction raising the threshold.
+    __syncthreads();
+    if (tid == 0) {
+      sh->count = 0;
+      sh->overflow = 0;
+    }
+    tau = 0;
+    tf = -__int_as_float(0x7f800000);
+    __syncthreads();
+    if (warp == 0)
+      insert_candidate(re >= 0, composite(key_of(rx), (uint32_t)max(re, 0)), cand, &sh->count,
+                       &sh->overflow);
+    for (int base = 0; base < ngroups; base += kThreads) {
+      __syncthreads();
+      if (sh->count > (uint32_t)(kCandCap - 4 * kThreads)) compact();
+      const int g = base + tid;
+      const float4 w = g < ngroups ? __ldcg(p4 + g) : kPast;
+      filter_group(w, max3f(w.x, w.y, fmaxf(w.z, w.w)), g);
+    }
+    __syncthreads();
+  }
+  TRACE(9);
   // NaN or +inf logits leave s or m non-finite; -inf and values at or below the
   // reference's -3.0e38 sentinel show in the running min.
   const bool bad = !(s == s) || !(m <= 3.40282347e38f) || !(mn > kNegSentinel) ||
@@ -1101,15 +1302,8 @@ __global__ void __launch_bounds__(kThreads, TABBY_MIN_BLOCKS) stream_kernel(Stre
   // ---- this slice's <= k best and its (max, sum-exp) partial ----
   // The slice's k best, sorted by (value desc, index asc): cut to at most 2048 that
   // include them, sort, keep the first min(k, cnt).
-  int cnt = (int)sh->count;
-  if (k > 0 && cnt > 2048) {
-    int kept;
-    const uint64_t thr = shrink_to(cand, cnt, k, 2048, hist, sh, &kept);
-    if (tid == 0 && a.nslices > 1) atomicMax(&a.row_tau[row], (unsigned long long)thr);
-    cnt = kept;
-  }
-  block_sort_desc_2k(cand, cnt);
-  cnt = min(cnt, k);
+  const int cnt = top_sorted(cand, (int)sh->count, k, hist, sh);
+  TRACE(10);
   float M, S;
   uint32_t flags;
   {
@@ -1218,13 +1412,7 @@ __global__ void __launch_bounds__(kThreads, TABBY_MIN_BLOCKS) stream_kernel(Stre
         total = kept;
       }
     }
-    if (k > 0 && total > 2048) {
-      int kept;
-      shrink_to(cand, total, k, 2048, hist, sh, &kept);
-      total = kept;
-    }
-    block_sort_desc_2k(cand, total);
-    kk = min(k, total);
+    kk = top_sorted(cand, total, k, hist, sh);
     if (tid == 0) {
       // Leave the row's counters clean for the next launch.
       a.row_count[row] = 0;
@@ -1238,6 +1426,48 @@ __global__ void __launch_bounds__(kThreads, TABBY_MIN_BLOCKS) stream_kernel(Stre
                           : (flags & kFlagBadParams) ? (uint32_t)TABBY_EINVAL
                           : (flags & kFlagTimeout)   ? (uint32_t)TABBY_ETIMEOUT
                                                      : (uint32_t)TABBY_OK;
+  if (k <= 64) {
+    // Small pools: warp 0 finishes the row alone, the other warps leave the SM.
+    if (warp != 0) return;
+    const uint64_t c0 = cand[2 * lane], c1 = cand[2 * lane + 1];
+    const int32_t id0 = (int32_t)~(uint32_t)c0, id1 = (int32_t)~(uint32_t)c1;
+    float x0 = float_of_key((uint32_t)(c0 >> 32)), x1 = float_of_key((uint32_t)(c1 >> 32));
+    if (2 * lane < kk && (uint32_t)(c0 >> 32) == 0x80000000u) x0 = rowp[id0];  // sign of a zero
+    if (2 * lane + 1 < kk && (uint32_t)(c1 >> 32) == 0x80000000u) x1 = rowp[id1];
+    const float max_logit = kk > 0 ? __shfl_sync(0xffffffffu, x0, 0) : row_max;
+    if (a.mode == kModeTopK || a.mode == kModeShard) {
+      float *blk = a.block + (int64_t)row * a.block_ld;
+      const int slots = a.mode == kModeShard ? TABBY_SHARD_TOP_K : k;
+      if (lane == 0) {
+        blk[0] = status == TABBY_OK ? max_logit : __int_as_float(0x7fc00000);
+        blk[1] = sum_exp;
+      }
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const int i = 2 * lane + e;
+        if (i < slots) {
+          const bool in = i < kk;
+          blk[2 + 2 * i] = in ? (e ? x1 : x0) : __int_as_float(0xff800000);  // -inf pad
+          blk[3 + 2 * i] = __uint_as_float(
+              in ? (uint32_t)((int64_t)(e ? id1 : id0) + a.index_offset) : 0xffffffffu);
+        }
+      }
+      TRACE(7);
+      return;
+    }
+    if (a.topk_ids) {
+      if (2 * lane < kk) a.topk_ids[(int64_t)row * a.topk_ld + 2 * lane] = id0;
+      if (2 * lane + 1 < kk) a.topk_ids[(int64_t)row * a.topk_ld + 2 * lane + 1] = id1;
+    }
+    if (a.topk_values) {
+      if (2 * lane < kk) a.topk_values[(int64_t)row * a.topk_ld + 2 * lane] = x0;
+      if (2 * lane + 1 < kk) a.topk_values[(int64_t)row * a.topk_ld + 2 * lane + 1] = x1;
+    }
+    finalize_warp(id0, id1, x0, x1, kk, max_logit, sum_exp, a.params[row], a.uniforms[row],
+                  reinterpret_cast<double *>(hist), &a.out[row], status);
+    TRACE(7);
+    return;
+  }
   // Unpack into (id, value) in the histogram space; once that is done the candidate
   // buffer holds the float64 finalize arrays.
   int32_t *ids = reinterpret_cast<int32_t *>(hist);
@@ -1375,8 +1605,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch a) {
 static int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
 static size_t stream_smem_bytes() {
-  return (size_t)kCandCap * 8 + (size_t)kBins * 4 + (size_t)kVec * kThreads * 16 +
-         sizeof(Shared) + 64;
+  return (size_t)kCandCap * 8 + (size_t)kBins * 4 + sizeof(Shared) + 64;
 }
 
 int32_t max_slices(int32_t vocab, int32_t cap) {
