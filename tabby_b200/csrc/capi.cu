@@ -27,7 +27,8 @@ struct tabby_sampler {
   int32_t max_rows;
   int32_t max_vocab;
   int32_t sms;
-  Scratch scratch;  // per-row / per-slice state of the row kernel
+  Scratch scratch;     // per-row state of the row pass, carved from scratch_mem
+  void *scratch_mem;
   cudaStream_t stream;  // used by the host-buffer entry points
   float *d_logits;
   tabby_sampling_params *d_params;
@@ -106,7 +107,6 @@ cudaError_t plan_and_launch(const tabby_sampler *s, const RowLaunch &l, cudaStre
     RowGeometry geo;
     cudaError_t err = tabby::plan_rows(s->sms, b.rows, b.vocab, s->cap, &geo);
     if (err != cudaSuccess) return err;
-    if (geo.nslices > s->scratch.max_slices) return cudaErrorInvalidValue;
     err = tabby::launch_rows(b, geo, s->scratch, stream);
     if (err != cudaSuccess) return err;
   }
@@ -169,14 +169,9 @@ int tabby_sampler_create(const tabby_sampler_config *config, tabby_sampler **out
   s->max_rows = c.max_rows;
   s->max_vocab = c.max_vocab;
   s->sms = prop.multiProcessorCount;
-  const int32_t cand_ld = std::max(c.max_top_k, (int32_t)TABBY_SHARD_TOP_K);
-  const int32_t nsl = tabby::max_slices(c.max_vocab, c.max_top_k);
   const size_t nlog = (size_t)c.max_rows * (size_t)c.max_vocab;
-  const size_t nsr = (size_t)c.max_rows * (size_t)nsl;
-  Scratch &scr = s->scratch;
-  scr.cand_ld = cand_ld;
-  scr.max_rows = c.max_rows;
-  scr.max_slices = nsl;
+  // Row state for at most 1024 rows a launch; larger batches run in several launches.
+  const int32_t scratch_rows = std::min(c.max_rows, (int32_t)1024);
   if ((err = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking)) != cudaSuccess ||
       (err = cudaMalloc(&s->d_logits, nlog * sizeof(float))) != cudaSuccess ||
       (err = cudaMalloc(&s->d_params, (size_t)c.max_rows * sizeof(tabby_sampling_params))) !=
@@ -188,22 +183,13 @@ int tabby_sampler_create(const tabby_sampler_config *config, tabby_sampler **out
           cudaSuccess ||
       (err = cudaMalloc(&s->d_values, (size_t)c.max_rows * c.max_top_k * sizeof(float))) !=
           cudaSuccess ||
-      (err = cudaMalloc(&scr.row_count, (size_t)c.max_rows * sizeof(uint32_t))) != cudaSuccess ||
-      (err = cudaMalloc(&scr.row_tau, (size_t)c.max_rows * sizeof(unsigned long long))) !=
-          cudaSuccess ||
-      (err = cudaMalloc(&scr.slice_stats, nsr * sizeof(float2))) != cudaSuccess ||
-      (err = cudaMalloc(&scr.slice_meta, nsr * sizeof(uint2))) != cudaSuccess ||
-      (err = cudaMalloc(&scr.slice_cand, nsr * cand_ld * sizeof(unsigned long long))) !=
-          cudaSuccess ||
-      (err = cudaMemset(scr.row_count, 0, (size_t)c.max_rows * sizeof(uint32_t))) !=
-          cudaSuccess ||
-      (err = cudaMemset(scr.row_tau, 0, (size_t)c.max_rows * sizeof(unsigned long long))) !=
-          cudaSuccess ||
+      (err = cudaMalloc(&s->scratch_mem, Scratch::bytes(scratch_rows))) != cudaSuccess ||
       (err = cudaDeviceSynchronize()) != cudaSuccess) {
     tabby_sampler_destroy(s);
     cudaGetLastError();
     return fail(TABBY_ENOMEM, "allocation of sampler buffers failed: %s", cudaGetErrorString(err));
   }
+  s->scratch = Scratch::carve(s->scratch_mem, scratch_rows);
   *out = s;
   return TABBY_OK;
 }
@@ -217,11 +203,7 @@ int tabby_sampler_destroy(tabby_sampler *s) {
   if (s->d_out) cudaFree(s->d_out);
   if (s->d_ids) cudaFree(s->d_ids);
   if (s->d_values) cudaFree(s->d_values);
-  if (s->scratch.row_count) cudaFree(s->scratch.row_count);
-  if (s->scratch.row_tau) cudaFree(s->scratch.row_tau);
-  if (s->scratch.slice_stats) cudaFree(s->scratch.slice_stats);
-  if (s->scratch.slice_meta) cudaFree(s->scratch.slice_meta);
-  if (s->scratch.slice_cand) cudaFree(s->scratch.slice_cand);
+  if (s->scratch_mem) cudaFree(s->scratch_mem);
   if (s->stream) cudaStreamDestroy(s->stream);
   delete s;
   return TABBY_OK;
@@ -255,8 +237,6 @@ int tabby_sample_rows_async(tabby_sampler *s, const float *d_logits, int64_t row
   l.topk_values = d_topk_values;
   l.topk_ld = topk_ld;
   cudaError_t err = plan_and_launch(s, l, (cudaStream_t)stream);
-  if (err == cudaErrorInvalidValue && vocab > 0)
-    return fail(TABBY_EINVAL, "vocab %d needs more slices than the handle's scratch holds", vocab);
   if (err != cudaSuccess) return cuda_fail(err, "row_kernel launch");
   return TABBY_OK;
 }
@@ -349,8 +329,6 @@ int tabby_topk_rows_async(tabby_sampler *s, const float *d_logits, int64_t row_s
   l.block = d_block;
   l.block_ld = block_ld;
   cudaError_t err = plan_and_launch(s, l, (cudaStream_t)stream);
-  if (err == cudaErrorInvalidValue)
-    return fail(TABBY_EINVAL, "vocab %d needs more slices than the handle's scratch holds", vocab);
   if (err != cudaSuccess) return cuda_fail(err, "row_kernel launch");
   return TABBY_OK;
 }
@@ -380,9 +358,6 @@ int tabby_shard_local_async(tabby_sampler *s, const float *d_logits, int64_t row
   l.block = d_block;
   l.block_ld = block_ld;
   cudaError_t err = plan_and_launch(s, l, (cudaStream_t)stream);
-  if (err == cudaErrorInvalidValue)
-    return fail(TABBY_EINVAL, "shard vocab %d needs more slices than the handle's scratch holds",
-                shard_vocab);
   if (err != cudaSuccess) return cuda_fail(err, "row_kernel launch");
   return TABBY_OK;
 }

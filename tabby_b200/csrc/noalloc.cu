@@ -7,9 +7,9 @@
 // keeps the kernel's global scratch (per-row counters and per-slice candidate lists) in
 // a file-scope device array instead of a handle's cudaMalloc'd buffers.
 //
-// Limits: max_top_k <= TABBY_NOALLOC_MAX_TOP_K (256); rows are processed in batches of
-// at most kNoAllocRows whenever a row is split across CTAs. The array lives on every GPU
-// that loads this library until the process exits.
+// Limits: max_top_k <= TABBY_NOALLOC_MAX_TOP_K (256); rows are processed in launches of
+// at most kNoAllocRows. The array lives on every GPU that loads this library until the
+// process exits.
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -24,22 +24,8 @@
 namespace tabby {
 namespace {
 
-constexpr int kNoAllocRows = 32;     // rows per launch when rows are split into slices
-constexpr int kNoAllocSlices = 32;   // the row kernel never cuts a row into more
-constexpr int kNoAllocCandLd = TABBY_NOALLOC_MAX_TOP_K;
-
-// Byte layout of the scratch array.
-constexpr size_t kOffCount = 0;
-constexpr size_t kOffTau = 256;
-constexpr size_t kOffStats = kOffTau + 8ull * kNoAllocRows;
-constexpr size_t kOffMeta = kOffStats + 8ull * kNoAllocRows * kNoAllocSlices;
-constexpr size_t kOffCand = kOffMeta + 8ull * kNoAllocRows * kNoAllocSlices;
-constexpr size_t kScratchBytes =
-    kOffCand + 8ull * kNoAllocRows * kNoAllocSlices * kNoAllocCandLd;  // ~2.03 MB
-
-static_assert(kOffTau >= 4 * kNoAllocRows, "row counters overlap");
-static_assert(kOffStats % 256 == 0 && kOffMeta % 256 == 0 && kOffCand % 256 == 0,
-              "scratch sections must stay 256-byte aligned");
+constexpr int kNoAllocRows = 32;  // rows a launch; larger batches run in several launches
+constexpr size_t kScratchBytes = Scratch::layout_bytes(kNoAllocRows);  // ~2.1 MB
 
 // The scratch itself. In host code this name is only a stand-in for the symbol; its
 // device address comes from cudaGetSymbolAddress below.
@@ -88,19 +74,6 @@ int setup_current_device(DeviceState **out) {
   return TABBY_OK;
 }
 
-Scratch scratch_view(unsigned char *base) {
-  Scratch s;
-  s.row_count = reinterpret_cast<uint32_t *>(base + kOffCount);
-  s.row_tau = reinterpret_cast<unsigned long long *>(base + kOffTau);
-  s.slice_stats = reinterpret_cast<float2 *>(base + kOffStats);
-  s.slice_meta = reinterpret_cast<uint2 *>(base + kOffMeta);
-  s.slice_cand = reinterpret_cast<unsigned long long *>(base + kOffCand);
-  s.cand_ld = kNoAllocCandLd;
-  s.max_rows = kNoAllocRows;
-  s.max_slices = kNoAllocSlices;
-  return s;
-}
-
 }  // namespace
 }  // namespace tabby
 
@@ -130,7 +103,7 @@ extern "C" int tabby_sample_rows_noalloc(const float *d_logits, int64_t row_stri
   DeviceState *st = nullptr;
   int rc = setup_current_device(&st);
   if (rc) return rc;
-  const Scratch scr = scratch_view(st->scratch);
+  const Scratch scr = Scratch::carve(st->scratch, kNoAllocRows);
   cudaStream_t q = (cudaStream_t)stream;
 
   RowLaunch l;
@@ -146,17 +119,12 @@ extern "C" int tabby_sample_rows_noalloc(const float *d_logits, int64_t row_stri
   l.topk_values = d_topk_values;
   l.topk_ld = topk_ld;
 
-  // A previous call that failed part-way could leave row counters set: clear them (no
-  // allocation; a memset of the counter section on the caller's stream).
-  cudaError_t err = cudaMemsetAsync(scr.row_count, 0, kOffStats, q);
-  if (err != cudaSuccess) return fail(TABBY_ECUDA, "cudaMemsetAsync: %s", cudaGetErrorString(err));
-
-  RowGeometry whole;
-  plan_rows(st->sms, rows, vocab, max_top_k, &whole);
-  const int32_t batch = whole.nslices == 1 ? rows : kNoAllocRows;
-  for (int32_t r0 = 0; r0 < rows; r0 += batch) {
+  // The row pass resets the counters of the rows it plans (plan_kernel), so no clearing
+  // is needed here.
+  cudaError_t err = cudaSuccess;
+  for (int32_t r0 = 0; r0 < rows; r0 += kNoAllocRows) {
     RowLaunch b = l;
-    b.rows = std::min(rows - r0, batch);
+    b.rows = std::min(rows - r0, (int32_t)kNoAllocRows);
     b.logits = d_logits + (int64_t)r0 * row_stride;
     b.params = d_params + r0;
     b.uniforms = d_uniforms + r0;
@@ -165,9 +133,6 @@ extern "C" int tabby_sample_rows_noalloc(const float *d_logits, int64_t row_stri
     if (b.topk_values) b.topk_values = d_topk_values + (int64_t)r0 * topk_ld;
     RowGeometry geo;
     plan_rows(st->sms, b.rows, vocab, max_top_k, &geo);
-    if (geo.nslices > 1 && (b.rows > kNoAllocRows || geo.nslices > kNoAllocSlices))
-      return fail(TABBY_EINVAL, "batch of %d rows x %d slices exceeds the scratch array",
-                  b.rows, geo.nslices);
     err = launch_rows(b, geo, scr, q);
     if (err != cudaSuccess)
       return fail(TABBY_ECUDA, "row kernel launch: %s", cudaGetErrorString(err));

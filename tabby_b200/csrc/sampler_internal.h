@@ -47,29 +47,68 @@ struct MergeLaunch {
   int32_t topk_ld = 0;
 };
 
-// Geometry of one stream_kernel launch: the row is cut into `nslices` slices of
-// `slice` logits, one CTA each.
+// Geometry of one row pass: rows are cut into `nch` chunks of `chunk` logits; `grid`
+// persistent CTAs work through the rows * nch (row, chunk) units.
 struct RowGeometry {
-  int32_t slice = 0;        // logits per CTA (multiple of 4)
-  int32_t nslices = 0;      // CTAs per row
-  int32_t data_floats = 0;  // shared-memory staging region, floats
+  int32_t chunk = 0;  // logits a unit (multiple of 4)
+  int32_t nch = 0;    // units a row
+  int32_t grid = 0;   // CTAs of the row kernel
   size_t smem_bytes = 0;
 };
 
-// Global scratch of the row kernel, owned by the sampler handle. Row counters and
-// thresholds must be zero before a launch; the kernel leaves them zero again.
+constexpr int32_t kScratchCandidates = 8192;  // candidates a row may collect (kCandCap)
+constexpr int32_t kScratchChunks = 32;        // chunks a row may have (kMaxChunks)
+constexpr int32_t kScratchWarps = 16;         // warps a CTA has
+
+// Global scratch of the row pass for up to max_rows rows, carved from one device
+// allocation (every section 256-byte aligned). plan_kernel resets the counters of the
+// rows it plans, so no clearing is needed between launches.
 struct Scratch {
-  uint32_t *row_count = nullptr;             // [max_rows] slices finished
-  unsigned long long *row_tau = nullptr;     // [max_rows] exact lower bound of the k-th
-  float2 *slice_stats = nullptr;             // [max_rows * max_slices] (max, sum-exp)
-  uint2 *slice_meta = nullptr;               // [max_rows * max_slices] (count, flags)
-  unsigned long long *slice_cand = nullptr;  // [max_rows * max_slices * cand_ld]
-  int32_t cand_ld = 0;                       // candidates a slice may write (>= k)
+  uint32_t *sched = nullptr;                 // [1] unit counter
+  uint32_t *row_done = nullptr;              // [max_rows] chunks finished
+  uint32_t *chunk_cnt = nullptr;             // [max_rows][kScratchChunks] chunk candidates
+  uint32_t *row_flags = nullptr;             // [max_rows] bad input / overflow
+  float *row_tf = nullptr;                   // [max_rows] estimated threshold
+  int32_t *row_k = nullptr;                  // [max_rows] pool size
+  int32_t *order = nullptr;                  // [max_rows] processing order
+  float2 *warp_stats = nullptr;              // [max_rows][kScratchChunks][kScratchWarps]
+  unsigned long long *row_cand = nullptr;    // [max_rows][kScratchCandidates]
   int32_t max_rows = 0;
-  int32_t max_slices = 0;
+
+  static constexpr size_t section(size_t bytes) { return (bytes + 255) / 256 * 256; }
+  static constexpr size_t layout_bytes(int32_t rows) {
+    return section(4) + 5 * section(4 * (size_t)rows) +
+           section(4 * (size_t)rows * kScratchChunks) +
+           section(8 * (size_t)rows * kScratchChunks * kScratchWarps) +
+           section(8 * (size_t)rows * kScratchCandidates);
+  }
+  static size_t bytes(int32_t rows) { return layout_bytes(rows); }
+  static Scratch carve(void *base, int32_t rows) {
+    Scratch s;
+    unsigned char *p = static_cast<unsigned char *>(base);
+    const size_t r = (size_t)rows;
+    s.sched = reinterpret_cast<uint32_t *>(p);
+    p += section(4);
+    s.row_done = reinterpret_cast<uint32_t *>(p);
+    p += section(4 * r);
+    s.chunk_cnt = reinterpret_cast<uint32_t *>(p);
+    p += section(4 * r * kScratchChunks);
+    s.row_flags = reinterpret_cast<uint32_t *>(p);
+    p += section(4 * r);
+    s.row_tf = reinterpret_cast<float *>(p);
+    p += section(4 * r);
+    s.row_k = reinterpret_cast<int32_t *>(p);
+    p += section(4 * r);
+    s.order = reinterpret_cast<int32_t *>(p);
+    p += section(4 * r);
+    s.warp_stats = reinterpret_cast<float2 *>(p);
+    p += section(8 * r * kScratchChunks * kScratchWarps);
+    s.row_cand = reinterpret_cast<unsigned long long *>(p);
+    s.max_rows = rows;
+    return s;
+  }
 };
 
-int32_t max_slices(int32_t vocab, int32_t cap);
 cudaError_t plan_rows(int32_t sms, int32_t rows, int32_t vocab, int32_t cap, RowGeometry *geo);
 cudaError_t launch_rows(const RowLaunch &a, const RowGeometry &geo, const Scratch &scr,
                         cudaStream_t stream);

@@ -5,20 +5,21 @@
 // topk_partial + topk_select, i.e. k+4 passes over the row. Here every logit is read
 // from HBM once, in one streaming pass:
 //
-//   stream_kernel  one CTA per (row, slice); a slice is the whole row when the batch
-//                  fills the GPU. Every thread streams its own float4 groups straight
-//                  into registers (four 16-byte loads in flight a thread, 8K logits an
-//                  iteration per CTA, one barrier an iteration): online max and
-//                  sum(exp(x - max)) per thread, and a filter that keeps only logits
-//                  whose 64-bit composite (order-preserving key, inverted index) reaches
-//                  the current threshold. The threshold is an exact lower bound on the
-//                  row's k-th largest composite: a CTA whose candidate buffer fills
-//                  compacts it to its k largest by radix select and publishes that
-//                  bound in global memory, where the row's other slices pick it up.
-//                  Each slice writes its <= k candidates and its (max, sum-exp)
-//                  partial; the last CTA of the row to finish merges them, sorts the k
-//                  winners by (value desc, index asc) and runs sampleFromTopK in
-//                  float64 (finalize.cuh).
+//   plan_kernel    one CTA per row: resets the row's counters, fixes its pool size and
+//                  its place in the processing order, and estimates a filter threshold
+//                  from 2048 logits sampled evenly over the row.
+//   row_kernel     persistent, two 512-thread CTAs per SM taking (row, chunk) units from
+//                  a global counter. Each warp streams its part of the chunk straight
+//                  into registers (four 16-byte loads in flight a thread, the next
+//                  iteration's loads issued before this one is used), keeping online
+//                  max and sum(exp(x - max)) per thread and appending the logits at or
+//                  above the threshold, as 64-bit composites (order-preserving key,
+//                  inverted index), to a shared candidate buffer; no block barrier until
+//                  the chunk ends. Chunks append their candidates to the row's global
+//                  list; the unit that completes a row checks the estimate (falling
+//                  back to an exact re-filter), keeps the k best by radix select or a
+//                  warp-level top-64 tree, sorts them by (value desc, index asc) and
+//                  runs sampleFromTopK in float64 (finalize.cuh).
 //   merge_kernel   the vocab-sharded finish: merges all-gathered per-shard blocks.
 //
 // Selection works on the raw logits; temperature only enters the float64 finalize,
@@ -41,9 +42,12 @@ constexpr int kVec = 4;                   // float4 loads in flight per thread p
 constexpr int kWarpIter = 32 * kVec;      // float4 groups a warp reads per iteration (2 KB)
 constexpr int kCandCap = 8192;            // candidate buffer (composites) per CTA
 constexpr int kBins = 2048;               // radix digit: 11 bits
-constexpr int kMaxSlices = 32;            // slices of one row (one warp merges their stats)
-constexpr int kMinSlice = 8192;           // logits: below this a row is not split further
+constexpr int kMaxChunks = 32;            // chunks of one row (warp stats: chunks x 16 <= 512)
+constexpr int kMinChunk = 8192;           // logits: below this a row is not split further
 constexpr int kMergeThreads = 512;
+static_assert(kCandCap == kScratchCandidates && kMaxChunks == kScratchChunks &&
+                  kWarps == kScratchWarps && kMaxChunks * kWarps <= kThreads,
+              "scratch layout and kernel constants disagree");
 constexpr float kNegSentinel = -3.0e38f;  // NEG_INF of reduce_max.wgsl:13
 
 enum Flags : uint32_t { kFlagBadInput = 1u, kFlagTimeout = 2u, kFlagBadParams = 4u };
@@ -58,6 +62,24 @@ __device__ __forceinline__ unsigned long long globaltimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+constexpr int kUnitTraceCtas = 512, kUnitTraceUnits = 32;
+__device__ unsigned long long g_utrace[kUnitTraceCtas * kUnitTraceUnits * 4];
+__device__ unsigned long long g_ptrace[4096 * 2];
+__device__ unsigned long long g_ftrace[4096 * 8];
+__device__ unsigned long long g_pphase[4096 * 4];
+#define PPHASE(row, slot)                                                  \
+  do {                                                                     \
+    if (threadIdx.x == 0 && (row) < 4096) g_pphase[(row) * 4 + (slot)] = clock64(); \
+  } while (0)
+#define FTRACE(row, slot)                                                  \
+  do {                                                                     \
+    if (threadIdx.x == 0 && (row) < 4096) g_ftrace[(row) * 8 + (slot)] = clock64(); \
+  } while (0)
+#define UTRACE(j, slot, val)                                                          \
+  do {                                                                                \
+    if (threadIdx.x == 0 && blockIdx.x < kUnitTraceCtas && (j) < kUnitTraceUnits)     \
+      g_utrace[(blockIdx.x * kUnitTraceUnits + (j)) * 4 + (slot)] = (val);            \
+  } while (0)
 #define TRACE(ph)                                                  \
   do {                                                             \
     if (threadIdx.x == 0 && blockIdx.x < kTraceCtas)               \
@@ -69,6 +91,15 @@ __device__ __forceinline__ unsigned long long globaltimer() {
       g_trace[blockIdx.x * kTraceSlots + (ph)] = (unsigned long long)(v);   \
   } while (0)
 #else
+#define UTRACE(j, slot, val) \
+  do {                       \
+  } while (0)
+#define FTRACE(row, slot) \
+  do {                    \
+  } while (0)
+#define PPHASE(row, slot) \
+  do {                    \
+  } while (0)
 #define TRACE(ph) \
   do {            \
   } while (0)
@@ -187,7 +218,9 @@ struct Shared {
   uint32_t bucket;
   uint32_t above;
   uint32_t inb;
-  uint32_t last;  // this CTA merges the row
+  uint32_t last;  // this CTA finishes the row
+  uint32_t unit;  // the unit this CTA works on
+  uint32_t base;  // where the unit's candidates go in the row's list
   int32_t cut_claim;
   int32_t chosen_claim;
   int32_t fallback;
@@ -195,7 +228,9 @@ struct Shared {
   uint32_t overflow;  // an insert found the candidate buffer full
   uint64_t tau;  // accept composites >= tau
   float red_f[kWarps];
+  float red_f2[kWarps];
   uint32_t red_u[kWarps];
+  uint32_t red_u2[kWarps];
   double red_d[kWarps];
   float merge_max;
   float merge_sum;
@@ -208,18 +243,37 @@ struct Shared {
 // Block primitives (blockDim.x == 512)
 // ------------------------------------------------------------------------------------
 
-// Deterministic block sum of one double per thread (fixed shuffle tree, warps in order).
+// Warp-wide reductions of the 16 per-warp partials a block left in shared memory:
+// every lane reads one partial, so the result costs one load and one reduction
+// instead of a loop over the warps. Same value in every thread.
+__device__ __forceinline__ uint32_t partials_min_u32(const uint32_t *p) {
+  const int lane = threadIdx.x & 31;
+  return __reduce_min_sync(0xffffffffu, lane < kWarps ? p[lane] : 0xffffffffu);
+}
+__device__ __forceinline__ uint32_t partials_max_u32(const uint32_t *p) {
+  const int lane = threadIdx.x & 31;
+  return __reduce_max_sync(0xffffffffu, lane < kWarps ? p[lane] : 0u);
+}
+// Sum of the partials of warps above w (w = this thread's warp).
+__device__ __forceinline__ uint32_t partials_sum_above_u32(const uint32_t *p, int w) {
+  const int lane = threadIdx.x & 31;
+  return __reduce_add_sync(0xffffffffu, (lane > w && lane < kWarps) ? p[lane] : 0u);
+}
+
+
+// Deterministic block sum of one double per thread: a fixed shuffle tree in each warp,
+// then the same tree over the 16 warp sums (one per lane). Same value in every thread.
 __device__ double block_sum_f64(double v, Shared *sh) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = JS_ADD(v, __shfl_xor_sync(0xffffffffu, v, o));
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  const int nw = blockDim.x >> 5;
   __syncthreads();
   if (l == 0) sh->red_d[w] = v;
   __syncthreads();
-  double total = 0.0;
-  for (int i = 0; i < nw; i++) total = JS_ADD(total, sh->red_d[i]);
-  return total;  // same value in every thread
+  double total = l < kWarps ? sh->red_d[l] : 0.0;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) total = JS_ADD(total, __shfl_xor_sync(0xffffffffu, total, o));
+  return total;
 }
 
 // Exclusive block scan of one double per thread in thread order.
@@ -234,8 +288,10 @@ __device__ double block_exclusive_scan_f64(double v, Shared *sh) {
   __syncthreads();
   if (l == 31) sh->red_d[w] = inc;
   __syncthreads();
-  double before = 0.0;
-  for (int i = 0; i < w; i++) before = JS_ADD(before, sh->red_d[i]);
+  // Sum of the warps before this one, one warp total a lane.
+  double before = l < w ? sh->red_d[l] : 0.0;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) before = JS_ADD(before, __shfl_xor_sync(0xffffffffu, before, o));
   return JS_ADD(before, JS_SUB(inc, v));
 }
 
@@ -260,8 +316,7 @@ __device__ void find_bucket(const uint32_t *hist, uint32_t R, Shared *sh) {
   __syncthreads();
   if (lane == 0) sh->red_u[w] = inc;
   __syncthreads();
-  uint32_t above = inc - mine;
-  for (int i = w + 1; i < kWarps; i++) above += sh->red_u[i];
+  uint32_t above = inc - mine + partials_sum_above_u32(sh->red_u, w);
   if (above < R && above + mine >= R) {
     int b = 3;
     for (; b > 0; b--) {
@@ -493,10 +548,7 @@ __device__ __noinline__ int block_count_ge(const uint64_t *cand, int n, uint64_t
   __syncthreads();
   if ((threadIdx.x & 31) == 0) sh->red_u[threadIdx.x >> 5] = (uint32_t)c;
   __syncthreads();
-  int total = 0;
-#pragma unroll
-  for (int w = 0; w < kWarps; w++) total += (int)sh->red_u[w];
-  return total;
+  return (int)__reduce_add_sync(0xffffffffu, (threadIdx.x & 31) < kWarps ? sh->red_u[threadIdx.x & 31] : 0u);
 }
 
 // Keeps the composites >= t of cand[0, n) at the front, in order, in place: chunk by chunk
@@ -907,20 +959,137 @@ __device__ __noinline__ void finalize_warp(int32_t id0, int32_t id1, float x0, f
   }
 }
 
+// Sorts cand[0, n) descending into out[0, min(n, R)) for n <= kThreads by rank: each
+// thread counts the composites above its own (broadcast reads of the whole list).
+// Block-uniform call; out must not overlap cand[0, n).
+__device__ __forceinline__ void rank_sort_small(const uint64_t *cand, int n, int R, uint64_t *out) {
+  const int tid = threadIdx.x;
+  if (tid < n) {
+    const uint64_t c = cand[tid];
+    int r = 0;
+    for (int q = 0; q < n; q++) r += cand[q] > c ? 1 : 0;
+    if (r < R) out[r] = c;
+  }
+  __syncthreads();
+}
+
+// Exact top-R (R = min(k, n)) with its order. Candidates are binned on their key
+// relative to the smallest one (2048 bins, the shift set by the key range); bins are
+// counted and turned into offsets in descending order; the bins down to the one that
+// holds the R-th are scattered into a grouped list behind the input; every element's
+// position is its bin's offset plus the number of larger composites in its bin. Writes
+// the R largest of cand[0, n), sorted descending, to cand[0, R) and returns R; returns
+// -1 without changing cand when the grouped list does not fit behind the input (cand
+// holds `capacity` slots) or a bin
+// holds more than 512 elements (long runs of equal logits), for the caller's fallback.
+// Block-uniform call.
+__device__ __noinline__ int bin_rank_topk(uint64_t *cand, int n, int k, int capacity,
+                                          uint32_t *hist, Shared *sh) {
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int R = min(k, n);
+  // Key range.
+  uint32_t kmin = 0xffffffffu, kmax = 0u;
+  for (int i = tid; i < n; i += kThreads) {
+    const uint32_t key = (uint32_t)(cand[i] >> 32);
+    kmin = min(kmin, key);
+    kmax = max(kmax, key);
+  }
+  kmin = __reduce_min_sync(0xffffffffu, kmin);
+  kmax = __reduce_max_sync(0xffffffffu, kmax);
+  if (lane == 0) {
+    sh->red_u[w] = kmin;
+    sh->red_u2[w] = kmax;
+  }
+  for (int i = tid; i < kBins; i += kThreads) hist[i] = 0;
+  __syncthreads();
+  kmin = partials_min_u32(sh->red_u);
+  kmax = partials_max_u32(sh->red_u2);
+  const uint32_t range = kmax - kmin;
+  const int shift = max(0, 32 - __clz((int)range) - 11);  // (range >> shift) < 2048
+  for (int i = tid; i < n; i += kThreads)
+    atomicAdd(&hist[((uint32_t)(cand[i] >> 32) - kmin) >> shift], 1u);
+  __syncthreads();
+  // In place: hist[b] = elements in bins above b (exclusive suffix sum, high bins first).
+  uint32_t h[4], mine = 0, big = 0;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    h[j] = hist[4 * tid + j];
+    mine += h[j];
+    big = max(big, h[j]);
+  }
+  uint32_t inc = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_down_sync(0xffffffffu, inc, o);
+    if (lane + o < 32) inc += t;
+  }
+  big = __reduce_max_sync(0xffffffffu, big);
+  __syncthreads();  // everyone has read hist and the red arrays
+  if (lane == 0) {
+    sh->red_u[w] = inc;
+    sh->red_u2[w] = big;
+  }
+  __syncthreads();
+  big = partials_max_u32(sh->red_u2);
+  if (big > 512u) return -1;  // block-uniform
+  uint32_t off = inc - mine + partials_sum_above_u32(sh->red_u, w);
+  for (int j = 3; j >= 0; j--) {
+    if (off < (uint32_t)R && off + h[j] >= (uint32_t)R) {
+      sh->bucket = 4 * tid + j;
+      sh->above = off;
+      sh->inb = h[j];
+    }
+    hist[4 * tid + j] = off;
+    off += h[j];
+  }
+  __syncthreads();
+  const uint32_t kb = sh->bucket;
+  const int kept = (int)(sh->above + sh->inb);  // elements in bins >= kb
+  if (n + kept > capacity) return -1;  // block-uniform
+  uint64_t *g = cand + n;
+  for (int i = tid; i < n; i += kThreads) {
+    const uint64_t c = cand[i];
+    const uint32_t b = ((uint32_t)(c >> 32) - kmin) >> shift;
+    if (b >= kb) g[atomicAdd(&hist[b], 1u)] = c;
+  }
+  __syncthreads();
+  // Now hist[b] is the end of bin b and hist[b + 1] its start.
+  for (int p = tid; p < kept; p += kThreads) {
+    const uint64_t c = g[p];
+    const uint32_t b = ((uint32_t)(c >> 32) - kmin) >> shift;
+    const int s = b + 1 < (uint32_t)kBins ? (int)hist[b + 1] : 0;
+    const int e = (int)hist[b];
+    int r = 0;
+    for (int q = s; q < e; q++) r += g[q] > c ? 1 : 0;
+    if (s + r < R) cand[s + r] = c;
+  }
+  __syncthreads();
+  return R;
+}
+
 // The min(k, n) largest of cand[0, n) (k <= 1024), sorted descending, at cand[0, ...);
-// returns how many. Block-uniform call. Pools of at most 64 go through the per-warp
-// top-64 tree; larger ones through the exact radix select, then a sort of the k kept.
+// returns how many. Block-uniform call. Lists of at most 512 are ranked directly,
+// longer ones through the binned ranking; long runs of equal logits fall back to the
+// per-warp top-64 tree (pools up to 64) or the exact radix select and a sort.
 __device__ __forceinline__ int top_sorted(uint64_t *cand, int n, int k, uint32_t *hist,
                                           Shared *sh) {
   if (k <= 0 || n <= 0) {
     __syncthreads();
     return 0;
   }
+  if (n <= kThreads && 2 * n <= kCandCap) {
+    // Small lists: rank every element against all the others, then move the result
+    // to the front.
+    rank_sort_small(cand, n, min(k, n), cand + n);
+    const int R = min(k, n);
+    for (int i = threadIdx.x; i < R; i += kThreads) cand[i] = cand[n + i];
+    __syncthreads();
+    return R;
+  }
+  const int r = bin_rank_topk(cand, n, k, kCandCap, hist, sh);
+  if (r >= 0) return r;
   if (k <= 64) {
-    if (n <= 64)
-      block_sort_desc(cand, n);
-    else
-      top64_sorted(cand, n, reinterpret_cast<uint64_t *>(hist));
+    top64_sorted(cand, n, reinterpret_cast<uint64_t *>(hist));
     return min(k, n);
   }
   if (n > k) {
@@ -932,12 +1101,28 @@ __device__ __forceinline__ int top_sorted(uint64_t *cand, int n, int k, uint32_t
 }
 
 // ------------------------------------------------------------------------------------
-// The streaming kernel.
+// The row pass: plan_kernel, then row_kernel.
+//
+// plan_kernel (one CTA a row) resets the row's counters, fixes its pool size k and its
+// place in the processing order (rows with pools above 64 first, so that the rows whose
+// finish is cheap come last), and estimates a threshold from a sample of 512 float4
+// groups spread over the row: a logit with about rr sample logits at or above it, rr
+// chosen so that the row holds at least k logits at or above it with near certainty
+// (rr = mu + 3 sqrt(mu) + 4, mu the expected sample count above the row's k-th largest).
+//
+// row_kernel is persistent: every CTA takes (row, chunk) units from a global counter in
+// that order, so fast CTAs take more. A unit streams its chunk once (online max /
+// sum-exp, and the threshold filter into the shared candidate buffer), appends its
+// candidates to the row's global list and its per-warp statistics to the row's table;
+// the unit that completes a row finishes it: it checks the estimate (at least min(k, V)
+// candidates and no overflow, else the row is filtered again exactly), keeps the k
+// best, sorts them and runs sampleFromTopK. Rows finish while other rows still stream.
 // ------------------------------------------------------------------------------------
-struct StreamArgs {
+struct PassArgs {
   const float *logits;
   int64_t row_stride;
-  int32_t rows, vocab, slice, nslices;
+  int32_t rows, vocab;
+  int32_t nch, chunk;  // chunks a row, logits a chunk (a multiple of 4)
   int32_t mode, cap, fixed_k;
   int64_t index_offset;
   const tabby_sampling_params *params;
@@ -948,16 +1133,24 @@ struct StreamArgs {
   int32_t topk_ld;
   float *block;
   int32_t block_ld;
-  uint32_t *row_count;
-  unsigned long long *row_tau;
-  float2 *slice_stats;
-  uint2 *slice_meta;
-  unsigned long long *slice_cand;
-  int32_t cand_ld;
+  uint32_t *sched;       // unit counter
+  uint32_t *row_done;    // [rows] chunks finished
+  uint32_t *chunk_cnt;   // [rows][nch] candidates of each chunk
+  uint32_t *row_flags;   // [rows] kFlagBadInput | kRowOverflow
+  float *row_tf;         // [rows] threshold
+  int32_t *row_k;        // [rows] pool size
+  int32_t *order;        // [rows] processing order
+  float2 *warp_stats;    // [rows][nch][kWarps] (max, sum-exp)
+  unsigned long long *row_cand;  // [rows][kCandCap]: chunk c owns slots [c * cc, (c + 1) * cc)
 };
 
+// Candidate slots of the row's list each chunk owns.
+__device__ __forceinline__ int chunk_slots(const PassArgs &a) { return kCandCap / a.nch; }
+
+constexpr uint32_t kRowOverflow = 8u;  // the row's candidates did not fit: filter it again
+
 // Appends c to the candidate buffer when pred holds (warp-uniform call). Slots past
-// kCandCap are not written; the overflow flag tells the block to redo the iteration.
+// kCandCap are not written; the overflow flag records the loss.
 __device__ __forceinline__ void insert_candidate(bool pred, uint64_t c, uint64_t *cand,
                                                  uint32_t *count, uint32_t *overflow) {
   const uint32_t mask = __ballot_sync(0xffffffffu, pred);
@@ -976,458 +1169,260 @@ __device__ __forceinline__ void insert_candidate(bool pred, uint64_t c, uint64_t
   }
 }
 
-#ifndef TABBY_MIN_BLOCKS
-#define TABBY_MIN_BLOCKS 2
-#endif
-__global__ void __launch_bounds__(kThreads, TABBY_MIN_BLOCKS) stream_kernel(StreamArgs a) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  uint64_t *cand = reinterpret_cast<uint64_t *>(smem_raw);
-  uint32_t *hist = reinterpret_cast<uint32_t *>(cand + kCandCap);
-  Shared *sh = reinterpret_cast<Shared *>(hist + kBins);
-
-  const int tid = threadIdx.x;
-  const int row = blockIdx.x / a.nslices;
-  const int sl = blockIdx.x - row * a.nslices;
-  const float *rowp = a.logits + (int64_t)row * a.row_stride;
-  const int lo = sl * a.slice;
-  const int hi = min(lo + a.slice, a.vocab);
-  // [a0, a1) is the 16-byte aligned middle of the slice, read as float4; the ragged ends
-  // (fewer than 4 logits each) come in through scalar loads.
-  const int mis = (int)((reinterpret_cast<uintptr_t>(rowp + lo) >> 2) & 3);
-  int a0 = lo + ((4 - mis) & 3);
-  if (a0 > hi) a0 = hi;
-  const int a1 = a0 + ((max(hi - a0, 0)) & ~3);
-  const int ngroups = (a1 - a0) >> 2;  // float4 groups in the aligned middle
-  const float4 *p4 = reinterpret_cast<const float4 *>(rowp + a0);
-  TRACE(0);
-#ifdef TABBY_TRACE
-  {
-    uint32_t smid;
-    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-    TRACE_VAL(12, smid);
-  }
-#endif
-
-  if (tid == 0) {
-    sh->count = 0;
-    sh->flags = 0;
-    sh->overflow = 0;
-  }
-  // Pool size of this row.
-  int32_t k;
-  uint32_t pflags = 0;
+// Pool size of a row (inference.worker.ts:120-123 with the handle's cap in sample mode).
+__device__ __forceinline__ int32_t row_pool(const PassArgs &a, int row, uint32_t *pflags) {
   if (a.mode == kModeSample) {
     const tabby_sampling_params p = a.params[row];
-    k = pool_rule(p.temperature, p.top_k, a.cap);
-    if (isnan(p.temperature) || isnan(p.top_p)) pflags = kFlagBadParams;
-  } else {
-    k = a.fixed_k;
+    if (isnan(p.temperature) || isnan(p.top_p)) *pflags = kFlagBadParams;
+    return min(pool_rule(p.temperature, p.top_k, a.cap), a.vocab);
   }
-  k = min(k, a.vocab);
-  __syncthreads();
-  TRACE(1);
+  return min(a.fixed_k, a.vocab);
+}
 
-  // Per-thread online statistics: s = sum exp(x - m) as 2^((x - m) * log2(e)).
-  constexpr float kLog2e = 1.44269504088896341f;
-  float m = -3.40282347e38f, s = 0.f;
-  float mL = 0.f;      // rn(m * log2(e)) for the FFMA form of the exponent argument
-  bool small = false;  // |m| small enough for the FFMA form
-  float mn = 3.40282347e38f;  // running min: catches -inf and the -3e38 sentinel
-  uint64_t tau = 0;  // accept composites >= tau
-  float tf = -__int_as_float(0x7f800000);  // value of tau's key: a cheap superset filter
-  const int warp = tid >> 5, lane = tid & 31;
-  const int slice_len = hi - lo;
-  const int need = min(k, slice_len);  // candidates >= tau the slice must end with
+// First float4-aligned logit of [lo, hi) and the number of whole float4 groups after it.
+struct Span {
+  int a0, a1, ngroups;
+};
+__device__ __forceinline__ Span aligned_span(const float *rowp, int lo, int hi) {
+  const int mis = (int)((reinterpret_cast<uintptr_t>(rowp + lo) >> 2) & 3);
+  Span s;
+  s.a0 = min(lo + ((4 - mis) & 3), hi);
+  s.a1 = s.a0 + ((hi - s.a0) & ~3);
+  s.ngroups = (s.a1 - s.a0) >> 2;
+  return s;
+}
 
-  // Ragged ends: at most 3 logits before a0 and 3 after a1, one per thread of warp 0.
-  // Their statistics count now; they join the candidates once the threshold is known.
-  float rx = 0.f;
-  int re = -1;
-  if (tid < 8) {
-    const int e = tid < 4 ? lo + tid : a1 + (tid - 4);
-    if (tid < 4 ? (e < a0) : (e < hi)) {
-      rx = __ldg(rowp + e);
-      re = e;
-      m = rx;
-      mL = m * kLog2e;
-      small = fabsf(m) <= 16.f;
-      s = 1.f;
-      mn = rx;
+__global__ void __launch_bounds__(kThreads) plan_kernel(const __grid_constant__ PassArgs a) {
+  __shared__ uint64_t cand[4 * kThreads];  // 1024 sample slots and room to rank them
+  __shared__ uint32_t hist[kBins];
+  __shared__ Shared sh_s;
+  __shared__ int red[3][kWarps];
+  Shared *sh = &sh_s;
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float *rowp = a.logits + (int64_t)row * a.row_stride;
+  // The row kernel may start launching now; it waits for this grid's results.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  PPHASE(row, 0);
+  uint32_t pf = 0;
+#ifdef TABBY_TRACE
+  if (tid == 0 && row < 4096) g_ptrace[row * 2] = globaltimer();
+#endif
+  const int k = row_pool(a, row, &pf);
+  if (tid == 0) {
+    a.row_done[row] = 0;
+    a.row_flags[row] = 0;
+    if (row == 0) *a.sched = 0;
+  }
+  // Place in the order: rows with k > 64 first, each group in row order.
+  int large = 0, large_before = 0, small_before = 0;
+  for (int r = tid; r < a.rows; r += kThreads) {
+    uint32_t f = 0;
+    const int lg = row_pool(a, r, &f) > 64 ? 1 : 0;
+    large += lg;
+    if (r < row) {
+      large_before += lg;
+      small_before += 1 - lg;
     }
   }
-
-  // Warp segments: warp w streams the float4 groups [sg0, sg0 + wn) of the aligned
-  // middle, 128 groups (2 KB, four 512-byte coalesced loads) an iteration.
-  const int seg = (ngroups + kWarps - 1) / kWarps;
-  const int sg0 = min(warp * seg, ngroups);
-  const int wn = min(sg0 + seg, ngroups) - sg0;
-  const int wit = (wn + kWarpIter - 1) / kWarpIter;
-  const float4 *wp = p4 + sg0;
-  const int gbase = a0 + 4 * sg0;  // logit index of this warp's first group
-  const float4 kPast = make_float4(-3.40282347e38f, -3.40282347e38f, -3.40282347e38f,
-                                   -3.40282347e38f);
-
-  auto load_iter = [&](float4 (&dst)[kVec], int it) {
+  large = __reduce_add_sync(0xffffffffu, large);
+  large_before = __reduce_add_sync(0xffffffffu, large_before);
+  small_before = __reduce_add_sync(0xffffffffu, small_before);
+  if (lane == 0) {
+    red[0][warp] = large;
+    red[1][warp] = large_before;
+    red[2][warp] = small_before;
+  }
+  // The sample: 512 float4 groups spread evenly over the aligned middle of the row.
+  const Span sp = aligned_span(rowp, 0, a.vocab);
+  const int S = min(kThreads, sp.ngroups);
+  uint64_t t1 = 0, t2 = 0;
+  if (k > 0 && tid < S) {
+    const int g = (int)(((2LL * tid + 1) * sp.ngroups) / (2LL * S));
+    const float4 v = __ldg(reinterpret_cast<const float4 *>(rowp + sp.a0) + g);
+    const float xs[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int q = 0; q < kVec; q++) {
-      const int g = it * kWarpIter + q * 32 + lane;
-      dst[q] = g < wn ? __ldcs(wp + g) : kPast;
-    }
-  };
-  // Online max / sum-exp over one iteration's 16 values. Groups past the segment hold
-  // -FLT_MAX: they never raise the max and add exp(-huge) = 0 to the sum.
-  auto stats_iter = [&](const float4 (&v)[kVec], int it) -> float {
-    float im = max3f(max3f(v[0].x, v[0].y, v[0].z), max3f(v[0].w, v[1].x, v[1].y),
-                     max3f(v[1].z, v[1].w, v[2].x));
-    im = max3f(im, max3f(v[2].y, v[2].z, v[2].w), max3f(v[3].x, v[3].y, max3f(v[3].z, v[3].w, im)));
-    if (it + 1 < wit) {
-      float l = min3f(min3f(v[0].x, v[0].y, v[0].z), min3f(v[0].w, v[1].x, v[1].y),
-                      min3f(v[1].z, v[1].w, v[2].x));
-      l = min3f(l, min3f(v[2].y, v[2].z, v[2].w), min3f(v[3].x, v[3].y, min3f(v[3].z, v[3].w, l)));
-      mn = fminf(mn, l);
-    } else {
-#pragma unroll
-      for (int q = 0; q < kVec; q++)
-        if (it * kWarpIter + q * 32 + lane < wn)
-          mn = min3f(mn, min3f(v[q].x, v[q].y, v[q].z), v[q].w);
-    }
-    if (im > m) {
-      s *= ex2_approx((m - im) * kLog2e);
-      m = im;
-      mL = m * kLog2e;
-      // fma(x, L, -rn(m*L)) differs from (x - m)*L by the rounding of m*L, at most
-      // 2^-20 for |m| <= 16: every term then carries a factor within 7e-7 of 1 (well
-      // inside the 1e-5 budget). Larger |m| uses the subtraction form.
-      small = fabsf(m) <= 16.f;
-    }
-    if (small) {
-#pragma unroll
-      for (int q = 0; q < kVec; q++)
-        s += (ex2_approx(fmaf(v[q].x, kLog2e, -mL)) + ex2_approx(fmaf(v[q].y, kLog2e, -mL))) +
-             (ex2_approx(fmaf(v[q].z, kLog2e, -mL)) + ex2_approx(fmaf(v[q].w, kLog2e, -mL)));
-    } else {
-#pragma unroll
-      for (int q = 0; q < kVec; q++)
-        s += (ex2_approx((v[q].x - m) * kLog2e) + ex2_approx((v[q].y - m) * kLog2e)) +
-             (ex2_approx((v[q].z - m) * kLog2e) + ex2_approx((v[q].w - m) * kLog2e));
-    }
-    return im;
-  };
-  // Appends this iteration's logits >= tf (warp-uniform call). On this path tau carries
-  // no index bits, so the float compare is the whole test. Slots past kCandCap are not
-  // written; the overflow flag sends the slice to the re-filter at the end.
-  auto filter_iter = [&](const float4 (&v)[kVec], int it, float im) {
-    if (!__any_sync(0xffffffffu, im >= tf)) return;
-    uint32_t hm = 0;
-#pragma unroll
-    for (int q = 0; q < kVec; q++) {
-      if (it * kWarpIter + q * 32 + lane < wn) {
-        hm |= (v[q].x >= tf ? 1u : 0u) << (4 * q);
-        hm |= (v[q].y >= tf ? 2u : 0u) << (4 * q);
-        hm |= (v[q].z >= tf ? 4u : 0u) << (4 * q);
-        hm |= (v[q].w >= tf ? 8u : 0u) << (4 * q);
+    for (int e = 0; e < 4; e++) {
+      const uint64_t c = composite(key_of(xs[e]), (uint32_t)(sp.a0 + 4 * g + e));
+      if (c > t1) {
+        t2 = t1;
+        t1 = c;
+      } else if (c > t2) {
+        t2 = c;
       }
     }
-    const int nh = __popc(hm);
-    int incl = nh;
+  }
+  cand[2 * tid] = t1;
+  cand[2 * tid + 1] = t2;
+  __syncthreads();
+  PPHASE(row, 1);
+  if (tid == 0) {
+    int lt = 0, lb = 0, sb = 0;
+    for (int w = 0; w < kWarps; w++) {
+      lt += red[0][w];
+      lb += red[1][w];
+      sb += red[2][w];
+    }
+    a.order[k > 64 ? lb : lt + sb] = row;
+  }
+  float tf = -__int_as_float(0x7f800000);  // no estimate: every logit is a candidate
+  if (k > 0) {
+    const int ns = 4 * S;
+    const float mu = (float)k * (float)ns / (float)a.vocab;
+    // The sample is part of the row, so rr = k can never fail; for larger k the
+    // statistical rank is smaller (and the check at the end of the pass guards it).
+    const int rr = min(k, (int)ceilf(mu + 3.f * sqrtf(mu) + 4.f));
+    // The per-thread top two stand in for the sample's top (at least rr sample logits
+    // are at or above their rr-th largest).
+    if (rr >= 1 && rr < 2 * S && rr < ns) {
+      uint64_t thr;
+      if (bin_rank_topk(cand, 2 * kThreads, rr, 4 * kThreads, hist, sh) >= 0)
+        thr = cand[rr - 1];
+      else
+        thr = select_top(cand, 2 * kThreads, rr, hist, sh);
+      if ((thr >> 32) != 0ull) tf = float_of_key((uint32_t)(thr >> 32));
+    }
+  }
+  PPHASE(row, 2);
+  if (tid == 0) {
+    a.row_tf[row] = tf;
+    a.row_k[row] = k;
+  }
+#ifdef TABBY_TRACE
+  if (tid == 0 && row < 4096) g_ptrace[row * 2 + 1] = globaltimer();
+#endif
+}
+
+// Filters a whole row again, exactly: every logit starts as a candidate and compaction
+// (keep a superset of the k best, raise the threshold) makes room. Block-uniform call;
+// returns the candidate count (at least min(k, vocab)).
+__device__ __noinline__ int rescan_row(const float *rowp, int vocab, int k, uint64_t *cand,
+                                       uint32_t *hist, Shared *sh) {
+  const int tid = threadIdx.x, warp = tid >> 5;
+  __syncthreads();
+  if (tid == 0) {
+    sh->count = 0;
+    sh->overflow = 0;
+  }
+  __syncthreads();
+  uint64_t tau = 0;
+  float tf = -__int_as_float(0x7f800000);
+  const Span sp = aligned_span(rowp, 0, vocab);
+  const float4 *p4 = reinterpret_cast<const float4 *>(rowp + sp.a0);
+  if (warp == 0) {
+    const int e = tid < 4 ? tid : sp.a1 + (tid - 4);
+    const bool in = tid < 8 && (tid < 4 ? (e < sp.a0) : (e < vocab));
+    const float x = in ? __ldcg(rowp + e) : 0.f;
+    insert_candidate(in, composite(key_of(x), (uint32_t)(in ? e : 0)), cand, &sh->count,
+                     &sh->overflow);
+  }
+  for (int base = 0; base < sp.ngroups; base += kThreads) {
+    __syncthreads();
+    if (sh->count > (uint32_t)(kCandCap - 4 * kThreads)) {
+      int kept;
+      const uint64_t thr =
+          shrink_to(cand, (int)sh->count, k, max(2 * k, 1024), hist, sh, &kept);
+      if (tid == 0) sh->count = (uint32_t)kept;
+      __syncthreads();
+      tau = thr;
+      tf = float_of_key((uint32_t)(thr >> 32));
+    }
+    const int g = base + tid;
+    const float4 w = g < sp.ngroups ? __ldcg(p4 + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const bool hit = g < sp.ngroups && max3f(w.x, w.y, fmaxf(w.z, w.w)) >= tf;
+    if (__any_sync(0xffffffffu, hit)) {
+      const float xs[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const uint64_t c = composite(key_of(xs[e]), (uint32_t)(sp.a0 + 4 * g + e));
+        insert_candidate(hit && c >= tau, c, cand, &sh->count, &sh->overflow);
+      }
+    }
+  }
+  __syncthreads();
+  return (int)sh->count;
+}
+
+// The finish of one row, run by the CTA whose unit completed it (block-uniform call).
+__device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint64_t *cand,
+                                        uint32_t *hist, Shared *sh) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const float *rowp = a.logits + (int64_t)row * a.row_stride;
+  uint32_t pflags = 0;
+  FTRACE(row, 0);
+  // Everything the finish reads from global memory, issued together.
+  const int np = a.nch * kWarps;
+  float2 st = make_float2(-3.40282347e38f, 0.f);
+  if (tid < np) st = __ldcg(&a.warp_stats[(int64_t)row * np + tid]);
+  const int ccount = (warp == 0 && lane < a.nch) ? (int)__ldcg(&a.chunk_cnt[row * a.nch + lane]) : 0;
+  const uint32_t rflags = __ldcg(&a.row_flags[row]);
+  tabby_sampling_params prm = {};
+  double uni = 0.0;
+  if (a.mode == kModeSample) {
+    prm = a.params[row];
+    uni = a.uniforms[row];
+    if (isnan(prm.temperature) || isnan(prm.top_p)) pflags = kFlagBadParams;
+  }
+  // Chunk counts and their offsets in the gathered list (a.nch <= 32: warp 0).
+  if (warp == 0) {
+    int incl = ccount;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int t = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += t;
     }
-    const int wtotal = __shfl_sync(0xffffffffu, incl, 31);
-    if (wtotal == 0) return;
-    uint32_t wb = 0;
-    if (lane == 31) wb = atomicAdd(&sh->count, (uint32_t)wtotal);
-    wb = __shfl_sync(0xffffffffu, wb, 31);
-    uint32_t slot = wb + (uint32_t)(incl - nh);
-#pragma unroll
-    for (int q = 0; q < kVec; q++) {
-      const uint32_t gb = (hm >> (4 * q)) & 15u;
-      if (gb) {
-        const float xs[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
-        const int base_idx = gbase + 4 * (it * kWarpIter + q * 32 + lane);
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          if ((gb >> e) & 1u) {
-            if (slot < (uint32_t)kCandCap)
-              cand[slot] = composite(key_of(xs[e]), (uint32_t)(base_idx + e));
-            else
-              sh->overflow = 1u;
-            slot++;
-          }
-        }
-      }
-    }
-  };
-
-  // Keeps the k best candidates and raises the threshold (block-uniform call).
-  auto compact = [&]() {
-    int kept;
-    const uint64_t thr = shrink_to(cand, (int)sh->count, k, max(2 * k, 1024), hist, sh, &kept);
-    if (tid == 0) {
-      sh->count = (uint32_t)kept;
-      uint64_t t = thr;
-      if (a.nslices > 1) {
-        atomicMax(&a.row_tau[row], (unsigned long long)thr);
-        const uint64_t g = ld_cg_u64(&a.row_tau[row]);
-        t = thr > g ? thr : g;
-      }
-      sh->tau = t;
-    }
-    __syncthreads();
-    tau = sh->tau;
-    tf = float_of_key((uint32_t)(tau >> 32));
-  };
-  // Inserts the candidates of float4 group g of the aligned middle (warp-uniform call;
-  // groups past the end of the slice insert nothing).
-  auto filter_group = [&](const float4 w, const float gm, int g) {
-    const bool hit = g < ngroups && gm >= tf;
-    if (__any_sync(0xffffffffu, hit)) {
-      const float xs[4] = {w.x, w.y, w.z, w.w};
-      const int base_idx = a0 + 4 * g;
-#pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const uint64_t c = composite(key_of(xs[e]), (uint32_t)(base_idx + e));
-        insert_candidate(hit && c >= tau, c, cand, &sh->count, &sh->overflow);
-      }
-    }
-  };
-
-  // ---- iteration 0 of every warp, then the threshold estimate ----
-  float4 v[kVec], nx[kVec];
-  load_iter(v, 0);
-  if (wit > 1) load_iter(nx, 1);
-  const float im0 = wit > 0 ? stats_iter(v, 0) : -3.40282347e38f;
-  if (k > 0) {
-    // The 16 first iterations (one per warp, spread over the slice) are the sample. The
-    // threshold is a logit with about rr sample logits at or above it, rr set so that
-    // the slice holds at least k logits above it with near certainty (rr = mu +
-    // 3 sqrt(mu) + 4, mu the expected sample count above the slice's k-th largest). The
-    // end of the pass checks it; a failed estimate (fewer than k above it, or more than
-    // the buffer holds) re-filters the slice.
-    uint64_t t1 = 0, t2 = 0;
-    if (wit > 0) {
-#pragma unroll
-      for (int q = 0; q < kVec; q++) {
-        if (q * 32 + lane < wn) {
-          const float xs[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
-#pragma unroll
-          for (int e = 0; e < 4; e++) {
-            const uint64_t c = composite(key_of(xs[e]), (uint32_t)(gbase + 4 * (q * 32 + lane) + e));
-            if (c > t1) {
-              t2 = t1;
-              t1 = c;
-            } else if (c > t2) {
-              t2 = c;
-            }
-          }
-        }
-      }
-    }
-    // ns: logits in the sample; nw: warps that read any; rr: sample rank wanted.
-    int ns = 0, nw = 0;
-    for (int w = 0; w < kWarps; w++) {
-      const int b0 = min(w * seg, ngroups);
-      const int gw = min(kWarpIter, min(b0 + seg, ngroups) - b0);
-      ns += 4 * gw;
-      nw += gw > 0 ? 1 : 0;
-    }
-    const float mu = (float)k * (float)ns / (float)max(slice_len, 1);
-    const int rr = (int)ceilf(mu + 3.f * sqrtf(mu) + 4.f);
-    // Each warp sorts its 64 top-two slots and offers its j-th largest (j = rr / nw
-    // rounded up); the smallest offer has at least j logits of every offering warp at
-    // or above it, so about rr of the sample.
-    const int j = nw > 0 ? (rr + nw - 1) / nw : 65;
-    warp_sort64_desc(t1, t2);
-    const uint64_t jth = __shfl_sync(0xffffffffu, ((j - 1) & 1) ? t2 : t1, ((j - 1) >> 1) & 31);
-    if (lane == 0) sh->samp[warp] = (j <= 2 * min(32, wn)) ? jth : ~0ull;
-    __syncthreads();
-    uint64_t thr = ~0ull;
-#pragma unroll
-    for (int w = 0; w < kWarps; w++) thr = min(thr, (uint64_t)sh->samp[w]);
-    if (rr <= 256 && j <= 64 && thr != ~0ull && (thr >> 32) != 0ull) {
-      tau = thr & 0xffffffff00000000ull;
-      tf = float_of_key((uint32_t)(thr >> 32));
-    }
-    if (warp == 0)
-      insert_candidate(re >= 0 && composite(key_of(rx), (uint32_t)re) >= tau,
-                       composite(key_of(rx), (uint32_t)max(re, 0)), cand, &sh->count,
-                       &sh->overflow);
-    if (wit > 0) filter_iter(v, 0, im0);
+    sh->off[lane] = incl - ccount;
+    sh->cnt[lane] = ccount;
   }
-  TRACE(8);
-
-  // ---- the rest of each warp's segment: no block barrier until the end ----
-  for (int it = 1; it < wit; it++) {
+  // Statistics of every warp of every chunk, merged in a fixed order.
+  float bm = st.x;
 #pragma unroll
-    for (int q = 0; q < kVec; q++) v[q] = nx[q];
-    if (it + 1 < wit) load_iter(nx, it + 1);
-    const float im = stats_iter(v, it);
-    if (k > 0) filter_iter(v, it, im);
-  }
-  TRACE(2);
+  for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+  if (lane == 0) sh->red_f[warp] = bm;
   __syncthreads();
-  TRACE_VAL(11, sh->count);
+  float M = lane < kWarps ? sh->red_f[lane] : -3.40282347e38f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float contrib = st.y > 0.f ? st.y * __expf(st.x - M) : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) contrib += __shfl_xor_sync(0xffffffffu, contrib, o);
+  if (lane == 0) sh->red_f2[warp] = contrib;
+  __syncthreads();
+  float S = lane < kWarps ? sh->red_f2[lane] : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+  const float row_max = M, sum_exp = S;
+  FTRACE(row, 5);
 
-  if (k > 0 && (sh->overflow != 0u || (int)sh->count < need)) {
-    // The estimate failed: filter the slice again from memory, block-synchronously,
-    // with every logit a candidate at first and compaction raising the threshold.
-    __syncthreads();
-    if (tid == 0) {
-      sh->count = 0;
-      sh->overflow = 0;
-    }
-    tau = 0;
-    tf = -__int_as_float(0x7f800000);
-    __syncthreads();
-    if (warp == 0)
-      insert_candidate(re >= 0, composite(key_of(rx), (uint32_t)max(re, 0)), cand, &sh->count,
-                       &sh->overflow);
-    for (int base = 0; base < ngroups; base += kThreads) {
-      __syncthreads();
-      if (sh->count > (uint32_t)(kCandCap - 4 * kThreads)) compact();
-      const int g = base + tid;
-      const float4 w = g < ngroups ? __ldcg(p4 + g) : kPast;
-      filter_group(w, max3f(w.x, w.y, fmaxf(w.z, w.w)), g);
-    }
-    __syncthreads();
-  }
-  TRACE(9);
-  // NaN or +inf logits leave s or m non-finite; -inf and values at or below the
-  // reference's -3.0e38 sentinel show in the running min.
-  const bool bad = !(s == s) || !(m <= 3.40282347e38f) || !(mn > kNegSentinel) ||
-                   !(s <= 3.40282347e38f);
-
-  // ---- this slice's <= k best and its (max, sum-exp) partial ----
-  // The slice's k best, sorted by (value desc, index asc): cut to at most 2048 that
-  // include them, sort, keep the first min(k, cnt).
-  const int cnt = top_sorted(cand, (int)sh->count, k, hist, sh);
-  TRACE(10);
-  float M, S;
-  uint32_t flags;
-  {
-    // Block merge of the per-thread online pairs, in a fixed order.
-    float bm = m;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
-    if ((tid & 31) == 0) sh->red_f[tid >> 5] = bm;
-    __syncthreads();
-    M = sh->red_f[0];
-    for (int i = 1; i < kWarps; i++) M = fmaxf(M, sh->red_f[i]);
-    float contrib = s > 0.f ? s * __expf(m - M) : 0.f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) contrib += __shfl_xor_sync(0xffffffffu, contrib, o);
-    const int any_bad = __syncthreads_or(bad ? 1 : 0);
-    if ((tid & 31) == 0) sh->red_f[tid >> 5] = contrib;
-    __syncthreads();
-    S = 0.f;
-    for (int i = 0; i < kWarps; i++) S += sh->red_f[i];
-    flags = pflags | (any_bad ? kFlagBadInput : 0u);
-  }
-  TRACE(3);
-
-  int kk;
-  float sum_exp, row_max;
-  if (a.nslices == 1) {
-    // The whole row was this CTA's: no merge.
-    kk = cnt;
-    sum_exp = S;
-    row_max = M;
-  } else {
-    // Publish the slice, then count it in; the row's last slice merges them all.
-    const int64_t sidx = (int64_t)row * a.nslices + sl;
-    if (tid == 0) {
-      a.slice_stats[sidx] = make_float2(M, S);
-      a.slice_meta[sidx] = make_uint2((uint32_t)cnt, flags);
-    }
-    unsigned long long *dst = a.slice_cand + sidx * a.cand_ld;
-    for (int i = tid; i < cnt; i += kThreads) dst[i] = cand[i];
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-      const uint32_t done = atomicAdd(&a.row_count[row], 1u);
-      sh->last = done == (uint32_t)(a.nslices - 1);
-    }
-    __syncthreads();
-    if (!sh->last) return;
-    __threadfence();
-    TRACE(4);
-    // Statistics of every slice, loaded in parallel and merged in slice order.
-    const int64_t sbase = (int64_t)row * a.nslices;
-    float2 mine = make_float2(-3.40282347e38f, 0.f);
-    uint2 meta = make_uint2(0u, 0u);
-    if (tid < a.nslices) {
-      (void)CHECK(a.nslices <= kMaxSlices, 6, a.nslices, 0);
-      mine = __ldcg(&a.slice_stats[sbase + tid]);
-      meta = __ldcg(&a.slice_meta[sbase + tid]);
-    }
-    float wm = mine.x;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, o));
-    uint32_t wf = meta.y;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) wf |= __shfl_xor_sync(0xffffffffu, wf, o);
-    // a.nslices <= 32: warp 0 holds everything.
-    double part = (mine.y > 0.f) ? (double)mine.y * (double)__expf(mine.x - wm) : 0.0;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-    // Candidate offsets: exclusive scan of the slice counts.
-    int c = (int)meta.x, incl = c;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(0xffffffffu, incl, o);
-      if ((tid & 31) >= o) incl += t;
-    }
-    if (tid < 32) {
-      sh->off[tid] = incl - c;
-      sh->cnt[tid] = c;
-    }
-    if (tid == 0) {
-      sh->merge_max = wm;
-      sh->merge_sum = (float)part;
-      sh->flags = wf;
-    }
-    __syncthreads();
-    flags = sh->flags;
-    row_max = sh->merge_max;
-    sum_exp = sh->merge_sum;
-    // Gather the slices' candidates, compacting whenever the buffer would overflow.
-    int total = 0;
-    int q0 = 0;
-    while (q0 < a.nslices) {
-      int q1 = q0, add = 0;
-      while (q1 < a.nslices && total + add + sh->cnt[q1] <= kCandCap) add += sh->cnt[q1++];
-      for (int q = q0; q < q1; q++) {
-        const unsigned long long *src = a.slice_cand + (sbase + q) * a.cand_ld;
-        const int base = total + sh->off[q] - sh->off[q0];
-        for (int i = tid; i < sh->cnt[q]; i += kThreads) cand[base + i] = ld_cg_u64(src + i);
+  const int total = sh->off[31] + sh->cnt[31];
+  int n = 0;
+  if (k > 0) {
+    if (!(rflags & kRowOverflow) && total >= k) {
+      // Every element of the gathered list is one independent load.
+      const unsigned long long *src = a.row_cand + (int64_t)row * kCandCap;
+      const int cc = chunk_slots(a);
+      for (int i = tid; i < total; i += kThreads) {
+        int c = 0;
+        while (c + 1 < a.nch && sh->off[c + 1] <= i) c++;
+        cand[i] = ld_cg_u64(src + (int64_t)c * cc + (i - sh->off[c]));
       }
-      total += add;
-      q0 = q1;
+      n = total;
       __syncthreads();
-      if (q0 < a.nslices && total > kCandCap / 2) {
-        int kept;
-        shrink_to(cand, total, k, 2048, hist, sh, &kept);
-        total = kept;
-      }
-    }
-    kk = top_sorted(cand, total, k, hist, sh);
-    if (tid == 0) {
-      // Leave the row's counters clean for the next launch.
-      a.row_count[row] = 0;
-      a.row_tau[row] = 0;
+    } else {
+      n = rescan_row(rowp, a.vocab, k, cand, hist, sh);
     }
   }
-  TRACE(5);
-  TRACE(6);
-
+  FTRACE(row, 1);
+#ifdef TABBY_TRACE
+  if (tid == 0 && row < 4096) g_ftrace[row * 8 + 6] = (unsigned long long)n;
+#endif
+  const int kk = top_sorted(cand, n, k, hist, sh);
+  FTRACE(row, 2);
+  const uint32_t flags = (rflags & kFlagBadInput) | pflags;
   const uint32_t status = (flags & kFlagBadInput)    ? (uint32_t)TABBY_EINPUT
                           : (flags & kFlagBadParams) ? (uint32_t)TABBY_EINVAL
-                          : (flags & kFlagTimeout)   ? (uint32_t)TABBY_ETIMEOUT
                                                      : (uint32_t)TABBY_OK;
   if (k <= 64) {
-    // Small pools: warp 0 finishes the row alone, the other warps leave the SM.
+    // Small pools: warp 0 finishes the row alone.
     if (warp != 0) return;
     const uint64_t c0 = cand[2 * lane], c1 = cand[2 * lane + 1];
     const int32_t id0 = (int32_t)~(uint32_t)c0, id1 = (int32_t)~(uint32_t)c1;
@@ -1452,7 +1447,6 @@ __global__ void __launch_bounds__(kThreads, TABBY_MIN_BLOCKS) stream_kernel(Stre
               in ? (uint32_t)((int64_t)(e ? id1 : id0) + a.index_offset) : 0xffffffffu);
         }
       }
-      TRACE(7);
       return;
     }
     if (a.topk_ids) {
@@ -1463,9 +1457,10 @@ __global__ void __launch_bounds__(kThreads, TABBY_MIN_BLOCKS) stream_kernel(Stre
       if (2 * lane < kk) a.topk_values[(int64_t)row * a.topk_ld + 2 * lane] = x0;
       if (2 * lane + 1 < kk) a.topk_values[(int64_t)row * a.topk_ld + 2 * lane + 1] = x1;
     }
-    finalize_warp(id0, id1, x0, x1, kk, max_logit, sum_exp, a.params[row], a.uniforms[row],
+    FTRACE(row, 3);
+    finalize_warp(id0, id1, x0, x1, kk, max_logit, sum_exp, prm, uni,
                   reinterpret_cast<double *>(hist), &a.out[row], status);
-    TRACE(7);
+    FTRACE(row, 4);
     return;
   }
   // Unpack into (id, value) in the histogram space; once that is done the candidate
@@ -1475,18 +1470,22 @@ __global__ void __launch_bounds__(kThreads, TABBY_MIN_BLOCKS) stream_kernel(Stre
   double *exact = reinterpret_cast<double *>(cand);
   double *scaled = exact + kk;
   double *cum = scaled + kk;
-  for (int i = tid; i < kk; i += kThreads) {
-    const uint64_t e = cand[i];
-    const uint32_t key = (uint32_t)(e >> 32);
-    const uint32_t idx = ~(uint32_t)e;
-    float v = float_of_key(key);
-    if (key == 0x80000000u) v = rowp[idx];  // keep the sign of a zero logit
-    ids[i] = (int32_t)idx;
-    vals[i] = v;
+  uint64_t mine[2];
+  for (int j = 0; j < 2; j++) mine[j] = tid + j * kThreads < kk ? cand[tid + j * kThreads] : 0ull;
+  __syncthreads();
+  for (int j = 0; j < 2; j++) {
+    const int i = tid + j * kThreads;
+    if (i < kk) {
+      const uint32_t key = (uint32_t)(mine[j] >> 32);
+      const uint32_t idx = ~(uint32_t)mine[j];
+      float v = float_of_key(key);
+      if (key == 0x80000000u) v = rowp[idx];  // keep the sign of a zero logit
+      ids[i] = (int32_t)idx;
+      vals[i] = v;
+    }
   }
   __syncthreads();
   const float max_logit = kk > 0 ? vals[0] : row_max;
-
   if (a.mode == kModeTopK || a.mode == kModeShard) {
     float *blk = a.block + (int64_t)row * a.block_ld;
     const int slots = a.mode == kModeShard ? TABBY_SHARD_TOP_K : k;
@@ -1504,17 +1503,255 @@ __global__ void __launch_bounds__(kThreads, TABBY_MIN_BLOCKS) stream_kernel(Stre
       blk[2 + 2 * i] = v;
       blk[3 + 2 * i] = __uint_as_float(gi);
     }
-    TRACE(7);
     return;
   }
-
   if (a.topk_ids)
     for (int i = tid; i < kk; i += kThreads) a.topk_ids[(int64_t)row * a.topk_ld + i] = ids[i];
   if (a.topk_values)
     for (int i = tid; i < kk; i += kThreads) a.topk_values[(int64_t)row * a.topk_ld + i] = vals[i];
-  finalize_sample(ids, vals, kk, max_logit, sum_exp, a.params[row], a.uniforms[row], exact,
-                  scaled, cum, sh, &a.out[row], status);
-  TRACE(7);
+  FTRACE(row, 3);
+  finalize_sample(ids, vals, kk, max_logit, sum_exp, prm, uni, exact, scaled, cum, sh,
+                  &a.out[row], status);
+  FTRACE(row, 4);
+}
+
+__global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant__ PassArgs a) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  uint64_t *cand = reinterpret_cast<uint64_t *>(smem_raw);
+  uint32_t *hist = reinterpret_cast<uint32_t *>(cand + kCandCap);
+  Shared *sh = reinterpret_cast<Shared *>(hist + kBins);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int units = a.rows * a.nch;
+  constexpr float kLog2e = 1.44269504088896341f;
+  const float4 kPast = make_float4(-3.40282347e38f, -3.40282347e38f, -3.40282347e38f,
+                                   -3.40282347e38f);
+  // plan_kernel's results (and its reset of the counters) are complete past this point.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+#ifdef TABBY_TRACE
+  int uj = 0;
+#define NOW() globaltimer()
+#else
+#define NOW() 0ull
+#endif
+  for (;;) {
+    __syncthreads();  // the previous unit is done with the shared state
+    if (tid == 0) {
+      sh->unit = atomicAdd(a.sched, 1u);
+      sh->count = 0;
+      sh->overflow = 0;
+    }
+    __syncthreads();
+    const int unit = (int)sh->unit;
+    if (unit >= units) break;
+#ifdef TABBY_TRACE
+    UTRACE(uj, 0, NOW());
+#endif
+    const int ri = unit / a.nch;
+    const int chunk = unit - ri * a.nch;
+    const int row = a.order[ri];
+    const int k = a.row_k[row];
+    const float tf = a.row_tf[row];
+    const float *rowp = a.logits + (int64_t)row * a.row_stride;
+    const int lo = chunk * a.chunk;
+    const int hi = min(lo + a.chunk, a.vocab);
+    const Span sp = aligned_span(rowp, lo, hi);
+    const float4 *p4 = reinterpret_cast<const float4 *>(rowp + sp.a0);
+
+    // Per-thread online statistics: s = sum exp(x - m) as 2^((x - m) * log2(e)).
+    float m = -3.40282347e38f, s = 0.f;
+    float mL = 0.f;      // rn(m * log2(e)) for the FFMA form of the exponent argument
+    bool small = false;  // |m| small enough for the FFMA form
+    float mn = 3.40282347e38f;  // running min: catches -inf and the -3e38 sentinel
+
+    // Ragged ends of the chunk: at most 3 logits before a0 and 3 after a1, one per lane
+    // of warp 0.
+    if (warp == 0) {
+      const int e = lane < 4 ? lo + lane : sp.a1 + (lane - 4);
+      const bool in = lane < 8 && (lane < 4 ? (e < sp.a0) : (e < hi));
+      float rx = 0.f;
+      if (in) {
+        rx = __ldg(rowp + e);
+        m = rx;
+        mL = m * kLog2e;
+        small = fabsf(m) <= 16.f;
+        s = 1.f;
+        mn = rx;
+      }
+      insert_candidate(in && k > 0 && rx >= tf, composite(key_of(rx), (uint32_t)(in ? e : 0)),
+                       cand, &sh->count, &sh->overflow);
+    }
+
+    // Warp segments: warp w streams the float4 groups [sg0, sg0 + wn) of the chunk's
+    // aligned middle, 128 groups (2 KB, four 512-byte coalesced loads) an iteration,
+    // the next iteration's loads in flight while one is worked on.
+    const int seg = (sp.ngroups + kWarps - 1) / kWarps;
+    const int sg0 = min(warp * seg, sp.ngroups);
+    const int wn = min(sg0 + seg, sp.ngroups) - sg0;
+    const int wit = (wn + kWarpIter - 1) / kWarpIter;
+    const float4 *wp = p4 + sg0;
+    const int gbase = sp.a0 + 4 * sg0;  // logit index of this warp's first group
+
+    auto load_iter = [&](float4 (&dst)[kVec], int it) {
+#pragma unroll
+      for (int q = 0; q < kVec; q++) {
+        const int g = it * kWarpIter + q * 32 + lane;
+        dst[q] = g < wn ? __ldcs(wp + g) : kPast;
+      }
+    };
+    // Online max / sum-exp over one iteration's 16 values. Groups past the segment hold
+    // -FLT_MAX: they never raise the max and add exp(-huge) = 0 to the sum.
+    auto stats_iter = [&](const float4 (&v)[kVec], int it) -> float {
+      float im = max3f(max3f(v[0].x, v[0].y, v[0].z), max3f(v[0].w, v[1].x, v[1].y),
+                       max3f(v[1].z, v[1].w, v[2].x));
+      im = max3f(im, max3f(v[2].y, v[2].z, v[2].w),
+                 max3f(v[3].x, v[3].y, max3f(v[3].z, v[3].w, im)));
+      if (it + 1 < wit) {
+        float l = min3f(min3f(v[0].x, v[0].y, v[0].z), min3f(v[0].w, v[1].x, v[1].y),
+                        min3f(v[1].z, v[1].w, v[2].x));
+        l = min3f(l, min3f(v[2].y, v[2].z, v[2].w),
+                  min3f(v[3].x, v[3].y, min3f(v[3].z, v[3].w, l)));
+        mn = fminf(mn, l);
+      } else {
+#pragma unroll
+        for (int q = 0; q < kVec; q++)
+          if (it * kWarpIter + q * 32 + lane < wn)
+            mn = min3f(mn, min3f(v[q].x, v[q].y, v[q].z), v[q].w);
+      }
+      if (im > m) {
+        s *= ex2_approx((m - im) * kLog2e);
+        m = im;
+        mL = m * kLog2e;
+        // fma(x, L, -rn(m*L)) differs from (x - m)*L by the rounding of m*L, at most
+        // 2^-20 for |m| <= 16: every term then carries a factor within 7e-7 of 1 (well
+        // inside the 1e-5 budget). Larger |m| uses the subtraction form.
+        small = fabsf(m) <= 16.f;
+      }
+      if (small) {
+#pragma unroll
+        for (int q = 0; q < kVec; q++)
+          s += (ex2_approx(fmaf(v[q].x, kLog2e, -mL)) + ex2_approx(fmaf(v[q].y, kLog2e, -mL))) +
+               (ex2_approx(fmaf(v[q].z, kLog2e, -mL)) + ex2_approx(fmaf(v[q].w, kLog2e, -mL)));
+      } else {
+#pragma unroll
+        for (int q = 0; q < kVec; q++)
+          s += (ex2_approx((v[q].x - m) * kLog2e) + ex2_approx((v[q].y - m) * kLog2e)) +
+               (ex2_approx((v[q].z - m) * kLog2e) + ex2_approx((v[q].w - m) * kLog2e));
+      }
+      return im;
+    };
+    // Appends this iteration's logits >= tf (warp-uniform call). Slots past kCandCap are
+    // not written; the overflow flag sends the row to the exact re-filter.
+    auto filter_iter = [&](const float4 (&v)[kVec], int it, float im) {
+      if (!__any_sync(0xffffffffu, im >= tf)) return;
+      uint32_t hm = 0;
+#pragma unroll
+      for (int q = 0; q < kVec; q++) {
+        if (it * kWarpIter + q * 32 + lane < wn) {
+          hm |= (v[q].x >= tf ? 1u : 0u) << (4 * q);
+          hm |= (v[q].y >= tf ? 2u : 0u) << (4 * q);
+          hm |= (v[q].z >= tf ? 4u : 0u) << (4 * q);
+          hm |= (v[q].w >= tf ? 8u : 0u) << (4 * q);
+        }
+      }
+      const int nh = __popc(hm);
+      int incl = nh;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const int wtotal = __shfl_sync(0xffffffffu, incl, 31);
+      if (wtotal == 0) return;
+      uint32_t wb = 0;
+      if (lane == 31) wb = atomicAdd(&sh->count, (uint32_t)wtotal);
+      wb = __shfl_sync(0xffffffffu, wb, 31);
+      uint32_t slot = wb + (uint32_t)(incl - nh);
+#pragma unroll
+      for (int q = 0; q < kVec; q++) {
+        const uint32_t gb = (hm >> (4 * q)) & 15u;
+        if (gb) {
+          const float xs[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+          const int base_idx = gbase + 4 * (it * kWarpIter + q * 32 + lane);
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            if ((gb >> e) & 1u) {
+              if (slot < (uint32_t)kCandCap)
+                cand[slot] = composite(key_of(xs[e]), (uint32_t)(base_idx + e));
+              else
+                sh->overflow = 1u;
+              slot++;
+            }
+          }
+        }
+      }
+    };
+
+    float4 v[kVec], nx[kVec];
+    if (wit > 0) load_iter(v, 0);
+    if (wit > 1) load_iter(nx, 1);
+    for (int it = 0; it < wit; it++) {
+      if (it > 0) {
+#pragma unroll
+        for (int q = 0; q < kVec; q++) v[q] = nx[q];
+        if (it + 1 < wit) load_iter(nx, it + 1);
+      }
+      const float im = stats_iter(v, it);
+      if (k > 0) filter_iter(v, it, im);
+    }
+
+#ifdef TABBY_TRACE
+    UTRACE(uj, 1, NOW());
+#endif
+    // Per-warp statistics into the row's table.
+    {
+      float wm = m;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, o));
+      float ws = s > 0.f ? s * __expf(m - wm) : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o);
+      // NaN or +inf logits leave s or m non-finite; -inf and values at or below the
+      // reference's -3.0e38 sentinel show in the running min.
+      const bool bad = !(s == s) || !(m <= 3.40282347e38f) || !(mn > kNegSentinel) ||
+                       !(s <= 3.40282347e38f);
+      const bool wbad = __any_sync(0xffffffffu, bad);
+      if (lane == 0) {
+        a.warp_stats[((int64_t)row * a.nch + chunk) * kWarps + warp] = make_float2(wm, ws);
+        if (wbad) atomicOr(&a.row_flags[row], kFlagBadInput);
+      }
+    }
+    __syncthreads();
+    // The chunk's candidates into its slots of the row's list.
+    const uint32_t cnt = sh->count;
+    const int cc = chunk_slots(a);
+    const bool fits = sh->overflow == 0u && cnt <= (uint32_t)cc;
+    if (tid == 0) {
+      a.chunk_cnt[row * a.nch + chunk] = fits ? cnt : 0u;
+      if (!fits) atomicOr(&a.row_flags[row], kRowOverflow);
+    }
+    if (fits) {
+      unsigned long long *dst = a.row_cand + (int64_t)row * kCandCap + (int64_t)chunk * cc;
+      for (int i = tid; i < (int)cnt; i += kThreads) dst[i] = cand[i];
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) sh->last = atomicAdd(&a.row_done[row], 1u) == (uint32_t)(a.nch - 1) ? 1u : 0u;
+    __syncthreads();
+#ifdef TABBY_TRACE
+    UTRACE(uj, 2, NOW());
+#endif
+    if (sh->last) {
+      __threadfence();
+      finish_row(a, row, k, cand, hist, sh);
+#ifdef TABBY_TRACE
+      UTRACE(uj, 3, NOW());
+#endif
+    }
+#ifdef TABBY_TRACE
+    uj++;
+#endif
+  }
 }
 
 // ------------------------------------------------------------------------------------
@@ -1604,35 +1841,34 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch a) {
 // ------------------------------------------------------------------------------------
 static int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
-static size_t stream_smem_bytes() {
+static size_t row_smem_bytes() {
   return (size_t)kCandCap * 8 + (size_t)kBins * 4 + sizeof(Shared) + 64;
 }
 
-int32_t max_slices(int32_t vocab, int32_t cap) {
-  (void)cap;
-  return std::max(1, std::min(kMaxSlices, (vocab + kMinSlice - 1) / kMinSlice));
-}
+// Units a CTA should see on average: enough for the dynamic schedule to even out the
+// CTAs' speeds, few enough that the per-unit overhead stays small.
+constexpr int kUnitsPerCta = 3;
 
 cudaError_t plan_rows(int32_t sms, int32_t rows, int32_t vocab, int32_t cap, RowGeometry *geo) {
-  // One CTA streams a whole row when there are enough rows to fill two CTAs per SM;
-  // smaller batches split rows into up to 32 slices of >= kMinSlice logits, merged by
-  // the row's last slice. Two CTAs share an SM (shared memory ~107 KB each).
-  int S = (int)std::min<int64_t>(kMaxSlices, (2LL * sms) / std::max(rows, 1));
-  S = std::max(1, std::min(S, max_slices(vocab, cap)));
+  (void)cap;
+  const int ctas = 2 * std::max(sms, 1);  // two 512-thread CTAs per SM
+  const int max_by_size = std::max(1, vocab / kMinChunk);
+  int nch = (kUnitsPerCta * ctas + std::max(rows, 1) - 1) / std::max(rows, 1);
+  nch = std::max(1, std::min(nch, std::min(kMaxChunks, max_by_size)));
   RowGeometry g;
-  g.slice = round_up((vocab + S - 1) / S, 4);
-  g.nslices = (vocab + g.slice - 1) / g.slice;
-  g.data_floats = 0;
-  g.smem_bytes = stream_smem_bytes();
+  g.chunk = round_up((vocab + nch - 1) / nch, 4);
+  g.nch = (vocab + g.chunk - 1) / g.chunk;
+  g.grid = (int32_t)std::min<int64_t>((int64_t)rows * g.nch, ctas);
+  g.smem_bytes = row_smem_bytes();
   *geo = g;
   return cudaSuccess;
 }
 
-static cudaError_t prepare_stream_kernel(size_t smem_bytes) {
+static cudaError_t prepare_row_kernel(size_t smem_bytes) {
   static size_t configured = 0;
   if (smem_bytes > configured) {
     cudaError_t err = cudaFuncSetAttribute(
-        stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes);
+        row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes);
     if (err != cudaSuccess) return err;
     configured = smem_bytes;
   }
@@ -1642,13 +1878,14 @@ static cudaError_t prepare_stream_kernel(size_t smem_bytes) {
 cudaError_t launch_rows(const RowLaunch &l, const RowGeometry &geo, const Scratch &scr,
                         cudaStream_t stream) {
   if (l.rows == 0) return cudaSuccess;
-  StreamArgs a;
+  if (l.rows > scr.max_rows || geo.nch > kMaxChunks) return cudaErrorInvalidValue;
+  PassArgs a;
   a.logits = l.logits;
   a.row_stride = l.row_stride;
   a.rows = l.rows;
   a.vocab = l.vocab;
-  a.slice = geo.slice;
-  a.nslices = geo.nslices;
+  a.nch = geo.nch;
+  a.chunk = geo.chunk;
   a.mode = l.mode;
   a.cap = l.cap;
   a.fixed_k = l.fixed_k;
@@ -1661,17 +1898,33 @@ cudaError_t launch_rows(const RowLaunch &l, const RowGeometry &geo, const Scratc
   a.topk_ld = l.topk_ld;
   a.block = l.block;
   a.block_ld = l.block_ld;
-  a.row_count = scr.row_count;
-  a.row_tau = scr.row_tau;
-  a.slice_stats = scr.slice_stats;
-  a.slice_meta = scr.slice_meta;
-  a.slice_cand = scr.slice_cand;
-  a.cand_ld = scr.cand_ld;
-  cudaError_t err = prepare_stream_kernel(geo.smem_bytes);
+  a.sched = scr.sched;
+  a.row_done = scr.row_done;
+  a.chunk_cnt = scr.chunk_cnt;
+  a.row_flags = scr.row_flags;
+  a.row_tf = scr.row_tf;
+  a.row_k = scr.row_k;
+  a.order = scr.order;
+  a.warp_stats = scr.warp_stats;
+  a.row_cand = scr.row_cand;
+  cudaError_t err = prepare_row_kernel(geo.smem_bytes);
   if (err != cudaSuccess) return err;
-  const unsigned grid = (unsigned)((int64_t)l.rows * geo.nslices);
-  stream_kernel<<<grid, kThreads, geo.smem_bytes, stream>>>(a);
-  return cudaGetLastError();
+  plan_kernel<<<l.rows, kThreads, 0, stream>>>(a);
+  err = cudaGetLastError();
+  if (err != cudaSuccess) return err;
+  // Programmatic dependent launch: the row kernel's CTAs are scheduled while the plan
+  // finishes and wait for it in griddepcontrol.wait, hiding the launch gap.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)geo.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = geo.smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, row_kernel, a);
 }
 
 cudaError_t launch_merge(const MergeLaunch &l, cudaStream_t stream) {
@@ -1714,6 +1967,18 @@ int host_sample_from_topk(const int32_t *ids, const float *logits, int32_t n, fl
 extern "C" __attribute__((visibility("default"))) int tabby_debug_trace(unsigned long long *host,
                                                                         int n) {
   return (int)cudaMemcpyFromSymbol(host, tabby::g_trace, (size_t)n * 8);
+}
+extern "C" __attribute__((visibility("default"))) int tabby_debug_utrace(unsigned long long *u,
+                                                                         unsigned long long *p) {
+  int e = (int)cudaMemcpyFromSymbol(u, tabby::g_utrace, sizeof(tabby::g_utrace));
+  if (e) return e;
+  return (int)cudaMemcpyFromSymbol(p, tabby::g_ptrace, sizeof(tabby::g_ptrace));
+}
+extern "C" __attribute__((visibility("default"))) int tabby_debug_ftrace(unsigned long long *f) {
+  return (int)cudaMemcpyFromSymbol(f, tabby::g_ftrace, sizeof(tabby::g_ftrace));
+}
+extern "C" __attribute__((visibility("default"))) int tabby_debug_pphase(unsigned long long *f) {
+  return (int)cudaMemcpyFromSymbol(f, tabby::g_pphase, sizeof(tabby::g_pphase));
 }
 #endif
 

@@ -280,20 +280,21 @@ def test_seeded_determinism(torch_cuda):
 
 @pytest.mark.parametrize("rows", [2, 256])
 def test_threshold_estimate_failures(torch_cuda, oracle, rows):
-    """Rows built so the threshold the row kernel estimates from the start of each of its
-    16 warp segments is wrong in both directions: too high (the segment starts hold the
-    largest logits, so fewer than k logits pass) and too low (the starts hold the
-    smallest, so the candidates overflow the buffer). Both must end in the exact result
-    through the re-filter. Small batches split rows into slices, 256 rows do not."""
+    """Rows built so the threshold estimated from the 512 float4 groups sampled evenly
+    over the row is wrong in both directions: too high (the sampled groups hold the
+    largest logits, so fewer than k logits pass) and too low (they hold the smallest,
+    so the candidates overflow the row's list). Both must end in the exact result
+    through the re-filter."""
     g = np.random.default_rng(17)
     vocab = 151936
-    seg = (vocab // 4 + 15) // 16 * 4  # logits per warp segment at one slice per row
-    starts = np.zeros(vocab, bool)
-    for w in range(16):
-        starts[w * seg:w * seg + 512] = True
+    ngroups = vocab // 4
+    sampled = np.zeros(vocab, bool)
+    for i in range(512):
+        grp = (2 * i + 1) * ngroups // 1024
+        sampled[4 * grp:4 * grp + 4] = True
     x = g.standard_normal((rows, vocab)).astype(np.float32)
-    x[0::2, starts] += 20.0   # too-high estimate
-    x[1::2, starts] -= 20.0   # too-low estimate
+    x[0::2, sampled] += 20.0   # too-high estimate
+    x[1::2, sampled] -= 20.0   # too-low estimate
     for k, cap in [(1, 64), (50, 64), (1000, 1024)]:
         p = oracle.make_params(1.0, 0.9, k, rows)
         u = g.random(rows)
