@@ -183,7 +183,7 @@ TABBY_API int tabby_sample_from_topk(const int32_t *ids, const float *logits, in
  * (code running under an allocator that owns all device memory, plug-in hosts that
  * forbid allocation on their request path, callers that must not add allocations
  * between steps). The row kernel's global scratch -- per-row counters and per-slice
- * candidate lists, about 2 MB -- lives in a file-scope __device__ array that every GPU
+ * candidate lists, about 5.4 MB -- lives in a file-scope __device__ array that every GPU
  * loading the library keeps until the process exits. Same inputs, outputs and results
  * as tabby_sample_rows_async with max_top_k as the pool cap; max_top_k must be
  * 1..TABBY_NOALLOC_MAX_TOP_K, larger values are rejected with TABBY_EINVAL.

@@ -25,7 +25,7 @@ namespace tabby {
 namespace {
 
 constexpr int kNoAllocRows = 32;  // rows a launch; larger batches run in several launches
-constexpr size_t kScratchBytes = Scratch::layout_bytes(kNoAllocRows);  // ~2.1 MB
+constexpr size_t kScratchBytes = Scratch::layout_bytes(kNoAllocRows);  // ~5.4 MB
 
 // The scratch itself. In host code this name is only a stand-in for the symbol; its
 // device address comes from cudaGetSymbolAddress below.

@@ -56,7 +56,7 @@ struct RowGeometry {
   size_t smem_bytes = 0;
 };
 
-constexpr int32_t kScratchCandidates = 8192;  // candidates a row may collect (kCandCap)
+constexpr int32_t kScratchGroups = 8192;      // candidate groups a row may collect
 constexpr int32_t kScratchChunks = 32;        // chunks a row may have (kMaxChunks)
 constexpr int32_t kScratchWarps = 16;         // warps a CTA has
 
@@ -66,21 +66,24 @@ constexpr int32_t kScratchWarps = 16;         // warps a CTA has
 struct Scratch {
   uint32_t *sched = nullptr;                 // [1] unit counter
   uint32_t *row_done = nullptr;              // [max_rows] chunks finished
-  uint32_t *chunk_cnt = nullptr;             // [max_rows][kScratchChunks] chunk candidates
+  uint32_t *warp_cnt = nullptr;              // [max_rows][kScratchChunks * kScratchWarps]
   uint32_t *row_flags = nullptr;             // [max_rows] bad input / overflow
   float *row_tf = nullptr;                   // [max_rows] estimated threshold
-  int32_t *row_k = nullptr;                  // [max_rows] pool size
+  float *row_tf_lo = nullptr;                // [max_rows] the re-filter's starting threshold
+  float *pos_tf = nullptr;                   // [max_rows] threshold by processing position
+  int32_t *pos_k = nullptr;                  // [max_rows] pool size by processing position
   int32_t *order = nullptr;                  // [max_rows] processing order
   float2 *warp_stats = nullptr;              // [max_rows][kScratchChunks][kScratchWarps]
-  unsigned long long *row_cand = nullptr;    // [max_rows][kScratchCandidates]
+  float4 *row_gval = nullptr;                // [max_rows][kScratchGroups] group values
+  int32_t *row_gidx = nullptr;               // [max_rows][kScratchGroups] group first index
   int32_t max_rows = 0;
 
   static constexpr size_t section(size_t bytes) { return (bytes + 255) / 256 * 256; }
   static constexpr size_t layout_bytes(int32_t rows) {
-    return section(4) + 5 * section(4 * (size_t)rows) +
-           section(4 * (size_t)rows * kScratchChunks) +
+    return section(4) + 7 * section(4 * (size_t)rows) +
+           section(4 * (size_t)rows * kScratchChunks * kScratchWarps) +
            section(8 * (size_t)rows * kScratchChunks * kScratchWarps) +
-           section(8 * (size_t)rows * kScratchCandidates);
+           section(16 * (size_t)rows * kScratchGroups) + section(4 * (size_t)rows * kScratchGroups);
   }
   static size_t bytes(int32_t rows) { return layout_bytes(rows); }
   static Scratch carve(void *base, int32_t rows) {
@@ -91,19 +94,25 @@ struct Scratch {
     p += section(4);
     s.row_done = reinterpret_cast<uint32_t *>(p);
     p += section(4 * r);
-    s.chunk_cnt = reinterpret_cast<uint32_t *>(p);
-    p += section(4 * r * kScratchChunks);
+    s.warp_cnt = reinterpret_cast<uint32_t *>(p);
+    p += section(4 * r * kScratchChunks * kScratchWarps);
     s.row_flags = reinterpret_cast<uint32_t *>(p);
     p += section(4 * r);
     s.row_tf = reinterpret_cast<float *>(p);
     p += section(4 * r);
-    s.row_k = reinterpret_cast<int32_t *>(p);
+    s.row_tf_lo = reinterpret_cast<float *>(p);
+    p += section(4 * r);
+    s.pos_tf = reinterpret_cast<float *>(p);
+    p += section(4 * r);
+    s.pos_k = reinterpret_cast<int32_t *>(p);
     p += section(4 * r);
     s.order = reinterpret_cast<int32_t *>(p);
     p += section(4 * r);
     s.warp_stats = reinterpret_cast<float2 *>(p);
     p += section(8 * r * kScratchChunks * kScratchWarps);
-    s.row_cand = reinterpret_cast<unsigned long long *>(p);
+    s.row_gval = reinterpret_cast<float4 *>(p);
+    p += section(16 * r * kScratchGroups);
+    s.row_gidx = reinterpret_cast<int32_t *>(p);
     s.max_rows = rows;
     return s;
   }

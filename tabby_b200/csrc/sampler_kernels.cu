@@ -7,7 +7,7 @@
 //
 //   plan_kernel    one CTA per row: resets the row's counters, fixes its pool size and
 //                  its place in the processing order, and estimates a filter threshold
-//                  from 2048 logits sampled evenly over the row.
+//                  from 4096 logits sampled evenly over the row.
 //   row_kernel     persistent, two 512-thread CTAs per SM taking (row, chunk) units from
 //                  a global counter. Each warp streams its part of the chunk straight
 //                  into registers (four 16-byte loads in flight a thread, the next
@@ -30,6 +30,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "finalize.cuh"
 #include "sampler_internal.h"
@@ -40,12 +41,23 @@ constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kVec = 4;                   // float4 loads in flight per thread per iteration
 constexpr int kWarpIter = 32 * kVec;      // float4 groups a warp reads per iteration (2 KB)
-constexpr int kCandCap = 8192;            // candidate buffer (composites) per CTA
+#ifndef TABBY_PREFETCH
+#define TABBY_PREFETCH 0  // ask for the next unit before the current one ends
+#endif
+#ifndef TABBY_PLAN_GROUPS
+#define TABBY_PLAN_GROUPS 1  // float4 groups a plan thread samples
+#endif
+constexpr int kRowGroups = 8192;   // candidate groups (float4 + index) a row's global list holds
+constexpr int kStages = 3;         // cp.async stages of the streaming loop
+constexpr int kStageBytes = kStages * 4 * 512 * 16;  // the stages (kStages x kVec x kThreads)
+// The finish reuses the stage region: composites first, the histogram at its end.
+constexpr int kFinishCap = (kStageBytes - 2048 * 4) / 8;
 constexpr int kBins = 2048;               // radix digit: 11 bits
 constexpr int kMaxChunks = 32;            // chunks of one row (warp stats: chunks x 16 <= 512)
 constexpr int kMinChunk = 8192;           // logits: below this a row is not split further
 constexpr int kMergeThreads = 512;
-static_assert(kCandCap == kScratchCandidates && kMaxChunks == kScratchChunks &&
+static_assert(kRowGroups == kScratchGroups && kFinishCap >= 8192 &&
+                  kRowGroups / (kMaxChunks * kWarps) >= 16 && kMaxChunks == kScratchChunks &&
                   kWarps == kScratchWarps && kMaxChunks * kWarps <= kThreads,
               "scratch layout and kernel constants disagree");
 constexpr float kNegSentinel = -3.0e38f;  // NEG_INF of reduce_max.wgsl:13
@@ -67,6 +79,13 @@ __device__ unsigned long long g_utrace[kUnitTraceCtas * kUnitTraceUnits * 4];
 __device__ unsigned long long g_ptrace[4096 * 2];
 __device__ unsigned long long g_ftrace[4096 * 8];
 __device__ unsigned long long g_pphase[4096 * 4];
+__device__ unsigned long long g_lcyc[kUnitTraceCtas * kUnitTraceUnits * 4];
+__device__ unsigned long long g_fz[4096 * 8];
+#define FZ(slot)                                                                    \
+  do {                                                                              \
+    if (threadIdx.x == 0 && sh->trace_row >= 0 && sh->trace_row < 4096)             \
+      g_fz[sh->trace_row * 8 + (slot)] = clock64();                                 \
+  } while (0)
 #define PPHASE(row, slot)                                                  \
   do {                                                                     \
     if (threadIdx.x == 0 && (row) < 4096) g_pphase[(row) * 4 + (slot)] = clock64(); \
@@ -99,6 +118,9 @@ __device__ unsigned long long g_pphase[4096 * 4];
   } while (0)
 #define PPHASE(row, slot) \
   do {                    \
+  } while (0)
+#define FZ(slot) \
+  do {           \
   } while (0)
 #define TRACE(ph) \
   do {            \
@@ -172,6 +194,26 @@ __device__ __forceinline__ void cp_async_commit() {
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
+__device__ __forceinline__ void cp_async16_u32(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void st_shared_f4(uint32_t dst, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ float4 ld_shared_f4(uint32_t src) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(src)
+               : "memory");
+  return v;
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 // Three-input float max / min (sm_100 max.f32 / min.f32 with three sources).
 __device__ __forceinline__ float max3f(float a, float b, float c) {
@@ -220,6 +262,9 @@ struct Shared {
   uint32_t inb;
   uint32_t last;  // this CTA finishes the row
   uint32_t unit;  // the unit this CTA works on
+  int32_t urow, uk;  // its row and pool size
+  float utf;         // its threshold
+  int32_t trace_row;  // row being finished (tuning traces only)
   uint32_t base;  // where the unit's candidates go in the row's list
   int32_t cut_claim;
   int32_t chosen_claim;
@@ -622,21 +667,21 @@ __device__ __noinline__ uint64_t shrink_to(uint64_t *cand, int n, int k, int lim
 // ------------------------------------------------------------------------------------
 // sampleFromTopK on the device (sampler.ts:147-212).
 //
-// The exponentials and the divisions by the pool sums are per candidate, so all threads
-// compute them. The reference then makes three decisions from left-to-right float64
-// sums: the top-p cut, the drawn candidate and poolExhausted. Here those sums come from
-// a parallel tree / scan, whose results differ from the sequential ones by at most
-// (2n + 2*log2(n) + 3) * 2^-53 (n <= 1024 candidates, all terms positive, every sum
-// <= 1 + n * 2^-53). A decision is taken from the parallel sums only when its margin
-// exceeds 4x that bound; otherwise thread 0 replays the reference's sequential
+// The reference makes three decisions from left-to-right float64 sums: the top-p cut,
+// the drawn candidate and poolExhausted. Here those sums come from parallel trees /
+// scans of fast estimates of the terms (approx_exact / approx_scaled); each decision is
+// taken from them only when its margin exceeds decision_bound(n), a rigorous bound on
+// the difference to the reference's sums, otherwise thread 0 replays the reference's
 // arithmetic (decide_sequential). The token id, considered count and poolExhausted
-// therefore always equal the reference's; poolMass is the parallel sum unless the
-// replay ran (it stays within 1e-12 relative of the left-to-right value).
+// therefore always equal the reference's; the reported probability is the reference's
+// exp(l - max) / sumExp of the chosen candidate, computed exactly (js_exp); poolMass is
+// the parallel sum (within 1e-12 relative of the reference's) unless the replay ran.
 // ------------------------------------------------------------------------------------
-__device__ __noinline__ void finalize_sample(const int32_t *ids, const float *vals, int n, float max_logit,
-                                float sum_exp, tabby_sampling_params p, double u, double *exact,
-                                double *scaled, double *cum, Shared *sh,
-                                tabby_sample_outcome *out, uint32_t status) {
+__device__ __noinline__ void finalize_sample(const int32_t *ids, const float *vals, int n,
+                                             float max_logit, float sum_exp,
+                                             tabby_sampling_params p, double u, double *cum,
+                                             double *work, Shared *sh,
+                                             tabby_sample_outcome *out, uint32_t status) {
   const int tid = threadIdx.x;
   if (status != TABBY_OK || n == 0) {
     if (tid == 0) {
@@ -656,33 +701,37 @@ __device__ __noinline__ void finalize_sample(const int32_t *ids, const float *va
     return;
   }
   const bool sample = p.temperature > 0;
+  FZ(0);
+  const double inv_sum = 1.0 / (double)sum_exp;
+  const double inv_t = sample ? 1.0 / p.temperature : 0.0;
   // Two consecutive candidates a thread (n <= 2 * blockDim.x).
   const int i0 = 2 * tid, i1 = 2 * tid + 1;
   double e0 = 0.0, e1 = 0.0, s0 = 0.0, s1 = 0.0;
   if (i0 < n) {
-    e0 = exact_prob(vals[i0], max_logit, sum_exp);
-    exact[i0] = e0;
-    if (sample) s0 = scaled_weight(vals[i0], max_logit, p.temperature);
-    scaled[i0] = s0;
+    e0 = approx_exact(vals[i0], max_logit, inv_sum);
+    if (sample) s0 = approx_scaled(vals[i0], max_logit, inv_t);
   }
   if (i1 < n) {
-    e1 = exact_prob(vals[i1], max_logit, sum_exp);
-    exact[i1] = e1;
-    if (sample) s1 = scaled_weight(vals[i1], max_logit, p.temperature);
-    scaled[i1] = s1;
+    e1 = approx_exact(vals[i1], max_logit, inv_sum);
+    if (sample) s1 = approx_scaled(vals[i1], max_logit, inv_t);
   }
-  const double pool_mass = block_sum_f64(JS_ADD(e0, e1), sh);
-  const double bound = 4.0 * (double)(2 * n + 2 * 11 + 3) * 1.1102230246251565e-16;
+  FZ(1);
+  const double pool_mass = block_sum_f64(e0 + e1, sh);
+  FZ(2);
+  const double bound = decision_bound(n);
 
   int32_t cut = 1, chosen = 0, exhausted = 0;
   bool fallback = false;
   if (sample) {
-    const double st = block_sum_f64(JS_ADD(s0, s1), sh);
-    const double w0 = i0 < n ? JS_DIV(s0, st) : 0.0;
-    const double w1 = i1 < n ? JS_DIV(s1, st) : 0.0;
-    const double before = block_exclusive_scan_f64(JS_ADD(w0, w1), sh);
-    const double c0 = JS_ADD(before, w0);
-    const double c1 = JS_ADD(c0, w1);
+    const double st = block_sum_f64(s0 + s1, sh);
+    const double inv_st = 1.0 / st;
+    const double w0 = i0 < n ? s0 * inv_st : 0.0;
+    const double w1 = i1 < n ? s1 * inv_st : 0.0;
+    FZ(3);
+    const double before = block_exclusive_scan_f64(w0 + w1, sh);
+    FZ(4);
+    const double c0 = before + w0;
+    const double c1 = c0 + w1;
     if (i0 < n) cum[i0] = c0;
     if (i1 < n) cum[i1] = c1;
     if (tid == 0) {
@@ -713,7 +762,7 @@ __device__ __noinline__ void finalize_sample(const int32_t *ids, const float *va
     }
     // target = u * total; first i < cut with target < cumulative (sampler.ts:191-203).
     const double total = cum[cut - 1];
-    const double target = JS_MUL(u, total);
+    const double target = u * total;
     if (i0 < cut && target < c0)
       atomicMin(&sh->chosen_claim, i0);
     else if (i1 < cut && target < c1)
@@ -730,12 +779,13 @@ __device__ __noinline__ void finalize_sample(const int32_t *ids, const float *va
     chosen = ch < cut ? ch : cut - 1;
     fallback = sh->fallback != 0;
   }
+  FZ(5);
   if (tid == 0) {
     tabby_sample_outcome o;
     double pm = pool_mass;
     if (fallback) {
-      // Exact replay of the reference's left-to-right float64 arithmetic.
-      const Decision d = decide_sequential(exact, scaled, cum, n, p.temperature, p.top_p, u);
+      const Decision d =
+          decide_sequential(vals, n, max_logit, sum_exp, p.temperature, p.top_p, u, work);
       chosen = d.chosen;
       cut = d.cut;
       exhausted = d.pool_exhausted;
@@ -743,7 +793,7 @@ __device__ __noinline__ void finalize_sample(const int32_t *ids, const float *va
     }
     o.id = ids[chosen];
     o.considered_count = cut;
-    o.probability = exact[chosen];
+    o.probability = exact_prob(vals[chosen], max_logit, sum_exp);
     o.pool_mass = pm;
     o.pool_exhausted = exhausted;
     o.pool_size = n;
@@ -753,6 +803,7 @@ __device__ __noinline__ void finalize_sample(const int32_t *ids, const float *va
     o.reserved = fallback ? 1 : 0;  // 1 when the sequential replay decided
     *out = o;
   }
+  FZ(6);
 }
 
 // Merges the sorted 64-list (w0, w1) into the sorted 64-list (v0, v1) (both descending,
@@ -847,14 +898,16 @@ __device__ __noinline__ void finalize_warp(int32_t id0, int32_t id1, float x0, f
   }
   const bool sample = p.temperature > 0;
   const int i0 = 2 * lane, i1 = i0 + 1;
-  const double e0 = i0 < n ? exact_prob(x0, max_logit, sum_exp) : 0.0;
-  const double e1 = i1 < n ? exact_prob(x1, max_logit, sum_exp) : 0.0;
-  const double s0 = (sample && i0 < n) ? scaled_weight(x0, max_logit, p.temperature) : 0.0;
-  const double s1 = (sample && i1 < n) ? scaled_weight(x1, max_logit, p.temperature) : 0.0;
-  double pm = JS_ADD(e0, e1);
+  const double inv_sum = 1.0 / (double)sum_exp;
+  const double inv_t = sample ? 1.0 / p.temperature : 0.0;
+  const double e0 = i0 < n ? approx_exact(x0, max_logit, inv_sum) : 0.0;
+  const double e1 = i1 < n ? approx_exact(x1, max_logit, inv_sum) : 0.0;
+  const double s0 = (sample && i0 < n) ? approx_scaled(x0, max_logit, inv_t) : 0.0;
+  const double s1 = (sample && i1 < n) ? approx_scaled(x1, max_logit, inv_t) : 0.0;
+  double pm = e0 + e1;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) pm = JS_ADD(pm, __shfl_xor_sync(kAll, pm, o));
-  const double bound = 4.0 * (double)(2 * n + 2 * 11 + 3) * 1.1102230246251565e-16;
+  for (int o = 16; o > 0; o >>= 1) pm += __shfl_xor_sync(kAll, pm, o);
+  const double bound = decision_bound(n);
 
   int32_t cut = 1, chosen = 0, exhausted = 0;
   bool fallback = false;
@@ -866,21 +919,22 @@ __device__ __noinline__ void finalize_warp(int32_t id0, int32_t id1, float x0, f
     return (i & 1) ? b : a;
   };
   if (sample) {
-    double st = JS_ADD(s0, s1);
+    double st = s0 + s1;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) st = JS_ADD(st, __shfl_xor_sync(kAll, st, o));
-    const double w0 = i0 < n ? JS_DIV(s0, st) : 0.0;
-    const double w1 = i1 < n ? JS_DIV(s1, st) : 0.0;
-    double incl = JS_ADD(w0, w1);
+    for (int o = 16; o > 0; o >>= 1) st += __shfl_xor_sync(kAll, st, o);
+    const double inv_st = 1.0 / st;
+    const double w0 = i0 < n ? s0 * inv_st : 0.0;
+    const double w1 = i1 < n ? s1 * inv_st : 0.0;
+    double incl = w0 + w1;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const double t = __shfl_up_sync(kAll, incl, o);
-      if (lane >= o) incl = JS_ADD(t, incl);
+      if (lane >= o) incl += t;
     }
     double excl = __shfl_up_sync(kAll, incl, 1);
     if (lane == 0) excl = 0.0;
-    c0 = JS_ADD(excl, w0);
-    c1 = JS_ADD(c0, w1);
+    c0 = excl + w0;
+    c1 = c0 + w1;
     cut = n;
     if (p.top_p < 1) {
       // First i with cumulative >= top_p (sampler.ts:175-189).
@@ -903,7 +957,7 @@ __device__ __noinline__ void finalize_warp(int32_t id0, int32_t id1, float x0, f
       cut = ci < n ? ci + 1 : n;
     }
     // target = u * total; first i < cut with target < cumulative (sampler.ts:191-203).
-    const double target = JS_MUL(u, cum_at(cut - 1));
+    const double target = u * cum_at(cut - 1);
     const bool g0 = i0 < cut && target < c0, g1 = i1 < cut && target < c1;
     const unsigned bal = __ballot_sync(kAll, g0 || g1);
     int ch = cut;
@@ -921,16 +975,16 @@ __device__ __noinline__ void finalize_warp(int32_t id0, int32_t id1, float x0, f
   }
   if (fallback) {
     // Exact replay of the reference's left-to-right float64 arithmetic.
-    double *ex = scratch, *sc = scratch + 64, *wt = scratch + 128;
-    ex[i0] = e0;
-    ex[i1] = e1;
-    sc[i0] = s0;
-    sc[i1] = s1;
+    float *xs = reinterpret_cast<float *>(scratch);
+    double *wk = scratch + 32;
+    if (i0 < n) xs[i0] = x0;
+    if (i1 < n) xs[i1] = x1;
     __syncwarp();
-    int32_t dv[4] = {0, 0, 0, 0};
+    int32_t dv[3] = {0, 0, 0};
     double dpm = 0.0;
     if (lane == 0) {
-      const Decision d = decide_sequential(ex, sc, wt, n, p.temperature, p.top_p, u);
+      const Decision d =
+          decide_sequential(xs, n, max_logit, sum_exp, p.temperature, p.top_p, u, wk);
       dv[0] = d.chosen;
       dv[1] = d.cut;
       dv[2] = d.pool_exhausted;
@@ -942,12 +996,12 @@ __device__ __noinline__ void finalize_warp(int32_t id0, int32_t id1, float x0, f
     pm = __shfl_sync(kAll, dpm, 0);
   }
   const int32_t cid = __shfl_sync(kAll, (chosen & 1) ? id1 : id0, (chosen >> 1) & 31);
-  const double cprob = __shfl_sync(kAll, (chosen & 1) ? e1 : e0, (chosen >> 1) & 31);
+  const float cx = __shfl_sync(kAll, (chosen & 1) ? x1 : x0, (chosen >> 1) & 31);
   if (lane == 0) {
     tabby_sample_outcome o;
     o.id = cid;
     o.considered_count = cut;
-    o.probability = cprob;
+    o.probability = exact_prob(cx, max_logit, sum_exp);
     o.pool_mass = pm;
     o.pool_exhausted = exhausted;
     o.pool_size = n;
@@ -1071,13 +1125,13 @@ __device__ __noinline__ int bin_rank_topk(uint64_t *cand, int n, int k, int capa
 // returns how many. Block-uniform call. Lists of at most 512 are ranked directly,
 // longer ones through the binned ranking; long runs of equal logits fall back to the
 // per-warp top-64 tree (pools up to 64) or the exact radix select and a sort.
-__device__ __forceinline__ int top_sorted(uint64_t *cand, int n, int k, uint32_t *hist,
-                                          Shared *sh) {
+__device__ __forceinline__ int top_sorted(uint64_t *cand, int n, int k, int capacity,
+                                          uint32_t *hist, Shared *sh) {
   if (k <= 0 || n <= 0) {
     __syncthreads();
     return 0;
   }
-  if (n <= kThreads && 2 * n <= kCandCap) {
+  if (n <= kThreads && 2 * n <= capacity) {
     // Small lists: rank every element against all the others, then move the result
     // to the front.
     rank_sort_small(cand, n, min(k, n), cand + n);
@@ -1086,7 +1140,7 @@ __device__ __forceinline__ int top_sorted(uint64_t *cand, int n, int k, uint32_t
     __syncthreads();
     return R;
   }
-  const int r = bin_rank_topk(cand, n, k, kCandCap, hist, sh);
+  const int r = bin_rank_topk(cand, n, k, capacity, hist, sh);
   if (r >= 0) return r;
   if (k <= 64) {
     top64_sorted(cand, n, reinterpret_cast<uint64_t *>(hist));
@@ -1105,7 +1159,7 @@ __device__ __forceinline__ int top_sorted(uint64_t *cand, int n, int k, uint32_t
 //
 // plan_kernel (one CTA a row) resets the row's counters, fixes its pool size k and its
 // place in the processing order (rows with pools above 64 first, so that the rows whose
-// finish is cheap come last), and estimates a threshold from a sample of 512 float4
+// finish is cheap come last), and estimates a threshold from a sample of 1024 float4
 // groups spread over the row: a logit with about rr sample logits at or above it, rr
 // chosen so that the row holds at least k logits at or above it with near certainty
 // (rr = mu + 3 sqrt(mu) + 4, mu the expected sample count above the row's k-th largest).
@@ -1135,23 +1189,28 @@ struct PassArgs {
   int32_t block_ld;
   uint32_t *sched;       // unit counter
   uint32_t *row_done;    // [rows] chunks finished
-  uint32_t *chunk_cnt;   // [rows][nch] candidates of each chunk
+  uint32_t *warp_cnt;    // [rows][nch * kWarps] candidate groups of each (chunk, warp)
   uint32_t *row_flags;   // [rows] kFlagBadInput | kRowOverflow
-  float *row_tf;         // [rows] threshold
-  int32_t *row_k;        // [rows] pool size
+  float *row_tf;         // [rows] threshold, by row
+  float *row_tf_lo;      // [rows] a lower threshold (far safer rank), by row
+  float *pos_tf;         // [rows] threshold, by processing position
+  int32_t *pos_k;        // [rows] pool size, by processing position
   int32_t *order;        // [rows] processing order
   float2 *warp_stats;    // [rows][nch][kWarps] (max, sum-exp)
-  unsigned long long *row_cand;  // [rows][kCandCap]: chunk c owns slots [c * cc, (c + 1) * cc)
+  float4 *row_gval;      // [rows][kRowGroups] candidate groups: warp w of chunk c owns the
+  int32_t *row_gidx;     //   region (c * kWarps + w) of region_slots() slots
 };
 
 // Candidate slots of the row's list each chunk owns.
-__device__ __forceinline__ int chunk_slots(const PassArgs &a) { return kCandCap / a.nch; }
+__device__ __forceinline__ int region_slots(const PassArgs &a) {
+  return kRowGroups / (a.nch * kWarps);
+}
 
 constexpr uint32_t kRowOverflow = 8u;  // the row's candidates did not fit: filter it again
 
 // Appends c to the candidate buffer when pred holds (warp-uniform call). Slots past
-// kCandCap are not written; the overflow flag records the loss.
-__device__ __forceinline__ void insert_candidate(bool pred, uint64_t c, uint64_t *cand,
+// `cap` are not written; the overflow flag records the loss.
+__device__ __forceinline__ void insert_candidate(bool pred, uint64_t c, uint64_t *cand, int cap,
                                                  uint32_t *count, uint32_t *overflow) {
   const uint32_t mask = __ballot_sync(0xffffffffu, pred);
   if (mask == 0) return;
@@ -1162,7 +1221,7 @@ __device__ __forceinline__ void insert_candidate(bool pred, uint64_t c, uint64_t
   base = __shfl_sync(0xffffffffu, base, leader);
   const uint32_t slot = base + __popc(mask & ((1u << lane) - 1u));
   if (pred) {
-    if (slot < (uint32_t)kCandCap)
+    if (slot < (uint32_t)cap)
       cand[slot] = c;
     else
       *overflow = 1u;
@@ -1234,20 +1293,27 @@ __global__ void __launch_bounds__(kThreads) plan_kernel(const __grid_constant__ 
   }
   // The sample: 512 float4 groups spread evenly over the aligned middle of the row.
   const Span sp = aligned_span(rowp, 0, a.vocab);
-  const int S = min(kThreads, sp.ngroups);
+  constexpr int kPlanSample = TABBY_PLAN_GROUPS * kThreads;  // float4 groups sampled
+  const int S = min(kPlanSample, sp.ngroups);
   uint64_t t1 = 0, t2 = 0;
-  if (k > 0 && tid < S) {
-    const int g = (int)(((2LL * tid + 1) * sp.ngroups) / (2LL * S));
-    const float4 v = __ldg(reinterpret_cast<const float4 *>(rowp + sp.a0) + g);
-    const float xs[4] = {v.x, v.y, v.z, v.w};
+  if (k > 0) {
 #pragma unroll
-    for (int e = 0; e < 4; e++) {
-      const uint64_t c = composite(key_of(xs[e]), (uint32_t)(sp.a0 + 4 * g + e));
-      if (c > t1) {
-        t2 = t1;
-        t1 = c;
-      } else if (c > t2) {
-        t2 = c;
+    for (int j = 0; j < kPlanSample / kThreads; j++) {
+      const int i = j * kThreads + tid;
+      if (i < S) {
+        const int g = (int)(((2LL * i + 1) * sp.ngroups) / (2LL * S));
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(rowp + sp.a0) + g);
+        const float xs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const uint64_t c = composite(key_of(xs[e]), (uint32_t)(sp.a0 + 4 * g + e));
+          if (c > t1) {
+            t2 = t1;
+            t1 = c;
+          } else if (c > t2) {
+            t2 = c;
+          }
+        }
       }
     }
   }
@@ -1262,83 +1328,98 @@ __global__ void __launch_bounds__(kThreads) plan_kernel(const __grid_constant__ 
       lb += red[1][w];
       sb += red[2][w];
     }
-    a.order[k > 64 ? lb : lt + sb] = row;
+    sh->unit = (uint32_t)(k > 64 ? lb : lt + sb);  // this row's processing position
   }
   float tf = -__int_as_float(0x7f800000);  // no estimate: every logit is a candidate
+  float tf_lo = tf;
   if (k > 0) {
     const int ns = 4 * S;
     const float mu = (float)k * (float)ns / (float)a.vocab;
     // The sample is part of the row, so rr = k can never fail; for larger k the
     // statistical rank is smaller (and the check at the end of the pass guards it).
-    const int rr = min(k, (int)ceilf(mu + 3.f * sqrtf(mu) + 4.f));
+    const int rr = min(k, (int)ceilf(mu + 4.f * sqrtf(mu) + 6.f));
     // The per-thread top two stand in for the sample's top (at least rr sample logits
     // are at or above their rr-th largest).
-    if (rr >= 1 && rr < 2 * S && rr < ns) {
-      uint64_t thr;
-      if (bin_rank_topk(cand, 2 * kThreads, rr, 4 * kThreads, hist, sh) >= 0)
+    if (rr >= 1 && rr < 2 * min(S, kThreads) && rr < ns) {
+      // rr2: a far safer rank, the starting threshold of the exact re-filter.
+      const int rr2 = min(4 * rr, 2 * min(S, kThreads) - 1);
+      uint64_t thr, thr2;
+      if (bin_rank_topk(cand, 2 * kThreads, rr2, 4 * kThreads, hist, sh) >= 0) {
         thr = cand[rr - 1];
-      else
-        thr = select_top(cand, 2 * kThreads, rr, hist, sh);
+        thr2 = cand[rr2 - 1];
+      } else {
+        thr = thr2 = select_top(cand, 2 * kThreads, rr, hist, sh);
+      }
       if ((thr >> 32) != 0ull) tf = float_of_key((uint32_t)(thr >> 32));
+      if ((thr2 >> 32) != 0ull) tf_lo = float_of_key((uint32_t)(thr2 >> 32));
     }
   }
   PPHASE(row, 2);
   if (tid == 0) {
+    const int pos = (int)sh->unit;
+    a.order[pos] = row;
+    a.pos_k[pos] = k;
+    a.pos_tf[pos] = tf;
     a.row_tf[row] = tf;
-    a.row_k[row] = k;
+    a.row_tf_lo[row] = tf_lo;
   }
 #ifdef TABBY_TRACE
   if (tid == 0 && row < 4096) g_ptrace[row * 2 + 1] = globaltimer();
 #endif
 }
 
-// Filters a whole row again, exactly: every logit starts as a candidate and compaction
-// (keep a superset of the k best, raise the threshold) makes room. Block-uniform call;
-// returns the candidate count (at least min(k, vocab)).
-__device__ __noinline__ int rescan_row(const float *rowp, int vocab, int k, uint64_t *cand,
-                                       uint32_t *hist, Shared *sh) {
+// Filters a whole row again, exactly (block-uniform call): candidates are the logits
+// >= start_tf (a threshold of far safer rank than the failed estimate), and when those
+// are fewer than k, every logit; compaction (keep a superset of the k best, raise the
+// threshold) makes room. Returns the candidate count (at least min(k, vocab)).
+__device__ __noinline__ int rescan_row(const float *rowp, int vocab, int k, float start_tf,
+                                       uint64_t *cand, uint32_t *hist, Shared *sh) {
   const int tid = threadIdx.x, warp = tid >> 5;
-  __syncthreads();
-  if (tid == 0) {
-    sh->count = 0;
-    sh->overflow = 0;
-  }
-  __syncthreads();
-  uint64_t tau = 0;
-  float tf = -__int_as_float(0x7f800000);
   const Span sp = aligned_span(rowp, 0, vocab);
   const float4 *p4 = reinterpret_cast<const float4 *>(rowp + sp.a0);
-  if (warp == 0) {
-    const int e = tid < 4 ? tid : sp.a1 + (tid - 4);
-    const bool in = tid < 8 && (tid < 4 ? (e < sp.a0) : (e < vocab));
-    const float x = in ? __ldcg(rowp + e) : 0.f;
-    insert_candidate(in, composite(key_of(x), (uint32_t)(in ? e : 0)), cand, &sh->count,
-                     &sh->overflow);
-  }
-  for (int base = 0; base < sp.ngroups; base += kThreads) {
+  const float kNegInf = -__int_as_float(0x7f800000);
+  for (int attempt = 0; attempt < 2; attempt++) {
+    float tf = attempt == 0 ? start_tf : kNegInf;
+    uint64_t tau = tf == kNegInf ? 0ull : ((uint64_t)key_of(tf) << 32);
     __syncthreads();
-    if (sh->count > (uint32_t)(kCandCap - 4 * kThreads)) {
-      int kept;
-      const uint64_t thr =
-          shrink_to(cand, (int)sh->count, k, max(2 * k, 1024), hist, sh, &kept);
-      if (tid == 0) sh->count = (uint32_t)kept;
-      __syncthreads();
-      tau = thr;
-      tf = float_of_key((uint32_t)(thr >> 32));
+    if (tid == 0) {
+      sh->count = 0;
+      sh->overflow = 0;
     }
-    const int g = base + tid;
-    const float4 w = g < sp.ngroups ? __ldcg(p4 + g) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const bool hit = g < sp.ngroups && max3f(w.x, w.y, fmaxf(w.z, w.w)) >= tf;
-    if (__any_sync(0xffffffffu, hit)) {
-      const float xs[4] = {w.x, w.y, w.z, w.w};
+    __syncthreads();
+    if (warp == 0) {
+      const int e = tid < 4 ? tid : sp.a1 + (tid - 4);
+      const bool in = tid < 8 && (tid < 4 ? (e < sp.a0) : (e < vocab));
+      const float x = in ? __ldcg(rowp + e) : 0.f;
+      const uint64_t c = composite(key_of(x), (uint32_t)(in ? e : 0));
+      insert_candidate(in && c >= tau, c, cand, kFinishCap, &sh->count, &sh->overflow);
+    }
+    for (int base = 0; base < sp.ngroups; base += kThreads) {
+      __syncthreads();
+      if (sh->count > (uint32_t)(kFinishCap - 4 * kThreads)) {
+        int kept;
+        const uint64_t thr =
+            shrink_to(cand, (int)sh->count, k, max(2 * k, 1024), hist, sh, &kept);
+        if (tid == 0) sh->count = (uint32_t)kept;
+        __syncthreads();
+        tau = thr;
+        tf = float_of_key((uint32_t)(thr >> 32));
+      }
+      const int g = base + tid;
+      const float4 w = g < sp.ngroups ? __ldcg(p4 + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const bool hit = g < sp.ngroups && max3f(w.x, w.y, fmaxf(w.z, w.w)) >= tf;
+      if (__any_sync(0xffffffffu, hit)) {
+        const float xs[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const uint64_t c = composite(key_of(xs[e]), (uint32_t)(sp.a0 + 4 * g + e));
-        insert_candidate(hit && c >= tau, c, cand, &sh->count, &sh->overflow);
+        for (int e = 0; e < 4; e++) {
+          const uint64_t c = composite(key_of(xs[e]), (uint32_t)(sp.a0 + 4 * g + e));
+          insert_candidate(hit && c >= tau, c, cand, kFinishCap, &sh->count, &sh->overflow);
+        }
       }
     }
+    __syncthreads();
+    if ((int)sh->count >= min(k, vocab)) break;  // block-uniform
   }
-  __syncthreads();
   return (int)sh->count;
 }
 
@@ -1348,13 +1429,15 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const float *rowp = a.logits + (int64_t)row * a.row_stride;
   uint32_t pflags = 0;
+  if (tid == 0) sh->trace_row = row;
   FTRACE(row, 0);
   // Everything the finish reads from global memory, issued together.
   const int np = a.nch * kWarps;
   float2 st = make_float2(-3.40282347e38f, 0.f);
   if (tid < np) st = __ldcg(&a.warp_stats[(int64_t)row * np + tid]);
-  const int ccount = (warp == 0 && lane < a.nch) ? (int)__ldcg(&a.chunk_cnt[row * a.nch + lane]) : 0;
+  const int rcount = tid < np ? (int)__ldcg(&a.warp_cnt[(int64_t)row * np + tid]) : 0;
   const uint32_t rflags = __ldcg(&a.row_flags[row]);
+  const float tf = a.row_tf[row];
   tabby_sampling_params prm = {};
   double uni = 0.0;
   if (a.mode == kModeSample) {
@@ -1362,17 +1445,16 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
     uni = a.uniforms[row];
     if (isnan(prm.temperature) || isnan(prm.top_p)) pflags = kFlagBadParams;
   }
-  // Chunk counts and their offsets in the gathered list (a.nch <= 32: warp 0).
-  if (warp == 0) {
-    int incl = ccount;
+  // Region counts (one a thread) and their exclusive offsets in the gathered list, kept
+  // in the histogram space (np <= 512 entries).
+  uint32_t *roff = hist;
+  int rincl = rcount;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += t;
-    }
-    sh->off[lane] = incl - ccount;
-    sh->cnt[lane] = ccount;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, rincl, o);
+    if (lane >= o) rincl += t;
   }
+  if (lane == 31) sh->red_u2[warp] = (uint32_t)rincl;
   // Statistics of every warp of every chunk, merged in a fixed order.
   float bm = st.x;
 #pragma unroll
@@ -1391,31 +1473,124 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
   const float row_max = M, sum_exp = S;
+  // The region offsets (sh->red_u2 was published by the barriers above).
+  const int rbefore = (int)partials_sum_above_u32(sh->red_u2, -1) -
+                      (int)partials_sum_above_u32(sh->red_u2, warp - 1);
+  if (tid < np) roff[tid] = (uint32_t)(rbefore + rincl - rcount);
+  const int total = (int)partials_sum_above_u32(sh->red_u2, -1);  // candidate groups of the row
+  __syncthreads();
   FTRACE(row, 5);
 
-  const int total = sh->off[31] + sh->cnt[31];
   int n = 0;
   if (k > 0) {
-    if (!(rflags & kRowOverflow) && total >= k) {
-      // Every element of the gathered list is one independent load.
-      const unsigned long long *src = a.row_cand + (int64_t)row * kCandCap;
-      const int cc = chunk_slots(a);
-      for (int i = tid; i < total; i += kThreads) {
-        int c = 0;
-        while (c + 1 < a.nch && sh->off[c + 1] <= i) c++;
-        cand[i] = ld_cg_u64(src + (int64_t)c * cc + (i - sh->off[c]));
+    bool ok = !(rflags & kRowOverflow);
+    if (ok) {
+      // Expand the groups into composites of their logits >= tf. Every group is one
+      // independent pair of loads; a warp reserves its slots with one atomic.
+      if (tid == 0) {
+        sh->count = 0;
+        sh->overflow = 0;
       }
-      n = total;
       __syncthreads();
-    } else {
-      n = rescan_row(rowp, a.vocab, k, cand, hist, sh);
+      const int regsize = region_slots(a);
+      const float4 *gv = a.row_gval + (int64_t)row * kRowGroups;
+      const int32_t *gi = a.row_gidx + (int64_t)row * kRowGroups;
+      // Four groups a thread in flight at once, then their logits >= tf as composites.
+      constexpr int kBatch = 4;
+#ifdef TABBY_TRACE
+      long long tl = 0, tp = 0, tq0;
+#endif
+      for (int r0 = 0; r0 < total; r0 += kBatch * kThreads) {
+#ifdef TABBY_TRACE
+        tq0 = clock64();
+#endif
+        float4 xb[kBatch];
+        int bb[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; j++) {
+          const int i = r0 + j * kThreads + tid;
+          xb[j] = make_float4(kNegSentinel, kNegSentinel, kNegSentinel, kNegSentinel);
+          bb[j] = 0;
+          if (i < total) {
+            // The region holding gathered element i: the last offset <= i.
+            int lo_r = 0, hi_r = np - 1;
+            while (lo_r < hi_r) {
+              const int mid = (lo_r + hi_r + 1) >> 1;
+              if ((int)roff[mid] <= i)
+                lo_r = mid;
+              else
+                hi_r = mid - 1;
+            }
+            const int64_t at = (int64_t)lo_r * regsize + (i - (int)roff[lo_r]);
+            xb[j] = __ldcg(gv + at);
+            bb[j] = __ldcg(gi + at);
+          }
+        }
+#ifdef TABBY_TRACE
+        {
+          float z = 0.f;
+          for (int j = 0; j < kBatch; j++) z += xb[j].x + (float)bb[j];
+          if (z == 1.2345f) sh->flags = 9;
+          tl += clock64() - tq0;
+          tq0 = clock64();
+        }
+#endif
+#pragma unroll
+        for (int j = 0; j < kBatch; j++) {
+          const float4 x = xb[j];
+          const uint32_t hm = (r0 + j * kThreads + tid < total)
+                                  ? ((x.x >= tf ? 1u : 0u) | (x.y >= tf ? 2u : 0u) |
+                                     (x.z >= tf ? 4u : 0u) | (x.w >= tf ? 8u : 0u))
+                                  : 0u;
+          const int nh = __popc(hm);
+          int incl = nh;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+          }
+          const int wtotal = __shfl_sync(0xffffffffu, incl, 31);
+          uint32_t wb = 0;
+          if (lane == 31 && wtotal > 0) wb = atomicAdd(&sh->count, (uint32_t)wtotal);
+          wb = __shfl_sync(0xffffffffu, wb, 31);
+          uint32_t slot = wb + (uint32_t)(incl - nh);
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            if ((hm >> e) & 1u) {
+              const float xe = e == 0 ? x.x : e == 1 ? x.y : e == 2 ? x.z : x.w;
+              if (slot < (uint32_t)kFinishCap)
+                cand[slot] = composite(key_of(xe), (uint32_t)(bb[j] + e));
+              else
+                sh->overflow = 1u;
+              slot++;
+            }
+          }
+        }
+#ifdef TABBY_TRACE
+        tp += clock64() - tq0;
+#endif
+      }
+#ifdef TABBY_TRACE
+      if (tid == 0 && row < 4096) {
+        g_ftrace[row * 8 + 7] = tl;
+        g_fz[row * 8 + 7] = tp;
+      }
+#endif
+      __syncthreads();
+      n = (int)sh->count;
+      ok = sh->overflow == 0u && n >= k;
+      __syncthreads();
     }
+    if (!ok) n = rescan_row(rowp, a.vocab, k, __ldcg(&a.row_tf_lo[row]), cand, hist, sh);
   }
   FTRACE(row, 1);
 #ifdef TABBY_TRACE
-  if (tid == 0 && row < 4096) g_ftrace[row * 8 + 6] = (unsigned long long)n;
+  if (tid == 0 && row < 4096)
+    g_ftrace[row * 8 + 6] = (unsigned long long)n | ((unsigned long long)total << 20) |
+                            ((unsigned long long)rflags << 40) |
+                            ((unsigned long long)(__float_as_uint(tf) >> 16) << 44);
 #endif
-  const int kk = top_sorted(cand, n, k, hist, sh);
+  const int kk = top_sorted(cand, n, k, kFinishCap, hist, sh);
   FTRACE(row, 2);
   const uint32_t flags = (rflags & kFlagBadInput) | pflags;
   const uint32_t status = (flags & kFlagBadInput)    ? (uint32_t)TABBY_EINPUT
@@ -1467,9 +1642,8 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
   // buffer holds the float64 finalize arrays.
   int32_t *ids = reinterpret_cast<int32_t *>(hist);
   float *vals = reinterpret_cast<float *>(ids + kk);
-  double *exact = reinterpret_cast<double *>(cand);
-  double *scaled = exact + kk;
-  double *cum = scaled + kk;
+  double *cum = reinterpret_cast<double *>(cand);
+  double *scaled = cum + kk;  // the replay's work space
   uint64_t mine[2];
   for (int j = 0; j < 2; j++) mine[j] = tid + j * kThreads < kk ? cand[tid + j * kThreads] : 0ull;
   __syncthreads();
@@ -1510,19 +1684,55 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
   if (a.topk_values)
     for (int i = tid; i < kk; i += kThreads) a.topk_values[(int64_t)row * a.topk_ld + i] = vals[i];
   FTRACE(row, 3);
-  finalize_sample(ids, vals, kk, max_logit, sum_exp, prm, uni, exact, scaled, cum, sh,
+  finalize_sample(ids, vals, kk, max_logit, sum_exp, prm, uni, cum, scaled, sh,
                   &a.out[row], status);
   FTRACE(row, 4);
 }
 
+// Packed pair arithmetic of sm_100 (two fp32 lanes in one 64-bit register pair).
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(unsigned long long v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
+                                                     unsigned long long c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// 2^x of both lanes (two MUFU.EX2), packed again.
+__device__ __forceinline__ unsigned long long f2_ex2(unsigned long long v) {
+  float lo, hi;
+  f2_unpack(v, lo, hi);
+  return f2_pack(ex2_approx(lo), ex2_approx(hi));
+}
+
 __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant__ PassArgs a) {
+  // Shared memory: the cp.async stages of the streaming loop; the finish reuses them as
+  // its composite buffer (kFinishCap) followed by the histogram.
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  uint64_t *cand = reinterpret_cast<uint64_t *>(smem_raw);
-  uint32_t *hist = reinterpret_cast<uint32_t *>(cand + kCandCap);
-  Shared *sh = reinterpret_cast<Shared *>(hist + kBins);
+  float4 *stage = reinterpret_cast<float4 *>(smem_raw);  // [kStages][kVec][kThreads]
+  uint64_t *fin = reinterpret_cast<uint64_t *>(smem_raw);
+  uint32_t *hist = reinterpret_cast<uint32_t *>(fin + kFinishCap);
+  Shared *sh = reinterpret_cast<Shared *>(smem_raw + kStageBytes);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int units = a.rows * a.nch;
   constexpr float kLog2e = 1.44269504088896341f;
+  const float kNaN = __int_as_float(0x7fc00000);
   const float4 kPast = make_float4(-3.40282347e38f, -3.40282347e38f, -3.40282347e38f,
                                    -3.40282347e38f);
   // plan_kernel's results (and its reset of the counters) are complete past this point.
@@ -1534,38 +1744,83 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
 #else
 #define NOW() 0ull
 #endif
-  for (;;) {
-    __syncthreads();  // the previous unit is done with the shared state
-    if (tid == 0) {
-      sh->unit = atomicAdd(a.sched, 1u);
-      sh->count = 0;
-      sh->overflow = 0;
+  // Unit pipeline, kept by thread 0: the next unit's id is requested near the end of the
+  // current unit's stream, and its row data travel together with the row's completion
+  // count, so one global round trip separates two units (the unit that completes a row
+  // finishes it at once).
+  int nid = 0, nrow = 0, nk = 0;
+  float ntf = 0.f;
+  if (tid == 0) {
+    nid = (int)atomicAdd(a.sched, 1u);
+    if (nid < units) {
+      const int ri = nid / a.nch;
+      nrow = a.order[ri];
+      nk = a.pos_k[ri];
+      ntf = a.pos_tf[ri];
     }
-    __syncthreads();
+    sh->unit = (uint32_t)nid;
+    sh->urow = nrow;
+    sh->uk = nk;
+    sh->utf = ntf;
+  }
+  __syncthreads();
+  for (;;) {
+    if (sh->unit == 0xffffffffu) {
+      // The previous unit finished a row without asking for its successor: ask now, so
+      // a CTA busy finishing never holds on to a unit other CTAs could take.
+      __syncthreads();
+      if (tid == 0) {
+        nid = (int)atomicAdd(a.sched, 1u);
+        if (nid < units) {
+          const int ri = nid / a.nch;
+          nrow = a.order[ri];
+          nk = a.pos_k[ri];
+          ntf = a.pos_tf[ri];
+        }
+        sh->unit = (uint32_t)nid;
+        sh->urow = nrow;
+        sh->uk = nk;
+        sh->utf = ntf;
+      }
+      __syncthreads();
+    }
     const int unit = (int)sh->unit;
+    const int row = sh->urow;
+    const int k = sh->uk;
+    const float tf = sh->utf;
     if (unit >= units) break;
+    bool fetched = false;  // thread 0: the next unit's id has been requested
 #ifdef TABBY_TRACE
     UTRACE(uj, 0, NOW());
 #endif
     const int ri = unit / a.nch;
     const int chunk = unit - ri * a.nch;
-    const int row = a.order[ri];
-    const int k = a.row_k[row];
-    const float tf = a.row_tf[row];
     const float *rowp = a.logits + (int64_t)row * a.row_stride;
     const int lo = chunk * a.chunk;
     const int hi = min(lo + a.chunk, a.vocab);
     const Span sp = aligned_span(rowp, lo, hi);
     const float4 *p4 = reinterpret_cast<const float4 *>(rowp + sp.a0);
 
-    // Per-thread online statistics: s = sum exp(x - m) as 2^((x - m) * log2(e)).
-    float m = -3.40282347e38f, s = 0.f;
+    // Per-thread online statistics, two packed lanes: s = sum exp(x - m) as
+    // 2^((x - m) * log2(e)).
+    float m = -3.40282347e38f;
+    unsigned long long s2 = 0ull;  // (0.f, 0.f)
     float mL = 0.f;      // rn(m * log2(e)) for the FFMA form of the exponent argument
     bool small = false;  // |m| small enough for the FFMA form
     float mn = 3.40282347e38f;  // running min: catches -inf and the -3e38 sentinel
 
+    // Candidate groups go straight to this warp's region of the row's global list; the
+    // warp counts them (wcnt, warp-uniform). A full region sends the row to the exact
+    // re-filter.
+    const int regsize = region_slots(a);
+    const int64_t region = (int64_t)row * kRowGroups + (int64_t)(chunk * kWarps + warp) * regsize;
+    float4 *rgv = a.row_gval + region;
+    int32_t *rgi = a.row_gidx + region;
+    int wcnt = 0;
+
     // Ragged ends of the chunk: at most 3 logits before a0 and 3 after a1, one per lane
-    // of warp 0.
+    // of warp 0, each kept as a group of its own (the other three slots NaN, which no
+    // threshold admits).
     if (warp == 0) {
       const int e = lane < 4 ? lo + lane : sp.a1 + (lane - 4);
       const bool in = lane < 8 && (lane < 4 ? (e < sp.a0) : (e < hi));
@@ -1575,16 +1830,23 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
         m = rx;
         mL = m * kLog2e;
         small = fabsf(m) <= 16.f;
-        s = 1.f;
+        s2 = f2_pack(1.f, 0.f);
         mn = rx;
       }
-      insert_candidate(in && k > 0 && rx >= tf, composite(key_of(rx), (uint32_t)(in ? e : 0)),
-                       cand, &sh->count, &sh->overflow);
+      const bool take = in && k > 0 && rx >= tf;
+      const uint32_t mask = __ballot_sync(0xffffffffu, take);
+      if (take) {
+        const int slot = wcnt + __popc(mask & ((1u << lane) - 1u));
+        if (slot < regsize) {
+          rgv[slot] = make_float4(rx, kNaN, kNaN, kNaN);
+          rgi[slot] = e;
+        }
+      }
+      wcnt += __popc(mask);
     }
 
     // Warp segments: warp w streams the float4 groups [sg0, sg0 + wn) of the chunk's
-    // aligned middle, 128 groups (2 KB, four 512-byte coalesced loads) an iteration,
-    // the next iteration's loads in flight while one is worked on.
+    // aligned middle, 128 groups (2 KB, four 512-byte coalesced loads) an iteration.
     const int seg = (sp.ngroups + kWarps - 1) / kWarps;
     const int sg0 = min(warp * seg, sp.ngroups);
     const int wn = min(sg0 + seg, sp.ngroups) - sg0;
@@ -1592,21 +1854,51 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
     const float4 *wp = p4 + sg0;
     const int gbase = sp.a0 + 4 * sg0;  // logit index of this warp's first group
 
-    auto load_iter = [&](float4 (&dst)[kVec], int it) {
+    // Iteration it's groups of this thread go to its own slots of stage it % kStages by
+    // cp.async (one commit group an iteration); slots of groups past the segment get
+    // -FLT_MAX instead. They come back into registers once the group has landed.
+    const uint32_t sslot = smem_u32(stage + tid);  // slot (s, q) at + (s * kVec + q) * 8 KB
+    const float4 *gsrc = wp + lane;                // this thread's group of the next issue
+    int inext = 0;                                 // iteration of the next issue
+    // Issues iteration inext into stage S (compile-time) and advances. Slots of groups
+    // past the segment get -FLT_MAX.
+    auto issue = [&](auto SC) {
+      constexpr int S = decltype(SC)::value;
+      if (inext + 1 < wit) {
 #pragma unroll
-      for (int q = 0; q < kVec; q++) {
-        const int g = it * kWarpIter + q * 32 + lane;
-        dst[q] = g < wn ? __ldcs(wp + g) : kPast;
+        for (int q = 0; q < kVec; q++)
+          cp_async16_u32(sslot + (uint32_t)((S * kVec + q) * kThreads * 16), gsrc + q * 32);
+      } else if (inext < wit) {
+        const int rem = wn - inext * kWarpIter - lane;
+#pragma unroll
+        for (int q = 0; q < kVec; q++) {
+          const uint32_t dst = sslot + (uint32_t)((S * kVec + q) * kThreads * 16);
+          if (q * 32 < rem)
+            cp_async16_u32(dst, gsrc + q * 32);
+          else
+            st_shared_f4(dst, kPast);
+        }
       }
+      cp_async_commit();  // one group an iteration, empty past the segment
+      gsrc += kWarpIter;
+      inext++;
     };
-    // Online max / sum-exp over one iteration's 16 values. Groups past the segment hold
-    // -FLT_MAX: they never raise the max and add exp(-huge) = 0 to the sum.
-    auto stats_iter = [&](const float4 (&v)[kVec], int it) -> float {
-      float im = max3f(max3f(v[0].x, v[0].y, v[0].z), max3f(v[0].w, v[1].x, v[1].y),
-                       max3f(v[1].z, v[1].w, v[2].x));
-      im = max3f(im, max3f(v[2].y, v[2].z, v[2].w),
-                 max3f(v[3].x, v[3].y, max3f(v[3].z, v[3].w, im)));
-      if (it + 1 < wit) {
+    // One iteration from stage S: statistics, the refill of the stage, the filter.
+    auto step = [&](auto SC, int it) {
+      constexpr int S = decltype(SC)::value;
+      cp_async_wait_group<kStages - 1>();  // iteration it has landed
+      float4 v[kVec];
+#pragma unroll
+      for (int q = 0; q < kVec; q++)
+        v[q] = ld_shared_f4(sslot + (uint32_t)((S * kVec + q) * kThreads * 16));
+      const bool full = it + 1 < wit;
+      // Group maxima, iteration max and min. Groups past the segment hold -FLT_MAX: they
+      // never raise the max, add exp(-huge) = 0 to the sum and are skipped by the min.
+      float gm[kVec];
+#pragma unroll
+      for (int q = 0; q < kVec; q++) gm[q] = max3f(v[q].x, v[q].y, fmaxf(v[q].z, v[q].w));
+      const float im = max3f(gm[0], gm[1], fmaxf(gm[2], gm[3]));
+      if (full) {
         float l = min3f(min3f(v[0].x, v[0].y, v[0].z), min3f(v[0].w, v[1].x, v[1].y),
                         min3f(v[1].z, v[1].w, v[2].x));
         l = min3f(l, min3f(v[2].y, v[2].z, v[2].w),
@@ -1618,8 +1910,14 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
           if (it * kWarpIter + q * 32 + lane < wn)
             mn = min3f(mn, min3f(v[q].x, v[q].y, v[q].z), v[q].w);
       }
+#ifdef TABBY_KNOB_NOSTATS
+      if (im == 1.2345f) sh->flags = 3;
+      if (false) {
+#else
       if (im > m) {
-        s *= ex2_approx((m - im) * kLog2e);
+#endif
+        const float r = ex2_approx((m - im) * kLog2e);
+        s2 = f2_mul(s2, f2_pack(r, r));
         m = im;
         mL = m * kLog2e;
         // fma(x, L, -rn(m*L)) differs from (x - m)*L by the rounding of m*L, at most
@@ -1627,84 +1925,104 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
         // inside the 1e-5 budget). Larger |m| uses the subtraction form.
         small = fabsf(m) <= 16.f;
       }
+#ifdef TABBY_KNOB_NOSTATS
+      if (false) {
+#else
       if (small) {
+#endif
+        const unsigned long long L2 = f2_pack(kLog2e, kLog2e), nmL2 = f2_pack(-mL, -mL);
 #pragma unroll
-        for (int q = 0; q < kVec; q++)
-          s += (ex2_approx(fmaf(v[q].x, kLog2e, -mL)) + ex2_approx(fmaf(v[q].y, kLog2e, -mL))) +
-               (ex2_approx(fmaf(v[q].z, kLog2e, -mL)) + ex2_approx(fmaf(v[q].w, kLog2e, -mL)));
-      } else {
+        for (int q = 0; q < kVec; q++) {
+          const unsigned long long e01 = f2_ex2(f2_fma(f2_pack(v[q].x, v[q].y), L2, nmL2));
+          const unsigned long long e23 = f2_ex2(f2_fma(f2_pack(v[q].z, v[q].w), L2, nmL2));
+          s2 = f2_add(s2, f2_add(e01, e23));
+        }
+      } else
+#ifdef TABBY_KNOB_NOSTATS
+      if (false)
+#endif
+      {
+        const unsigned long long L2 = f2_pack(kLog2e, kLog2e), nm2 = f2_pack(-m, -m);
 #pragma unroll
-        for (int q = 0; q < kVec; q++)
-          s += (ex2_approx((v[q].x - m) * kLog2e) + ex2_approx((v[q].y - m) * kLog2e)) +
-               (ex2_approx((v[q].z - m) * kLog2e) + ex2_approx((v[q].w - m) * kLog2e));
-      }
-      return im;
-    };
-    // Appends this iteration's logits >= tf (warp-uniform call). Slots past kCandCap are
-    // not written; the overflow flag sends the row to the exact re-filter.
-    auto filter_iter = [&](const float4 (&v)[kVec], int it, float im) {
-      if (!__any_sync(0xffffffffu, im >= tf)) return;
-      uint32_t hm = 0;
-#pragma unroll
-      for (int q = 0; q < kVec; q++) {
-        if (it * kWarpIter + q * 32 + lane < wn) {
-          hm |= (v[q].x >= tf ? 1u : 0u) << (4 * q);
-          hm |= (v[q].y >= tf ? 2u : 0u) << (4 * q);
-          hm |= (v[q].z >= tf ? 4u : 0u) << (4 * q);
-          hm |= (v[q].w >= tf ? 8u : 0u) << (4 * q);
+        for (int q = 0; q < kVec; q++) {
+          const unsigned long long e01 =
+              f2_ex2(f2_mul(f2_add(f2_pack(v[q].x, v[q].y), nm2), L2));
+          const unsigned long long e23 =
+              f2_ex2(f2_mul(f2_add(f2_pack(v[q].z, v[q].w), nm2), L2));
+          s2 = f2_add(s2, f2_add(e01, e23));
         }
       }
-      const int nh = __popc(hm);
-      int incl = nh;
+      issue(SC);  // refills stage S (its values are in registers and in use above)
+#ifndef TABBY_KNOB_NOFILTER
+      // Groups holding a logit >= tf go to the warp's region whole (the value check per
+      // logit happens in the finish).
+      if (k > 0 && __any_sync(0xffffffffu, im >= tf)) {
+        uint32_t hg = 0;
+        const int rem = full ? kWarpIter : wn - it * kWarpIter - lane;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += t;
-      }
-      const int wtotal = __shfl_sync(0xffffffffu, incl, 31);
-      if (wtotal == 0) return;
-      uint32_t wb = 0;
-      if (lane == 31) wb = atomicAdd(&sh->count, (uint32_t)wtotal);
-      wb = __shfl_sync(0xffffffffu, wb, 31);
-      uint32_t slot = wb + (uint32_t)(incl - nh);
+        for (int q = 0; q < kVec; q++) hg |= (gm[q] >= tf && q * 32 < rem) ? (1u << q) : 0u;
+        const int nh = __popc(hg);
+        int incl = nh;
 #pragma unroll
-      for (int q = 0; q < kVec; q++) {
-        const uint32_t gb = (hm >> (4 * q)) & 15u;
-        if (gb) {
-          const float xs[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
-          const int base_idx = gbase + 4 * (it * kWarpIter + q * 32 + lane);
+        for (int o = 1; o < 32; o <<= 1) {
+          const int t = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += t;
+        }
+        int slot = wcnt + incl - nh;
+        const int base0 = gbase + 4 * (it * kWarpIter + lane);
 #pragma unroll
-          for (int e = 0; e < 4; e++) {
-            if ((gb >> e) & 1u) {
-              if (slot < (uint32_t)kCandCap)
-                cand[slot] = composite(key_of(xs[e]), (uint32_t)(base_idx + e));
-              else
-                sh->overflow = 1u;
-              slot++;
+        for (int q = 0; q < kVec; q++) {
+          if ((hg >> q) & 1u) {
+            if (slot < regsize) {
+              rgv[slot] = v[q];
+              rgi[slot] = base0 + 4 * 32 * q;
             }
+            slot++;
           }
         }
+        wcnt += __shfl_sync(0xffffffffu, incl, 31);
       }
+#endif
     };
-
-    float4 v[kVec], nx[kVec];
-    if (wit > 0) load_iter(v, 0);
-    if (wit > 1) load_iter(nx, 1);
-    for (int it = 0; it < wit; it++) {
-      if (it > 0) {
+    using I0 = std::integral_constant<int, 0>;
+    using I1 = std::integral_constant<int, 1>;
+    using I2 = std::integral_constant<int, 2>;
+    static_assert(kStages == 3, "the loop below is unrolled for three stages");
+    issue(I0{});
+    issue(I1{});
+    issue(I2{});
+    // Thread 0 asks for the next unit two iterations before its segment ends, so the id
+    // is there at the end of this unit while the schedule stays dynamic.
+    // The last chunk of a row usually completes it; that unit asks after its finish.
+#if TABBY_PREFETCH
+    const int fetch_it = chunk == a.nch - 1 ? 0x7fffffff : max(wit - 2, 0);
+#else
+    const int fetch_it = 0x7fffffff;
+#endif
+    for (int it = 0; it < wit; it += kStages) {
 #pragma unroll
-        for (int q = 0; q < kVec; q++) v[q] = nx[q];
-        if (it + 1 < wit) load_iter(nx, it + 1);
+      for (int j = 0; j < kStages; j++) {
+        if (it + j < wit) {
+          if (tid == 0 && it + j == fetch_it) {
+            nid = (int)atomicAdd(a.sched, 1u);
+            fetched = true;
+          }
+          if (j == 0) step(I0{}, it);
+          if (j == 1) step(I1{}, it + 1);
+          if (j == 2) step(I2{}, it + 2);
+        }
       }
-      const float im = stats_iter(v, it);
-      if (k > 0) filter_iter(v, it, im);
     }
-
+    cp_async_wait_group<0>();
 #ifdef TABBY_TRACE
     UTRACE(uj, 1, NOW());
 #endif
+
     // Per-warp statistics into the row's table.
     {
+      float s_lo, s_hi;
+      f2_unpack(s2, s_lo, s_hi);
+      const float s = s_lo + s_hi;
       float wm = m;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, o));
@@ -1717,33 +2035,47 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
                        !(s <= 3.40282347e38f);
       const bool wbad = __any_sync(0xffffffffu, bad);
       if (lane == 0) {
-        a.warp_stats[((int64_t)row * a.nch + chunk) * kWarps + warp] = make_float2(wm, ws);
-        if (wbad) atomicOr(&a.row_flags[row], kFlagBadInput);
+        const int64_t at = ((int64_t)row * a.nch + chunk) * kWarps + warp;
+        a.warp_stats[at] = make_float2(wm, ws);
+        a.warp_cnt[at] = (uint32_t)min(wcnt, regsize);
+        const uint32_t f = (wbad ? kFlagBadInput : 0u) | (wcnt > regsize ? kRowOverflow : 0u);
+        if (f) atomicOr(&a.row_flags[row], f);
       }
     }
-    __syncthreads();
-    // The chunk's candidates into its slots of the row's list.
-    const uint32_t cnt = sh->count;
-    const int cc = chunk_slots(a);
-    const bool fits = sh->overflow == 0u && cnt <= (uint32_t)cc;
+    __syncthreads();  // every thread's candidate groups and statistics are written
     if (tid == 0) {
-      a.chunk_cnt[row * a.nch + chunk] = fits ? cnt : 0u;
-      if (!fits) atomicOr(&a.row_flags[row], kRowOverflow);
+      __threadfence();  // ... and visible before the count (release)
+      const uint32_t done = atomicAdd(&a.row_done[row], 1u);
+      const bool last = done == (uint32_t)(a.nch - 1);
+#if TABBY_PREFETCH
+      if (!fetched && !last) nid = (int)atomicAdd(a.sched, 1u);
+#else
+      if (!last) nid = (int)atomicAdd(a.sched, 1u);
+#endif
+      if ((fetched || !last) && nid < units) {  // the next unit's row data
+        const int ri = nid / a.nch;
+        nrow = a.order[ri];
+        nk = a.pos_k[ri];
+        ntf = a.pos_tf[ri];
+      }
+      sh->last = last ? 1u : 0u;
+      sh->unit = (fetched || !last) ? (uint32_t)nid : 0xffffffffu;
+      sh->urow = nrow;
+      sh->uk = nk;
+      sh->utf = ntf;
     }
-    if (fits) {
-      unsigned long long *dst = a.row_cand + (int64_t)row * kCandCap + (int64_t)chunk * cc;
-      for (int i = tid; i < (int)cnt; i += kThreads) dst[i] = cand[i];
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) sh->last = atomicAdd(&a.row_done[row], 1u) == (uint32_t)(a.nch - 1) ? 1u : 0u;
     __syncthreads();
 #ifdef TABBY_TRACE
     UTRACE(uj, 2, NOW());
 #endif
+#ifdef TABBY_KNOB_NOFINISH
+    if (false) {
+#else
     if (sh->last) {
+#endif
       __threadfence();
-      finish_row(a, row, k, cand, hist, sh);
+      finish_row(a, row, k, fin, hist, sh);
+      __syncthreads();  // the finish is done with the stage region before the loads reuse it
 #ifdef TABBY_TRACE
       UTRACE(uj, 3, NOW());
 #endif
@@ -1832,7 +2164,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch a) {
   if (a.topk_values)
     for (int i = tid; i < kk; i += kMergeThreads)
       a.topk_values[(int64_t)row * a.topk_ld + i] = vals[i];
-  finalize_sample(ids, vals, kk, max_logit, sh->merge_sum, p, a.uniforms[row], exact, scaled, cum,
+  finalize_sample(ids, vals, kk, max_logit, sh->merge_sum, p, a.uniforms[row], cum, scaled,
                   sh, &a.out[row], status);
 }
 
@@ -1842,12 +2174,15 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch a) {
 static int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
 static size_t row_smem_bytes() {
-  return (size_t)kCandCap * 8 + (size_t)kBins * 4 + sizeof(Shared) + 64;
+  return (size_t)kStageBytes + sizeof(Shared) + 64;
 }
 
 // Units a CTA should see on average: enough for the dynamic schedule to even out the
 // CTAs' speeds, few enough that the per-unit overhead stays small.
-constexpr int kUnitsPerCta = 3;
+#ifndef TABBY_UNITS_PER_CTA
+#define TABBY_UNITS_PER_CTA 3
+#endif
+constexpr int kUnitsPerCta = TABBY_UNITS_PER_CTA;
 
 cudaError_t plan_rows(int32_t sms, int32_t rows, int32_t vocab, int32_t cap, RowGeometry *geo) {
   (void)cap;
@@ -1900,13 +2235,16 @@ cudaError_t launch_rows(const RowLaunch &l, const RowGeometry &geo, const Scratc
   a.block_ld = l.block_ld;
   a.sched = scr.sched;
   a.row_done = scr.row_done;
-  a.chunk_cnt = scr.chunk_cnt;
+  a.warp_cnt = scr.warp_cnt;
   a.row_flags = scr.row_flags;
   a.row_tf = scr.row_tf;
-  a.row_k = scr.row_k;
+  a.row_tf_lo = scr.row_tf_lo;
+  a.pos_tf = scr.pos_tf;
+  a.pos_k = scr.pos_k;
   a.order = scr.order;
   a.warp_stats = scr.warp_stats;
-  a.row_cand = scr.row_cand;
+  a.row_gval = scr.row_gval;
+  a.row_gidx = scr.row_gidx;
   cudaError_t err = prepare_row_kernel(geo.smem_bytes);
   if (err != cudaSuccess) return err;
   plan_kernel<<<l.rows, kThreads, 0, stream>>>(a);
@@ -1923,7 +2261,11 @@ cudaError_t launch_rows(const RowLaunch &l, const RowGeometry &geo, const Scratc
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
+#ifdef TABBY_KNOB_NOPDL
+  cfg.numAttrs = 0;
+#else
   cfg.numAttrs = 1;
+#endif
   return cudaLaunchKernelEx(&cfg, row_kernel, a);
 }
 
@@ -1941,11 +2283,8 @@ int host_sample_from_topk(const int32_t *ids, const float *logits, int32_t n, fl
   if (n <= 0) return TABBY_EEMPTY;
   double *exact = new double[n];
   double *scaled = new double[n];
-  for (int32_t i = 0; i < n; i++) {
-    exact[i] = exact_prob(logits[i], max_logit, sum_exp);
-    scaled[i] = temperature > 0 ? scaled_weight(logits[i], max_logit, temperature) : 0.0;
-  }
-  const Decision d = decide_sequential(exact, scaled, scaled, n, temperature, top_p, u);
+  for (int32_t i = 0; i < n; i++) exact[i] = exact_prob(logits[i], max_logit, sum_exp);
+  const Decision d = decide_sequential(logits, n, max_logit, sum_exp, temperature, top_p, u, scaled);
   out->id = ids[d.chosen];
   out->considered_count = d.cut;
   out->probability = exact[d.chosen];
@@ -1976,6 +2315,12 @@ extern "C" __attribute__((visibility("default"))) int tabby_debug_utrace(unsigne
 }
 extern "C" __attribute__((visibility("default"))) int tabby_debug_ftrace(unsigned long long *f) {
   return (int)cudaMemcpyFromSymbol(f, tabby::g_ftrace, sizeof(tabby::g_ftrace));
+}
+extern "C" __attribute__((visibility("default"))) int tabby_debug_fz(unsigned long long *f) {
+  return (int)cudaMemcpyFromSymbol(f, tabby::g_fz, sizeof(tabby::g_fz));
+}
+extern "C" __attribute__((visibility("default"))) int tabby_debug_lcyc(unsigned long long *f) {
+  return (int)cudaMemcpyFromSymbol(f, tabby::g_lcyc, sizeof(tabby::g_lcyc));
 }
 extern "C" __attribute__((visibility("default"))) int tabby_debug_pphase(unsigned long long *f) {
   return (int)cudaMemcpyFromSymbol(f, tabby::g_pphase, sizeof(tabby::g_pphase));

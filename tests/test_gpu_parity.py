@@ -280,7 +280,7 @@ def test_seeded_determinism(torch_cuda):
 
 @pytest.mark.parametrize("rows", [2, 256])
 def test_threshold_estimate_failures(torch_cuda, oracle, rows):
-    """Rows built so the threshold estimated from the 512 float4 groups sampled evenly
+    """Rows built so the threshold estimated from the 1024 float4 groups sampled evenly
     over the row is wrong in both directions: too high (the sampled groups hold the
     largest logits, so fewer than k logits pass) and too low (they hold the smallest,
     so the candidates overflow the row's list). Both must end in the exact result
@@ -289,8 +289,8 @@ def test_threshold_estimate_failures(torch_cuda, oracle, rows):
     vocab = 151936
     ngroups = vocab // 4
     sampled = np.zeros(vocab, bool)
-    for i in range(512):
-        grp = (2 * i + 1) * ngroups // 1024
+    for i in range(1024):
+        grp = (2 * i + 1) * ngroups // 2048
         sampled[4 * grp:4 * grp + 4] = True
     x = g.standard_normal((rows, vocab)).astype(np.float32)
     x[0::2, sampled] += 20.0   # too-high estimate
