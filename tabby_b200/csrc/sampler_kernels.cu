@@ -7,7 +7,7 @@
 //
 //   plan_kernel    one CTA per row: resets the row's counters, fixes its pool size and
 //                  its place in the processing order, and estimates a filter threshold
-//                  from 4096 logits sampled evenly over the row.
+//                  from 2048 logits sampled in 32 runs spread over the row.
 //   row_kernel     persistent, two 512-thread CTAs per SM taking (row, chunk) units from
 //                  a global counter. Each warp streams its part of the chunk straight
 //                  into registers (four 16-byte loads in flight a thread, the next
@@ -1159,8 +1159,8 @@ __device__ __forceinline__ int top_sorted(uint64_t *cand, int n, int k, int capa
 //
 // plan_kernel (one CTA a row) resets the row's counters, fixes its pool size k and its
 // place in the processing order (rows with pools above 64 first, so that the rows whose
-// finish is cheap come last), and estimates a threshold from a sample of 1024 float4
-// groups spread over the row: a logit with about rr sample logits at or above it, rr
+// finish is cheap come last), and estimates a threshold from a sample of 512 float4
+// groups in 32 runs spread over the row: a logit with about rr sample logits at or above it, rr
 // chosen so that the row holds at least k logits at or above it with near certainty
 // (rr = mu + 3 sqrt(mu) + 4, mu the expected sample count above the row's k-th largest).
 //
@@ -1293,7 +1293,11 @@ __global__ void __launch_bounds__(kThreads) plan_kernel(const __grid_constant__ 
   }
   // The sample: 512 float4 groups spread evenly over the aligned middle of the row.
   const Span sp = aligned_span(rowp, 0, a.vocab);
+  // The sample: kPlanRuns runs of kPlanRun consecutive float4 groups (256 contiguous
+  // bytes, whole DRAM bursts), spread evenly over the aligned middle of the row.
   constexpr int kPlanSample = TABBY_PLAN_GROUPS * kThreads;  // float4 groups sampled
+  constexpr int kPlanRun = 16;
+  constexpr int kPlanRuns = kPlanSample / kPlanRun;
   const int S = min(kPlanSample, sp.ngroups);
   uint64_t t1 = 0, t2 = 0;
   if (k > 0) {
@@ -1301,7 +1305,14 @@ __global__ void __launch_bounds__(kThreads) plan_kernel(const __grid_constant__ 
     for (int j = 0; j < kPlanSample / kThreads; j++) {
       const int i = j * kThreads + tid;
       if (i < S) {
-        const int g = (int)(((2LL * i + 1) * sp.ngroups) / (2LL * S));
+        int g;
+        if (S == kPlanSample) {
+          const int run = i / kPlanRun;
+          const int start = (int)(((2LL * run + 1) * sp.ngroups) / (2LL * kPlanRuns)) - kPlanRun / 2;
+          g = max(0, min(start, sp.ngroups - kPlanRun)) + i % kPlanRun;
+        } else {
+          g = i;  // short rows: every group
+        }
         const float4 v = __ldg(reinterpret_cast<const float4 *>(rowp + sp.a0) + g);
         const float xs[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll

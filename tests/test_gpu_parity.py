@@ -280,18 +280,18 @@ def test_seeded_determinism(torch_cuda):
 
 @pytest.mark.parametrize("rows", [2, 256])
 def test_threshold_estimate_failures(torch_cuda, oracle, rows):
-    """Rows built so the threshold estimated from the 1024 float4 groups sampled evenly
-    over the row is wrong in both directions: too high (the sampled groups hold the
-    largest logits, so fewer than k logits pass) and too low (they hold the smallest,
-    so the candidates overflow the row's list). Both must end in the exact result
-    through the re-filter."""
+    """Rows built so the threshold estimated from the plan's sample (512 float4 groups in
+    32 runs of 16 spread over the row) is wrong in both directions: too high (the sampled
+    groups hold the largest logits, so fewer than k logits pass) and too low (they hold the
+    smallest, so the candidates overflow the row's list). Both must end in the exact result
+    through the re-filter. Small batches split rows into more chunks than 256 rows do."""
     g = np.random.default_rng(17)
     vocab = 151936
     ngroups = vocab // 4
     sampled = np.zeros(vocab, bool)
-    for i in range(1024):
-        grp = (2 * i + 1) * ngroups // 2048
-        sampled[4 * grp:4 * grp + 4] = True
+    for run in range(32):
+        start = min(max((2 * run + 1) * ngroups // 64 - 8, 0), ngroups - 16)
+        sampled[4 * start:4 * (start + 16)] = True
     x = g.standard_normal((rows, vocab)).astype(np.float32)
     x[0::2, sampled] += 20.0   # too-high estimate
     x[1::2, sampled] -= 20.0   # too-low estimate
