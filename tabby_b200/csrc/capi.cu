@@ -29,6 +29,7 @@ struct tabby_sampler {
   int32_t sms;
   Scratch scratch;     // per-row state of the row pass, carved from scratch_mem
   void *scratch_mem;
+  uint32_t epoch;      // launches on the scratch so far (the next launch is epoch + 1)
   cudaStream_t stream;  // used by the host-buffer entry points
   float *d_logits;
   tabby_sampling_params *d_params;
@@ -93,7 +94,7 @@ int check_params_host(const tabby_sampling_params *p, int32_t rows) {
 }
 
 // Launches the row kernel over `rows` rows in batches of the scratch capacity.
-cudaError_t plan_and_launch(const tabby_sampler *s, const RowLaunch &l, cudaStream_t stream) {
+cudaError_t plan_and_launch(tabby_sampler *s, const RowLaunch &l, cudaStream_t stream) {
   for (int32_t r0 = 0; r0 < l.rows; r0 += s->scratch.max_rows) {
     RowLaunch b = l;
     b.rows = std::min(l.rows - r0, s->scratch.max_rows);
@@ -107,6 +108,8 @@ cudaError_t plan_and_launch(const tabby_sampler *s, const RowLaunch &l, cudaStre
     RowGeometry geo;
     cudaError_t err = tabby::plan_rows(s->sms, b.rows, b.vocab, s->cap, &geo);
     if (err != cudaSuccess) return err;
+    s->epoch = s->epoch + 1 == 0 ? 1 : s->epoch + 1;
+    b.epoch = s->epoch;
     err = tabby::launch_rows(b, geo, s->scratch, stream);
     if (err != cudaSuccess) return err;
   }
@@ -184,6 +187,7 @@ int tabby_sampler_create(const tabby_sampler_config *config, tabby_sampler **out
       (err = cudaMalloc(&s->d_values, (size_t)c.max_rows * c.max_top_k * sizeof(float))) !=
           cudaSuccess ||
       (err = cudaMalloc(&s->scratch_mem, Scratch::bytes(scratch_rows))) != cudaSuccess ||
+      (err = cudaMemset(s->scratch_mem, 0, Scratch::bytes(scratch_rows))) != cudaSuccess ||
       (err = cudaDeviceSynchronize()) != cudaSuccess) {
     tabby_sampler_destroy(s);
     cudaGetLastError();

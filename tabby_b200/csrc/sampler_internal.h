@@ -32,6 +32,7 @@ struct RowLaunch {
   int32_t topk_ld = 0;
   float *block = nullptr;
   int32_t block_ld = 0;
+  uint32_t epoch = 1;  // launch number on this scratch, never 0 (see Scratch)
 };
 
 struct MergeLaunch {
@@ -61,10 +62,13 @@ constexpr int32_t kScratchChunks = 32;        // chunks a row may have (kMaxChun
 constexpr int32_t kScratchWarps = 16;         // warps a CTA has
 
 // Global scratch of the row pass for up to max_rows rows, carved from one device
-// allocation (every section 256-byte aligned). plan_kernel resets the counters of the
-// rows it plans, so no clearing is needed between launches.
+// allocation (every section 256-byte aligned). It must be zero when first used; after
+// that every launch resets the row counters it plans and the unit counter of the next
+// launch, and tags its plan entries with its epoch (the caller's launch count on this
+// scratch, starting at 1 and never 0), so no clearing is needed between launches.
 struct Scratch {
-  uint32_t *sched = nullptr;                 // [1] unit counter
+  uint32_t *sched = nullptr;                 // [2] unit counters (by launch parity)
+  uint32_t *ready = nullptr;                 // [max_rows] launch epoch once planned
   uint32_t *row_done = nullptr;              // [max_rows] chunks finished
   uint32_t *warp_cnt = nullptr;              // [max_rows][kScratchChunks * kScratchWarps]
   uint32_t *row_flags = nullptr;             // [max_rows] bad input / overflow
@@ -80,7 +84,7 @@ struct Scratch {
 
   static constexpr size_t section(size_t bytes) { return (bytes + 255) / 256 * 256; }
   static constexpr size_t layout_bytes(int32_t rows) {
-    return section(4) + 7 * section(4 * (size_t)rows) +
+    return section(8) + 8 * section(4 * (size_t)rows) +
            section(4 * (size_t)rows * kScratchChunks * kScratchWarps) +
            section(8 * (size_t)rows * kScratchChunks * kScratchWarps) +
            section(16 * (size_t)rows * kScratchGroups) + section(4 * (size_t)rows * kScratchGroups);
@@ -91,7 +95,9 @@ struct Scratch {
     unsigned char *p = static_cast<unsigned char *>(base);
     const size_t r = (size_t)rows;
     s.sched = reinterpret_cast<uint32_t *>(p);
-    p += section(4);
+    p += section(8);
+    s.ready = reinterpret_cast<uint32_t *>(p);
+    p += section(4 * r);
     s.row_done = reinterpret_cast<uint32_t *>(p);
     p += section(4 * r);
     s.warp_cnt = reinterpret_cast<uint32_t *>(p);

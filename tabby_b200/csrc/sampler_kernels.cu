@@ -5,7 +5,8 @@
 // topk_partial + topk_select, i.e. k+4 passes over the row. Here every logit is read
 // from HBM once, in one streaming pass:
 //
-//   plan_kernel    one CTA per row: resets the row's counters, fixes its pool size and
+//   plan_row       one CTA per row, first phase of row_kernel: resets the row's counters,
+//                  fixes its pool size and
 //                  its place in the processing order, and estimates a filter threshold
 //                  from 2048 logits sampled in 32 runs spread over the row.
 //   row_kernel     persistent, two 512-thread CTAs per SM taking (row, chunk) units from
@@ -210,6 +211,14 @@ __device__ __forceinline__ float4 ld_shared_f4(uint32_t src) {
                : "memory");
   return v;
 }
+__device__ __forceinline__ void st_release_u32(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 template <int N>
 __device__ __forceinline__ void cp_async_wait_group() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
@@ -263,6 +272,7 @@ struct Shared {
   uint32_t last;  // this CTA finishes the row
   uint32_t unit;  // the unit this CTA works on
   int32_t urow, uk;  // its row and pool size
+  int32_t plan_red[3][kWarps];  // plan: per-warp counts for the row order
   float utf;         // its threshold
   int32_t trace_row;  // row being finished (tuning traces only)
   uint32_t base;  // where the unit's candidates go in the row's list
@@ -1155,9 +1165,9 @@ __device__ __forceinline__ int top_sorted(uint64_t *cand, int n, int k, int capa
 }
 
 // ------------------------------------------------------------------------------------
-// The row pass: plan_kernel, then row_kernel.
+// The row pass: one cooperative row_kernel launch, a plan phase then the units.
 //
-// plan_kernel (one CTA a row) resets the row's counters, fixes its pool size k and its
+// plan_row (one CTA a row) resets the row's counters, fixes its pool size k and its
 // place in the processing order (rows with pools above 64 first, so that the rows whose
 // finish is cheap come last), and estimates a threshold from a sample of 512 float4
 // groups in 32 runs spread over the row: a logit with about rr sample logits at or above it, rr
@@ -1187,7 +1197,9 @@ struct PassArgs {
   int32_t topk_ld;
   float *block;
   int32_t block_ld;
-  uint32_t *sched;       // unit counter
+  uint32_t *sched;       // [2] unit counters; launch e uses sched[e & 1], clears the other
+  uint32_t *ready;       // [rows] = epoch once the row at that position is planned
+  uint32_t epoch;        // this launch's number (never 0)
   uint32_t *row_done;    // [rows] chunks finished
   uint32_t *warp_cnt;    // [rows][nch * kWarps] candidate groups of each (chunk, warp)
   uint32_t *row_flags;   // [rows] kFlagBadInput | kRowOverflow
@@ -1251,16 +1263,14 @@ __device__ __forceinline__ Span aligned_span(const float *rowp, int lo, int hi) 
   return s;
 }
 
-__global__ void __launch_bounds__(kThreads) plan_kernel(const __grid_constant__ PassArgs a) {
-  __shared__ uint64_t cand[4 * kThreads];  // 1024 sample slots and room to rank them
-  __shared__ uint32_t hist[kBins];
-  __shared__ Shared sh_s;
-  __shared__ int red[3][kWarps];
-  Shared *sh = &sh_s;
-  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+// Plans one row (block-uniform call): resets its counters, fixes its pool size and its
+// place in the processing order, estimates its threshold, then publishes the row's
+// position entry with ready[pos] = epoch (release). cand holds 2048 slots.
+__device__ __noinline__ void plan_row(const PassArgs &a, int row, uint64_t *cand,
+                                      uint32_t *hist, Shared *sh) {
+  int (*red)[kWarps] = sh->plan_red;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float *rowp = a.logits + (int64_t)row * a.row_stride;
-  // The row kernel may start launching now; it waits for this grid's results.
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   PPHASE(row, 0);
   uint32_t pf = 0;
 #ifdef TABBY_TRACE
@@ -1270,7 +1280,6 @@ __global__ void __launch_bounds__(kThreads) plan_kernel(const __grid_constant__ 
   if (tid == 0) {
     a.row_done[row] = 0;
     a.row_flags[row] = 0;
-    if (row == 0) *a.sched = 0;
   }
   // Place in the order: rows with k > 64 first, each group in row order.
   int large = 0, large_before = 0, small_before = 0;
@@ -1291,7 +1300,6 @@ __global__ void __launch_bounds__(kThreads) plan_kernel(const __grid_constant__ 
     red[1][warp] = large_before;
     red[2][warp] = small_before;
   }
-  // The sample: 512 float4 groups spread evenly over the aligned middle of the row.
   const Span sp = aligned_span(rowp, 0, a.vocab);
   // The sample: kPlanRuns runs of kPlanRun consecutive float4 groups (256 contiguous
   // bytes, whole DRAM bursts), spread evenly over the aligned middle of the row.
@@ -1373,7 +1381,10 @@ __global__ void __launch_bounds__(kThreads) plan_kernel(const __grid_constant__ 
     a.pos_tf[pos] = tf;
     a.row_tf[row] = tf;
     a.row_tf_lo[row] = tf_lo;
+    __threadfence();
+    st_release_u32(&a.ready[pos], a.epoch);
   }
+  __syncthreads();  // the slots and sh are free again
 #ifdef TABBY_TRACE
   if (tid == 0 && row < 4096) g_ptrace[row * 2 + 1] = globaltimer();
 #endif
@@ -1746,8 +1757,13 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
   const float kNaN = __int_as_float(0x7fc00000);
   const float4 kPast = make_float4(-3.40282347e38f, -3.40282347e38f, -3.40282347e38f,
                                    -3.40282347e38f);
-  // plan_kernel's results (and its reset of the counters) are complete past this point.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Plan phase: every CTA plans rows blockIdx.x, blockIdx.x + gridDim.x, ... and
+  // publishes each with ready[pos] = epoch; a unit waits only for its own row's entry, so
+  // streaming starts as soon as the first rows are planned. The launch is cooperative:
+  // every CTA is resident, so every awaited row gets planned.
+  if (blockIdx.x == 0 && tid == 0) a.sched[(a.epoch + 1) & 1] = 0;  // the next launch's
+  uint32_t *sched = a.sched + (a.epoch & 1);
+  for (int r = blockIdx.x; r < a.rows; r += gridDim.x) plan_row(a, r, fin, hist, sh);
 
 #ifdef TABBY_TRACE
   int uj = 0;
@@ -1761,14 +1777,26 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
   // finishes it at once).
   int nid = 0, nrow = 0, nk = 0;
   float ntf = 0.f;
-  if (tid == 0) {
-    nid = (int)atomicAdd(a.sched, 1u);
-    if (nid < units) {
-      const int ri = nid / a.nch;
-      nrow = a.order[ri];
-      nk = a.pos_k[ri];
-      ntf = a.pos_tf[ri];
+  // Thread 0: the row data of unit nid, once its row is planned (bounded wait; a wait
+  // that runs out ends this CTA's work, leaving the unit undone).
+  auto unit_info = [&]() {
+    if (nid >= units) return;
+    const int ri = nid / a.nch;
+    uint32_t spins = 0;
+    while (ld_acquire_u32(&a.ready[ri]) != a.epoch) {
+      if (++spins > (1u << 24)) {
+        nid = units;
+        return;
+      }
+      __nanosleep(100);
     }
+    nrow = a.order[ri];
+    nk = a.pos_k[ri];
+    ntf = a.pos_tf[ri];
+  };
+  if (tid == 0) {
+    nid = (int)atomicAdd(sched, 1u);
+    unit_info();
     sh->unit = (uint32_t)nid;
     sh->urow = nrow;
     sh->uk = nk;
@@ -1781,13 +1809,8 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
       // a CTA busy finishing never holds on to a unit other CTAs could take.
       __syncthreads();
       if (tid == 0) {
-        nid = (int)atomicAdd(a.sched, 1u);
-        if (nid < units) {
-          const int ri = nid / a.nch;
-          nrow = a.order[ri];
-          nk = a.pos_k[ri];
-          ntf = a.pos_tf[ri];
-        }
+        nid = (int)atomicAdd(sched, 1u);
+        unit_info();
         sh->unit = (uint32_t)nid;
         sh->urow = nrow;
         sh->uk = nk;
@@ -2015,7 +2038,7 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
       for (int j = 0; j < kStages; j++) {
         if (it + j < wit) {
           if (tid == 0 && it + j == fetch_it) {
-            nid = (int)atomicAdd(a.sched, 1u);
+            nid = (int)atomicAdd(sched, 1u);
             fetched = true;
           }
           if (j == 0) step(I0{}, it);
@@ -2059,16 +2082,11 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
       const uint32_t done = atomicAdd(&a.row_done[row], 1u);
       const bool last = done == (uint32_t)(a.nch - 1);
 #if TABBY_PREFETCH
-      if (!fetched && !last) nid = (int)atomicAdd(a.sched, 1u);
+      if (!fetched && !last) nid = (int)atomicAdd(sched, 1u);
 #else
-      if (!last) nid = (int)atomicAdd(a.sched, 1u);
+      if (!last) nid = (int)atomicAdd(sched, 1u);
 #endif
-      if ((fetched || !last) && nid < units) {  // the next unit's row data
-        const int ri = nid / a.nch;
-        nrow = a.order[ri];
-        nk = a.pos_k[ri];
-        ntf = a.pos_tf[ri];
-      }
+      if (fetched || !last) unit_info();  // the next unit's row data
       sh->last = last ? 1u : 0u;
       sh->unit = (fetched || !last) ? (uint32_t)nid : 0xffffffffu;
       sh->urow = nrow;
@@ -2195,9 +2213,24 @@ static size_t row_smem_bytes() {
 #endif
 constexpr int kUnitsPerCta = TABBY_UNITS_PER_CTA;
 
+static cudaError_t prepare_row_kernel(size_t smem_bytes);
+
 cudaError_t plan_rows(int32_t sms, int32_t rows, int32_t vocab, int32_t cap, RowGeometry *geo) {
   (void)cap;
-  const int ctas = 2 * std::max(sms, 1);  // two 512-thread CTAs per SM
+  // Resident CTAs a SM (two 512-thread CTAs by design); the cooperative launch needs the
+  // grid to fit at once.
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    cudaError_t err = prepare_row_kernel(row_smem_bytes());
+    if (err != cudaSuccess) return err;
+    int occ = 0;
+    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, row_kernel, kThreads,
+                                                        row_smem_bytes());
+    if (err != cudaSuccess) return err;
+    if (occ < 1) return cudaErrorInvalidConfiguration;
+    per_sm = std::min(occ, 2);
+  }
+  const int ctas = per_sm * std::max(sms, 1);
   const int max_by_size = std::max(1, vocab / kMinChunk);
   int nch = (kUnitsPerCta * ctas + std::max(rows, 1) - 1) / std::max(rows, 1);
   nch = std::max(1, std::min(nch, std::min(kMaxChunks, max_by_size)));
@@ -2256,27 +2289,21 @@ cudaError_t launch_rows(const RowLaunch &l, const RowGeometry &geo, const Scratc
   a.warp_stats = scr.warp_stats;
   a.row_gval = scr.row_gval;
   a.row_gidx = scr.row_gidx;
+  a.ready = scr.ready;
+  a.epoch = l.epoch;
   cudaError_t err = prepare_row_kernel(geo.smem_bytes);
   if (err != cudaSuccess) return err;
-  plan_kernel<<<l.rows, kThreads, 0, stream>>>(a);
-  err = cudaGetLastError();
-  if (err != cudaSuccess) return err;
-  // Programmatic dependent launch: the row kernel's CTAs are scheduled while the plan
-  // finishes and wait for it in griddepcontrol.wait, hiding the launch gap.
+  // Cooperative launch: all CTAs resident at once (units wait on rows other CTAs plan).
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)geo.grid);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = geo.smem_bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
   cfg.attrs = attr;
-#ifdef TABBY_KNOB_NOPDL
-  cfg.numAttrs = 0;
-#else
   cfg.numAttrs = 1;
-#endif
   return cudaLaunchKernelEx(&cfg, row_kernel, a);
 }
 
