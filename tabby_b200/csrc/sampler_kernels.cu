@@ -1557,34 +1557,43 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
           tq0 = clock64();
         }
 #endif
+        // This thread's logits >= tf over its batch, one warp scan and one atomic.
+        uint32_t hm = 0;  // 4 bits a group
 #pragma unroll
         for (int j = 0; j < kBatch; j++) {
           const float4 x = xb[j];
-          const uint32_t hm = (r0 + j * kThreads + tid < total)
-                                  ? ((x.x >= tf ? 1u : 0u) | (x.y >= tf ? 2u : 0u) |
-                                     (x.z >= tf ? 4u : 0u) | (x.w >= tf ? 8u : 0u))
-                                  : 0u;
-          const int nh = __popc(hm);
-          int incl = nh;
+          if (r0 + j * kThreads + tid < total)
+            hm |= ((x.x >= tf ? 1u : 0u) | (x.y >= tf ? 2u : 0u) | (x.z >= tf ? 4u : 0u) |
+                   (x.w >= tf ? 8u : 0u))
+                  << (4 * j);
+        }
+        const int nh = __popc(hm);
+        int incl = nh;
 #pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const int t = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += t;
-          }
-          const int wtotal = __shfl_sync(0xffffffffu, incl, 31);
-          uint32_t wb = 0;
-          if (lane == 31 && wtotal > 0) wb = atomicAdd(&sh->count, (uint32_t)wtotal);
-          wb = __shfl_sync(0xffffffffu, wb, 31);
-          uint32_t slot = wb + (uint32_t)(incl - nh);
+        for (int o = 1; o < 32; o <<= 1) {
+          const int t = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += t;
+        }
+        const int wtotal = __shfl_sync(0xffffffffu, incl, 31);
+        uint32_t wb = 0;
+        if (lane == 31 && wtotal > 0) wb = atomicAdd(&sh->count, (uint32_t)wtotal);
+        wb = __shfl_sync(0xffffffffu, wb, 31);
+        uint32_t slot = wb + (uint32_t)(incl - nh);
 #pragma unroll
-          for (int e = 0; e < 4; e++) {
-            if ((hm >> e) & 1u) {
-              const float xe = e == 0 ? x.x : e == 1 ? x.y : e == 2 ? x.z : x.w;
-              if (slot < (uint32_t)kFinishCap)
-                cand[slot] = composite(key_of(xe), (uint32_t)(bb[j] + e));
-              else
-                sh->overflow = 1u;
-              slot++;
+        for (int j = 0; j < kBatch; j++) {
+          const uint32_t jm = (hm >> (4 * j)) & 15u;
+          if (jm) {
+            const float4 x = xb[j];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+              if ((jm >> e) & 1u) {
+                const float xe = e == 0 ? x.x : e == 1 ? x.y : e == 2 ? x.z : x.w;
+                if (slot < (uint32_t)kFinishCap)
+                  cand[slot] = composite(key_of(xe), (uint32_t)(bb[j] + e));
+                else
+                  sh->overflow = 1u;
+                slot++;
+              }
             }
           }
         }
