@@ -120,7 +120,7 @@ extern "C" int tabby_sample_rows_noalloc(const float *d_logits, int64_t row_stri
   l.topk_values = d_topk_values;
   l.topk_ld = topk_ld;
 
-  // The row pass resets the counters of the rows it plans (plan_kernel), so no clearing
+  // The row pass resets the counters of the rows it plans (its plan phase), so no clearing
   // is needed here.
   cudaError_t err = cudaSuccess;
   for (int32_t r0 = 0; r0 < rows; r0 += kNoAllocRows) {

@@ -5,22 +5,22 @@
 // topk_partial + topk_select, i.e. k+4 passes over the row. Here every logit is read
 // from HBM once, in one streaming pass:
 //
-//   plan_row       one CTA per row, first phase of row_kernel: resets the row's counters,
-//                  fixes its pool size and
-//                  its place in the processing order, and estimates a filter threshold
-//                  from 2048 logits sampled in 32 runs spread over the row.
-//   row_kernel     persistent, two 512-thread CTAs per SM taking (row, chunk) units from
-//                  a global counter. Each warp streams its part of the chunk straight
-//                  into registers (four 16-byte loads in flight a thread, the next
-//                  iteration's loads issued before this one is used), keeping online
-//                  max and sum(exp(x - max)) per thread and appending the logits at or
-//                  above the threshold, as 64-bit composites (order-preserving key,
-//                  inverted index), to a shared candidate buffer; no block barrier until
-//                  the chunk ends. Chunks append their candidates to the row's global
-//                  list; the unit that completes a row checks the estimate (falling
-//                  back to an exact re-filter), keeps the k best by radix select or a
-//                  warp-level top-64 tree, sorts them by (value desc, index asc) and
-//                  runs sampleFromTopK in float64 (finalize.cuh).
+//   row_kernel     one cooperative launch, two 512-thread CTAs per SM.
+//     plan phase   CTA c plans rows c, c + grid, ...: resets the row's counters, fixes
+//                  its pool size and its place in the processing order, estimates a
+//                  filter threshold from 2048 logits sampled in 32 runs spread over the
+//                  row, and publishes the row with a per-launch ready flag.
+//     units        CTAs take (row, chunk) units from a global counter, waiting only for
+//                  their own row's plan. Each warp streams its part of the chunk through
+//                  a 3-stage cp.async ring in shared memory, keeps online max and
+//                  sum(exp(x - max)) per thread (packed f32x2 arithmetic) and appends
+//                  every float4 group holding a logit at or above the threshold to its
+//                  own region of the row's candidate list; no block barrier until the
+//                  chunk ends. The unit that completes a row finishes it: merges the
+//                  per-warp statistics, expands the groups into 64-bit composites
+//                  (order-preserving key, inverted index), checks the estimate (falling
+//                  back to an exact re-filter), keeps and sorts the k best (binned
+//                  ranking) and runs sampleFromTopK in float64 (finalize.cuh).
 //   merge_kernel   the vocab-sharded finish: merges all-gathered per-shard blocks.
 //
 // Selection works on the raw logits; temperature only enters the float64 finalize,
@@ -42,12 +42,6 @@ constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kVec = 4;                   // float4 loads in flight per thread per iteration
 constexpr int kWarpIter = 32 * kVec;      // float4 groups a warp reads per iteration (2 KB)
-#ifndef TABBY_PREFETCH
-#define TABBY_PREFETCH 0  // ask for the next unit before the current one ends
-#endif
-#ifndef TABBY_PLAN_GROUPS
-#define TABBY_PLAN_GROUPS 1  // float4 groups a plan thread samples
-#endif
 constexpr int kRowGroups = 8192;   // candidate groups (float4 + index) a row's global list holds
 constexpr int kStages = 3;         // cp.async stages of the streaming loop
 constexpr int kStageBytes = kStages * 4 * 512 * 16;  // the stages (kStages x kVec x kThreads)
@@ -1170,14 +1164,15 @@ __device__ __forceinline__ int top_sorted(uint64_t *cand, int n, int k, int capa
 // plan_row (one CTA a row) resets the row's counters, fixes its pool size k and its
 // place in the processing order (rows with pools above 64 first, so that the rows whose
 // finish is cheap come last), and estimates a threshold from a sample of 512 float4
-// groups in 32 runs spread over the row: a logit with about rr sample logits at or above it, rr
-// chosen so that the row holds at least k logits at or above it with near certainty
-// (rr = mu + 3 sqrt(mu) + 4, mu the expected sample count above the row's k-th largest).
+// groups in 32 runs spread over the row: a logit with about rr sample logits at or above
+// it, rr = min(k, mu + 4 sqrt(mu) + 6), mu the expected sample count above the row's
+// k-th largest, so that the row holds at least k logits at or above it with near
+// certainty (rr = k never fails: the sample is part of the row). It publishes the row
+// with ready[pos] = epoch.
 //
-// row_kernel is persistent: every CTA takes (row, chunk) units from a global counter in
-// that order, so fast CTAs take more. A unit streams its chunk once (online max /
-// sum-exp, and the threshold filter into the shared candidate buffer), appends its
-// candidates to the row's global list and its per-warp statistics to the row's table;
+// The units: every CTA takes (row, chunk) units from a global counter in that order, so
+// fast CTAs take more. A unit streams its chunk once, appends its candidate groups to
+// its warps' regions of the row's list and its per-warp statistics to the row's table;
 // the unit that completes a row finishes it: it checks the estimate (at least min(k, V)
 // candidates and no overflow, else the row is filtered again exactly), keeps the k
 // best, sorts them and runs sampleFromTopK. Rows finish while other rows still stream.
@@ -1303,7 +1298,7 @@ __device__ __noinline__ void plan_row(const PassArgs &a, int row, uint64_t *cand
   const Span sp = aligned_span(rowp, 0, a.vocab);
   // The sample: kPlanRuns runs of kPlanRun consecutive float4 groups (256 contiguous
   // bytes, whole DRAM bursts), spread evenly over the aligned middle of the row.
-  constexpr int kPlanSample = TABBY_PLAN_GROUPS * kThreads;  // float4 groups sampled
+  constexpr int kPlanSample = kThreads;  // float4 groups sampled
   constexpr int kPlanRun = 16;
   constexpr int kPlanRuns = kPlanSample / kPlanRun;
   const int S = min(kPlanSample, sp.ngroups);
@@ -1780,10 +1775,9 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
 #else
 #define NOW() 0ull
 #endif
-  // Unit pipeline, kept by thread 0: the next unit's id is requested near the end of the
-  // current unit's stream, and its row data travel together with the row's completion
-  // count, so one global round trip separates two units (the unit that completes a row
-  // finishes it at once).
+  // Unit schedule, kept by thread 0: at the end of a unit it counts the unit into its row
+  // (the unit that completes a row finishes it at once), then takes the next unit and its
+  // row data.
   int nid = 0, nrow = 0, nk = 0;
   float ntf = 0.f;
   // Thread 0: the row data of unit nid, once its row is planned (bounded wait; a wait
@@ -1832,7 +1826,6 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
     const int k = sh->uk;
     const float tf = sh->utf;
     if (unit >= units) break;
-    bool fetched = false;  // thread 0: the next unit's id has been requested
 #ifdef TABBY_TRACE
     UTRACE(uj, 0, NOW());
 #endif
@@ -1953,12 +1946,7 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
           if (it * kWarpIter + q * 32 + lane < wn)
             mn = min3f(mn, min3f(v[q].x, v[q].y, v[q].z), v[q].w);
       }
-#ifdef TABBY_KNOB_NOSTATS
-      if (im == 1.2345f) sh->flags = 3;
-      if (false) {
-#else
       if (im > m) {
-#endif
         const float r = ex2_approx((m - im) * kLog2e);
         s2 = f2_mul(s2, f2_pack(r, r));
         m = im;
@@ -1968,11 +1956,7 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
         // inside the 1e-5 budget). Larger |m| uses the subtraction form.
         small = fabsf(m) <= 16.f;
       }
-#ifdef TABBY_KNOB_NOSTATS
-      if (false) {
-#else
       if (small) {
-#endif
         const unsigned long long L2 = f2_pack(kLog2e, kLog2e), nmL2 = f2_pack(-mL, -mL);
 #pragma unroll
         for (int q = 0; q < kVec; q++) {
@@ -1980,11 +1964,7 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
           const unsigned long long e23 = f2_ex2(f2_fma(f2_pack(v[q].z, v[q].w), L2, nmL2));
           s2 = f2_add(s2, f2_add(e01, e23));
         }
-      } else
-#ifdef TABBY_KNOB_NOSTATS
-      if (false)
-#endif
-      {
+      } else {
         const unsigned long long L2 = f2_pack(kLog2e, kLog2e), nm2 = f2_pack(-m, -m);
 #pragma unroll
         for (int q = 0; q < kVec; q++) {
@@ -1996,7 +1976,6 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
         }
       }
       issue(SC);  // refills stage S (its values are in registers and in use above)
-#ifndef TABBY_KNOB_NOFILTER
       // Groups holding a logit >= tf go to the warp's region whole (the value check per
       // logit happens in the finish).
       if (k > 0 && __any_sync(0xffffffffu, im >= tf)) {
@@ -2025,7 +2004,6 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
         }
         wcnt += __shfl_sync(0xffffffffu, incl, 31);
       }
-#endif
     };
     using I0 = std::integral_constant<int, 0>;
     using I1 = std::integral_constant<int, 1>;
@@ -2034,27 +2012,10 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
     issue(I0{});
     issue(I1{});
     issue(I2{});
-    // Thread 0 asks for the next unit two iterations before its segment ends, so the id
-    // is there at the end of this unit while the schedule stays dynamic.
-    // The last chunk of a row usually completes it; that unit asks after its finish.
-#if TABBY_PREFETCH
-    const int fetch_it = chunk == a.nch - 1 ? 0x7fffffff : max(wit - 2, 0);
-#else
-    const int fetch_it = 0x7fffffff;
-#endif
     for (int it = 0; it < wit; it += kStages) {
-#pragma unroll
-      for (int j = 0; j < kStages; j++) {
-        if (it + j < wit) {
-          if (tid == 0 && it + j == fetch_it) {
-            nid = (int)atomicAdd(sched, 1u);
-            fetched = true;
-          }
-          if (j == 0) step(I0{}, it);
-          if (j == 1) step(I1{}, it + 1);
-          if (j == 2) step(I2{}, it + 2);
-        }
-      }
+      step(I0{}, it);
+      if (it + 1 < wit) step(I1{}, it + 1);
+      if (it + 2 < wit) step(I2{}, it + 2);
     }
     cp_async_wait_group<0>();
 #ifdef TABBY_TRACE
@@ -2090,14 +2051,14 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
       __threadfence();  // ... and visible before the count (release)
       const uint32_t done = atomicAdd(&a.row_done[row], 1u);
       const bool last = done == (uint32_t)(a.nch - 1);
-#if TABBY_PREFETCH
-      if (!fetched && !last) nid = (int)atomicAdd(sched, 1u);
-#else
-      if (!last) nid = (int)atomicAdd(sched, 1u);
-#endif
-      if (fetched || !last) unit_info();  // the next unit's row data
+      // A unit that completes a row asks for its successor only after the finish, so a
+      // CTA busy finishing never holds on to a unit other CTAs could take.
+      if (!last) {
+        nid = (int)atomicAdd(sched, 1u);
+        unit_info();  // the next unit's row data
+      }
       sh->last = last ? 1u : 0u;
-      sh->unit = (fetched || !last) ? (uint32_t)nid : 0xffffffffu;
+      sh->unit = last ? 0xffffffffu : (uint32_t)nid;
       sh->urow = nrow;
       sh->uk = nk;
       sh->utf = ntf;
@@ -2106,11 +2067,7 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
 #ifdef TABBY_TRACE
     UTRACE(uj, 2, NOW());
 #endif
-#ifdef TABBY_KNOB_NOFINISH
-    if (false) {
-#else
     if (sh->last) {
-#endif
       __threadfence();
       finish_row(a, row, k, fin, hist, sh);
       __syncthreads();  // the finish is done with the stage region before the loads reuse it
@@ -2217,10 +2174,7 @@ static size_t row_smem_bytes() {
 
 // Units a CTA should see on average: enough for the dynamic schedule to even out the
 // CTAs' speeds, few enough that the per-unit overhead stays small.
-#ifndef TABBY_UNITS_PER_CTA
-#define TABBY_UNITS_PER_CTA 3
-#endif
-constexpr int kUnitsPerCta = TABBY_UNITS_PER_CTA;
+constexpr int kUnitsPerCta = 3;
 
 static cudaError_t prepare_row_kernel(size_t smem_bytes);
 
