@@ -15,8 +15,8 @@ draw for every row -- over one batch of seeded synthetic logits.
   e2e        the same metric through the public host-buffer call tabby_sample_rows():
              pinned host logits -> device, sample, outcomes -> host, every step.
   roofline   algorithmic bytes = B * V * 4 per launch (each logit read once) / average
-             time of one tabby_sample_rows_async call (plan_kernel + row_kernel, CUDA
-             events on the launch stream), against MEASURED_PEAKS.json hbm_gbs.
+             time of one tabby_sample_rows_async call (one row_kernel launch; CUDA events
+             on the launch stream), against MEASURED_PEAKS.json hbm_gbs.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--profile]
 """
@@ -290,13 +290,13 @@ def run_ours(args, rank, local_rank, world):
                          "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS,
                          "traffic": profiled_traffic(),
                          "algorithmic_bytes_per_launch": bytes_per_launch,
-                         "kernel": "plan_kernel + row_kernel (one tabby_sample_rows_async "
-                                   "call; the time includes both)"},
+                         "kernel": "row_kernel (one cooperative launch per "
+                                   "tabby_sample_rows_async call)"},
             "e2e": {"value": e2e_value, "unit": "rows/s",
                     "h2d_bytes_per_step": ROWS * VOCAB * 4 + p.nbytes + u.nbytes,
                     "d2h_bytes_per_step": hout.nbytes, "steps": e2e_steps,
                     "call": "tabby_sample_rows (pinned host buffers, synchronous)"},
-            "gpu_launches": 2 * args.steps,  # plan_kernel + row_kernel per call
+            "gpu_launches": args.steps,  # one cooperative row_kernel launch per call
             "clocks": clocks.summary(),
         }
     if pg is not None:
