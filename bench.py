@@ -270,6 +270,10 @@ def run_ours(args, rank, local_rank, world):
             e2e_s = float(t.item())
         e2e_value = world * ROWS * e2e_steps / e2e_s
 
+    sharded = None
+    if pg is not None and not args.profile:
+        sharded = run_sharded(args, rank, local_rank, world, dev, pg)
+
     result = None
     if rank == 0:
         peak, peak_kind = measured_peak()
@@ -299,6 +303,8 @@ def run_ours(args, rank, local_rank, world):
             "gpu_launches": args.steps,  # one cooperative row_kernel launch per call
             "clocks": clocks.summary(),
         }
+        if sharded is not None:
+            result["sharded"] = sharded
     if pg is not None:
         pg.barrier()
     if rank == 0:
@@ -313,6 +319,56 @@ def run_ours(args, rank, local_rank, world):
     if pg is not None:
         pg.destroy_process_group()
     return 0
+
+
+SHARD_ROWS = 512  # the c5 configuration: B=512 x V=151936 split over the GPUs
+
+
+def run_sharded(args, rank, local_rank, world, dev, pg):
+    """Vocab-sharded sampling (c5): every rank holds columns [r*V/N, (r+1)*V/N) of 512
+    rows; a step is the local top-64 blocks, one NCCL all-gather of the blocks and the
+    merge (every rank ends with the same tokens). Strong scaling: the job is 512 rows of
+    the full vocabulary whatever N is. Device-timed with CUDA events, max over ranks."""
+    import torch
+
+    from tabby_b200 import synth
+    from tabby_b200._lib import OUTCOME_DTYPE, check, lib
+    from tabby_b200.sharded import BLOCK_WORDS, SHARD_TOP_K, ShardedSampler, gather_blocks
+
+    x, p, u = synth.config("c5", seed=0, rows=SHARD_ROWS)
+    s = ShardedSampler(VOCAB, device=local_rank, max_rows=SHARD_ROWS)
+    local = torch.from_numpy(np.ascontiguousarray(x[:, s.lo:s.hi])).to(dev)
+    p_dev = torch.from_numpy(p.view(np.uint8).copy()).to(dev)
+    u_dev = torch.from_numpy(u).to(dev)
+    out = torch.empty(SHARD_ROWS * OUTCOME_DTYPE.itemsize, dtype=torch.uint8, device=dev)
+    ids = torch.empty((SHARD_ROWS, SHARD_TOP_K), dtype=torch.int32, device=dev)
+
+    def step():
+        block = s.local_blocks(local)
+        gathered = gather_blocks(block)
+        s.merge_async(gathered, world, p_dev, u_dev, out, ids, None)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    pg.barrier()
+    steps = max(10, min(args.steps, 200))
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    ms = float(t.item()) / steps
+    s.close()
+    return {"metric": "sampled rows/s, vocab-sharded (c5: B=512 x V=151936 split over "
+                      f"{world} GPUs, local top-64, NCCL all-gather, merge)",
+            "value": SHARD_ROWS / (ms / 1e3), "unit": "rows/s", "ms_per_step": ms,
+            "steps": steps, "scaling": "strong",
+            "launches_per_step": "row_kernel + NCCL all-gather + merge_kernel"}
 
 
 def main():
