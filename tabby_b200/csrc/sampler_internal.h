@@ -68,15 +68,12 @@ constexpr int32_t kScratchWarps = 16;         // warps a CTA has
 // scratch, starting at 1 and never 0), so no clearing is needed between launches.
 struct Scratch {
   uint32_t *sched = nullptr;                 // [2] unit counters (by launch parity)
-  uint32_t *ready = nullptr;                 // [max_rows] launch epoch once planned
+  unsigned long long *pos_entry = nullptr;   // [max_rows][2] epoch-tagged plan by position
   uint32_t *row_done = nullptr;              // [max_rows] chunks finished
   uint32_t *warp_cnt = nullptr;              // [max_rows][kScratchChunks * kScratchWarps]
   uint32_t *row_flags = nullptr;             // [max_rows] bad input / overflow
   float *row_tf = nullptr;                   // [max_rows] estimated threshold
   float *row_tf_lo = nullptr;                // [max_rows] the re-filter's starting threshold
-  float *pos_tf = nullptr;                   // [max_rows] threshold by processing position
-  int32_t *pos_k = nullptr;                  // [max_rows] pool size by processing position
-  int32_t *order = nullptr;                  // [max_rows] processing order
   float2 *warp_stats = nullptr;              // [max_rows][kScratchChunks][kScratchWarps]
   float4 *row_gval = nullptr;                // [max_rows][kScratchGroups] group values
   int32_t *row_gidx = nullptr;               // [max_rows][kScratchGroups] group first index
@@ -84,7 +81,7 @@ struct Scratch {
 
   static constexpr size_t section(size_t bytes) { return (bytes + 255) / 256 * 256; }
   static constexpr size_t layout_bytes(int32_t rows) {
-    return section(8) + 8 * section(4 * (size_t)rows) +
+    return section(8) + section(16 * (size_t)rows) + 4 * section(4 * (size_t)rows) +
            section(4 * (size_t)rows * kScratchChunks * kScratchWarps) +
            section(8 * (size_t)rows * kScratchChunks * kScratchWarps) +
            section(16 * (size_t)rows * kScratchGroups) + section(4 * (size_t)rows * kScratchGroups);
@@ -96,8 +93,8 @@ struct Scratch {
     const size_t r = (size_t)rows;
     s.sched = reinterpret_cast<uint32_t *>(p);
     p += section(8);
-    s.ready = reinterpret_cast<uint32_t *>(p);
-    p += section(4 * r);
+    s.pos_entry = reinterpret_cast<unsigned long long *>(p);
+    p += section(16 * r);
     s.row_done = reinterpret_cast<uint32_t *>(p);
     p += section(4 * r);
     s.warp_cnt = reinterpret_cast<uint32_t *>(p);
@@ -107,12 +104,6 @@ struct Scratch {
     s.row_tf = reinterpret_cast<float *>(p);
     p += section(4 * r);
     s.row_tf_lo = reinterpret_cast<float *>(p);
-    p += section(4 * r);
-    s.pos_tf = reinterpret_cast<float *>(p);
-    p += section(4 * r);
-    s.pos_k = reinterpret_cast<int32_t *>(p);
-    p += section(4 * r);
-    s.order = reinterpret_cast<int32_t *>(p);
     p += section(4 * r);
     s.warp_stats = reinterpret_cast<float2 *>(p);
     p += section(8 * r * kScratchChunks * kScratchWarps);

@@ -205,12 +205,12 @@ __device__ __forceinline__ float4 ld_shared_f4(uint32_t src) {
                : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release_u32(uint32_t *p, uint32_t v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_release_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 template <int N>
@@ -1168,7 +1168,7 @@ __device__ __forceinline__ int top_sorted(uint64_t *cand, int n, int k, int capa
 // it, rr = min(k, mu + 4 sqrt(mu) + 6), mu the expected sample count above the row's
 // k-th largest, so that the row holds at least k logits at or above it with near
 // certainty (rr = k never fails: the sample is part of the row). It publishes the row
-// with ready[pos] = epoch.
+// as its position entry, tagged with the epoch.
 //
 // The units: every CTA takes (row, chunk) units from a global counter in that order, so
 // fast CTAs take more. A unit streams its chunk once, appends its candidate groups to
@@ -1193,16 +1193,14 @@ struct PassArgs {
   float *block;
   int32_t block_ld;
   uint32_t *sched;       // [2] unit counters; launch e uses sched[e & 1], clears the other
-  uint32_t *ready;       // [rows] = epoch once the row at that position is planned
+  unsigned long long *pos_entry;  // [rows][2] by processing position, each word tagged
+                                 // with the epoch: (epoch, row << 12 | k), (epoch, tf)
   uint32_t epoch;        // this launch's number (never 0)
   uint32_t *row_done;    // [rows] chunks finished
   uint32_t *warp_cnt;    // [rows][nch * kWarps] candidate groups of each (chunk, warp)
   uint32_t *row_flags;   // [rows] kFlagBadInput | kRowOverflow
   float *row_tf;         // [rows] threshold, by row
   float *row_tf_lo;      // [rows] a lower threshold (far safer rank), by row
-  float *pos_tf;         // [rows] threshold, by processing position
-  int32_t *pos_k;        // [rows] pool size, by processing position
-  int32_t *order;        // [rows] processing order
   float2 *warp_stats;    // [rows][nch][kWarps] (max, sum-exp)
   float4 *row_gval;      // [rows][kRowGroups] candidate groups: warp w of chunk c owns the
   int32_t *row_gidx;     //   region (c * kWarps + w) of region_slots() slots
@@ -1260,7 +1258,7 @@ __device__ __forceinline__ Span aligned_span(const float *rowp, int lo, int hi) 
 
 // Plans one row (block-uniform call): resets its counters, fixes its pool size and its
 // place in the processing order, estimates its threshold, then publishes the row's
-// position entry with ready[pos] = epoch (release). cand holds 2048 slots.
+// position entry, tagged with the epoch (release). cand holds 2048 slots.
 __device__ __noinline__ void plan_row(const PassArgs &a, int row, uint64_t *cand,
                                       uint32_t *hist, Shared *sh) {
   int (*red)[kWarps] = sh->plan_red;
@@ -1276,6 +1274,23 @@ __device__ __noinline__ void plan_row(const PassArgs &a, int row, uint64_t *cand
     a.row_done[row] = 0;
     a.row_flags[row] = 0;
   }
+  // The sample: 32 runs of 16 consecutive float4 groups (256 contiguous bytes, whole DRAM
+  // bursts), spread evenly over the aligned middle of the row; one group a thread, its
+  // load in flight while the row order is worked out.
+  const Span sp = aligned_span(rowp, 0, a.vocab);
+  constexpr int kPlanSample = kThreads;  // float4 groups sampled
+  constexpr int kPlanRun = 16;
+  constexpr int kPlanRuns = kPlanSample / kPlanRun;
+  const int S = min(kPlanSample, sp.ngroups);
+  int g = tid;  // short rows: every group
+  if (S == kPlanSample) {
+    const int run = tid / kPlanRun;
+    const int start = (int)(((2LL * run + 1) * sp.ngroups) / (2LL * kPlanRuns)) - kPlanRun / 2;
+    g = max(0, min(start, sp.ngroups - kPlanRun)) + tid % kPlanRun;
+  }
+  const bool sampled = k > 0 && tid < S;
+  float4 sv = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (sampled) sv = __ldg(reinterpret_cast<const float4 *>(rowp + sp.a0) + g);
   // Place in the order: rows with k > 64 first, each group in row order.
   int large = 0, large_before = 0, small_before = 0;
   for (int r = tid; r < a.rows; r += kThreads) {
@@ -1295,39 +1310,17 @@ __device__ __noinline__ void plan_row(const PassArgs &a, int row, uint64_t *cand
     red[1][warp] = large_before;
     red[2][warp] = small_before;
   }
-  const Span sp = aligned_span(rowp, 0, a.vocab);
-  // The sample: kPlanRuns runs of kPlanRun consecutive float4 groups (256 contiguous
-  // bytes, whole DRAM bursts), spread evenly over the aligned middle of the row.
-  constexpr int kPlanSample = kThreads;  // float4 groups sampled
-  constexpr int kPlanRun = 16;
-  constexpr int kPlanRuns = kPlanSample / kPlanRun;
-  const int S = min(kPlanSample, sp.ngroups);
   uint64_t t1 = 0, t2 = 0;
-  if (k > 0) {
+  if (sampled) {
+    const float xs[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
-    for (int j = 0; j < kPlanSample / kThreads; j++) {
-      const int i = j * kThreads + tid;
-      if (i < S) {
-        int g;
-        if (S == kPlanSample) {
-          const int run = i / kPlanRun;
-          const int start = (int)(((2LL * run + 1) * sp.ngroups) / (2LL * kPlanRuns)) - kPlanRun / 2;
-          g = max(0, min(start, sp.ngroups - kPlanRun)) + i % kPlanRun;
-        } else {
-          g = i;  // short rows: every group
-        }
-        const float4 v = __ldg(reinterpret_cast<const float4 *>(rowp + sp.a0) + g);
-        const float xs[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const uint64_t c = composite(key_of(xs[e]), (uint32_t)(sp.a0 + 4 * g + e));
-          if (c > t1) {
-            t2 = t1;
-            t1 = c;
-          } else if (c > t2) {
-            t2 = c;
-          }
-        }
+    for (int e = 0; e < 4; e++) {
+      const uint64_t c = composite(key_of(xs[e]), (uint32_t)(sp.a0 + 4 * g + e));
+      if (c > t1) {
+        t2 = t1;
+        t1 = c;
+      } else if (c > t2) {
+        t2 = c;
       }
     }
   }
@@ -1371,13 +1364,12 @@ __device__ __noinline__ void plan_row(const PassArgs &a, int row, uint64_t *cand
   PPHASE(row, 2);
   if (tid == 0) {
     const int pos = (int)sh->unit;
-    a.order[pos] = row;
-    a.pos_k[pos] = k;
-    a.pos_tf[pos] = tf;
     a.row_tf[row] = tf;
     a.row_tf_lo[row] = tf_lo;
     __threadfence();
-    st_release_u32(&a.ready[pos], a.epoch);
+    const unsigned long long tag = (unsigned long long)a.epoch << 32;
+    st_release_u64(&a.pos_entry[2 * pos], tag | ((unsigned long long)row << 12) | (uint32_t)k);
+    st_release_u64(&a.pos_entry[2 * pos + 1], tag | __float_as_uint(tf));
   }
   __syncthreads();  // the slots and sh are free again
 #ifdef TABBY_TRACE
@@ -1762,7 +1754,7 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
   const float4 kPast = make_float4(-3.40282347e38f, -3.40282347e38f, -3.40282347e38f,
                                    -3.40282347e38f);
   // Plan phase: every CTA plans rows blockIdx.x, blockIdx.x + gridDim.x, ... and
-  // publishes each with ready[pos] = epoch; a unit waits only for its own row's entry, so
+  // publishes each as an epoch-tagged position entry; a unit waits only for its own row's entry, so
   // streaming starts as soon as the first rows are planned. The launch is cooperative:
   // every CTA is resident, so every awaited row gets planned.
   if (blockIdx.x == 0 && tid == 0) a.sched[(a.epoch + 1) & 1] = 0;  // the next launch's
@@ -1786,16 +1778,20 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
     if (nid >= units) return;
     const int ri = nid / a.nch;
     uint32_t spins = 0;
-    while (ld_acquire_u32(&a.ready[ri]) != a.epoch) {
+    unsigned long long w0, w1;
+    for (;;) {  // both words of this launch's entry: one round trip once planned
+      w0 = ld_acquire_u64(&a.pos_entry[2 * ri]);
+      w1 = ld_acquire_u64(&a.pos_entry[2 * ri + 1]);
+      if ((uint32_t)(w0 >> 32) == a.epoch && (uint32_t)(w1 >> 32) == a.epoch) break;
       if (++spins > (1u << 24)) {
         nid = units;
         return;
       }
       __nanosleep(100);
     }
-    nrow = a.order[ri];
-    nk = a.pos_k[ri];
-    ntf = a.pos_tf[ri];
+    nrow = (int)((uint32_t)w0 >> 12);
+    nk = (int)((uint32_t)w0 & 0xfffu);
+    ntf = __uint_as_float((uint32_t)w1);
   };
   if (tid == 0) {
     nid = (int)atomicAdd(sched, 1u);
@@ -2246,13 +2242,10 @@ cudaError_t launch_rows(const RowLaunch &l, const RowGeometry &geo, const Scratc
   a.row_flags = scr.row_flags;
   a.row_tf = scr.row_tf;
   a.row_tf_lo = scr.row_tf_lo;
-  a.pos_tf = scr.pos_tf;
-  a.pos_k = scr.pos_k;
-  a.order = scr.order;
+  a.pos_entry = scr.pos_entry;
   a.warp_stats = scr.warp_stats;
   a.row_gval = scr.row_gval;
   a.row_gidx = scr.row_gidx;
-  a.ready = scr.ready;
   a.epoch = l.epoch;
   cudaError_t err = prepare_row_kernel(geo.smem_bytes);
   if (err != cudaSuccess) return err;
