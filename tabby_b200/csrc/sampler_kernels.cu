@@ -2170,7 +2170,11 @@ static size_t row_smem_bytes() {
 
 // Units a CTA should see on average: enough for the dynamic schedule to even out the
 // CTAs' speeds, few enough that the per-unit overhead stays small.
-constexpr int kUnitsPerCta = 3;
+// Rows are split into chunks only until the units cover about 0.8 of the resident CTAs:
+// every extra unit pays a pipeline refill and a cross-CTA hand-off to the row's finish,
+// which measured dearer than leaving a few CTAs idle (B=256 on 296 CTAs runs fastest
+// with whole rows).
+constexpr int kUnitsPerCtaX10 = 8;
 
 static cudaError_t prepare_row_kernel(size_t smem_bytes);
 
@@ -2191,7 +2195,7 @@ cudaError_t plan_rows(int32_t sms, int32_t rows, int32_t vocab, int32_t cap, Row
   }
   const int ctas = per_sm * std::max(sms, 1);
   const int max_by_size = std::max(1, vocab / kMinChunk);
-  int nch = (kUnitsPerCta * ctas + std::max(rows, 1) - 1) / std::max(rows, 1);
+  int nch = (kUnitsPerCtaX10 * ctas + 10 * std::max(rows, 1) - 1) / (10 * std::max(rows, 1));
   nch = std::max(1, std::min(nch, std::min(kMaxChunks, max_by_size)));
   RowGeometry g;
   g.chunk = round_up((vocab + nch - 1) / nch, 4);
