@@ -54,6 +54,7 @@ struct RowGeometry {
   int32_t chunk = 0;  // logits a unit (multiple of 4)
   int32_t nch = 0;    // units a row
   int32_t grid = 0;   // CTAs of the row kernel
+  int32_t whole = 0;  // 1: one CTA a row, threshold from the stream, no plan phase
   size_t smem_bytes = 0;
 };
 

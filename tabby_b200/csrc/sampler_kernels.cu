@@ -1182,6 +1182,7 @@ struct PassArgs {
   int64_t row_stride;
   int32_t rows, vocab;
   int32_t nch, chunk;  // chunks a row, logits a chunk (a multiple of 4)
+  int32_t whole;       // 1: whole rows a CTA, threshold from the stream (no plan phase)
   int32_t mode, cap, fixed_k;
   int64_t index_offset;
   const tabby_sampling_params *params;
@@ -1739,6 +1740,70 @@ __device__ __forceinline__ unsigned long long f2_ex2(unsigned long long v) {
   return f2_pack(ex2_approx(lo), ex2_approx(hi));
 }
 
+// Threshold of a row streamed whole by one CTA, from the first iteration of every warp's
+// segment (16 runs of up to 512 contiguous logits spread evenly over the row), which
+// stage 0 holds when this runs (block-uniform call). Each thread keeps the top two
+// composites of its up to 16 logits; the rr-th largest of those 1024 is at or below the
+// sample's rr-th largest, so the estimate errs towards more candidates. The rank rule is
+// the plan's (rr = min(k, ceil(mu + 4 sqrt(mu) + 6)), mu = k * sample / vocab;
+// rr2 = min(4 rr, 1023) for the re-filter). buf (2048 slots) and hist must not overlap
+// stages 0 and 1.
+__device__ __noinline__ float whole_threshold(const PassArgs &a, int row, int k, uint32_t sslot0,
+                                              int wn, int seg, int ngroups, int gbase,
+                                              uint64_t *buf, uint32_t *hist, Shared *sh) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  uint64_t t1 = 0, t2 = 0;
+#pragma unroll
+  for (int q = 0; q < kVec; q++) {
+    if (q * 32 + lane < wn) {
+      const float4 v = ld_shared_f4(sslot0 + (uint32_t)(q * kThreads * 16));
+      const float xs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const uint64_t c = composite(key_of(xs[e]), (uint32_t)(gbase + 4 * (q * 32 + lane) + e));
+        if (c > t1) {
+          t2 = t1;
+          t1 = c;
+        } else if (c > t2) {
+          t2 = c;
+        }
+      }
+    }
+  }
+  buf[2 * tid] = t1;
+  buf[2 * tid + 1] = t2;
+  int ns = 0;  // logits sampled (the same arithmetic for every thread)
+  for (int w = 0; w < kWarps; w++) {
+    const int g0 = min(w * seg, ngroups);
+    ns += 4 * min(kWarpIter, min(g0 + seg, ngroups) - g0);
+  }
+  __syncthreads();
+  float tf = -__int_as_float(0x7f800000);  // no estimate: every logit is a candidate
+  float tf_lo = tf;
+  if (k > 0) {
+    const float mu = (float)k * (float)ns / (float)a.vocab;
+    const int rr = min(k, (int)ceilf(mu + 4.f * sqrtf(mu) + 6.f));
+    if (rr >= 1 && rr < 2 * kThreads && rr < ns) {
+      const int rr2 = min(4 * rr, 2 * kThreads - 1);
+      uint64_t thr, thr2;
+      if (bin_rank_topk(buf, 2 * kThreads, rr2, 4 * kThreads, hist, sh) >= 0) {
+        thr = buf[rr - 1];
+        thr2 = buf[rr2 - 1];
+      } else {
+        thr = thr2 = select_top(buf, 2 * kThreads, rr, hist, sh);
+      }
+      if ((thr >> 32) != 0ull) tf = float_of_key((uint32_t)(thr >> 32));
+      if ((thr2 >> 32) != 0ull) tf_lo = float_of_key((uint32_t)(thr2 >> 32));
+    }
+  }
+  if (tid == 0) {
+    a.row_tf[row] = tf;
+    a.row_tf_lo[row] = tf_lo;
+  }
+  __syncthreads();  // buf and hist are free again
+  return tf;
+}
+
 __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant__ PassArgs a) {
   // Shared memory: the cp.async stages of the streaming loop; the finish reuses them as
   // its composite buffer (kFinishCap) followed by the histogram.
@@ -1759,7 +1824,8 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
   // every CTA is resident, so every awaited row gets planned.
   if (blockIdx.x == 0 && tid == 0) a.sched[(a.epoch + 1) & 1] = 0;  // the next launch's
   uint32_t *sched = a.sched + (a.epoch & 1);
-  for (int r = blockIdx.x; r < a.rows; r += gridDim.x) plan_row(a, r, fin, hist, sh);
+  if (!a.whole)
+    for (int r = blockIdx.x; r < a.rows; r += gridDim.x) plan_row(a, r, fin, hist, sh);
 
 #ifdef TABBY_TRACE
   int uj = 0;
@@ -1776,6 +1842,13 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
   // that runs out ends this CTA's work, leaving the unit undone).
   auto unit_info = [&]() {
     if (nid >= units) return;
+    if (a.whole) {  // unit = row; the threshold comes from the stream
+      uint32_t f = 0;
+      nrow = nid;
+      nk = row_pool(a, nid, &f);
+      ntf = 0.f;
+      return;
+    }
     const int ri = nid / a.nch;
     uint32_t spins = 0;
     unsigned long long w0, w1;
@@ -1820,7 +1893,7 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
     const int unit = (int)sh->unit;
     const int row = sh->urow;
     const int k = sh->uk;
-    const float tf = sh->utf;
+    float tf = sh->utf;
     if (unit >= units) break;
 #ifdef TABBY_TRACE
     UTRACE(uj, 0, NOW());
@@ -1849,33 +1922,6 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
     float4 *rgv = a.row_gval + region;
     int32_t *rgi = a.row_gidx + region;
     int wcnt = 0;
-
-    // Ragged ends of the chunk: at most 3 logits before a0 and 3 after a1, one per lane
-    // of warp 0, each kept as a group of its own (the other three slots NaN, which no
-    // threshold admits).
-    if (warp == 0) {
-      const int e = lane < 4 ? lo + lane : sp.a1 + (lane - 4);
-      const bool in = lane < 8 && (lane < 4 ? (e < sp.a0) : (e < hi));
-      float rx = 0.f;
-      if (in) {
-        rx = __ldg(rowp + e);
-        m = rx;
-        mL = m * kLog2e;
-        small = fabsf(m) <= 16.f;
-        s2 = f2_pack(1.f, 0.f);
-        mn = rx;
-      }
-      const bool take = in && k > 0 && rx >= tf;
-      const uint32_t mask = __ballot_sync(0xffffffffu, take);
-      if (take) {
-        const int slot = wcnt + __popc(mask & ((1u << lane) - 1u));
-        if (slot < regsize) {
-          rgv[slot] = make_float4(rx, kNaN, kNaN, kNaN);
-          rgi[slot] = e;
-        }
-      }
-      wcnt += __popc(mask);
-    }
 
     // Warp segments: warp w streams the float4 groups [sg0, sg0 + wn) of the chunk's
     // aligned middle, 128 groups (2 KB, four 512-byte coalesced loads) an iteration.
@@ -2007,7 +2053,44 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
     static_assert(kStages == 3, "the loop below is unrolled for three stages");
     issue(I0{});
     issue(I1{});
+    if (a.whole) {
+      // Whole rows: the threshold from iteration 0 (stage 0), while iteration 1 is in
+      // flight; stage 2's region holds the selection until iteration 2 is issued.
+      if (tid == 0) a.row_flags[row] = 0;
+      cp_async_wait_group<1>();
+      __syncthreads();
+      uint64_t *sel = reinterpret_cast<uint64_t *>(smem_raw + 2 * (kStageBytes / kStages));
+      tf = whole_threshold(a, row, k, sslot, wn, seg, sp.ngroups, gbase, sel,
+                           reinterpret_cast<uint32_t *>(sel + 4 * kThreads), sh);
+    }
     issue(I2{});
+    // Ragged ends of the chunk: at most 3 logits before a0 and 3 after a1, one per lane
+    // of warp 0, each kept as a group of its own (the other three slots NaN, which no
+    // threshold admits).
+    if (warp == 0) {
+      const int e = lane < 4 ? lo + lane : sp.a1 + (lane - 4);
+      const bool in = lane < 8 && (lane < 4 ? (e < sp.a0) : (e < hi));
+      float rx = 0.f;
+      if (in) {
+        rx = __ldg(rowp + e);
+        m = rx;
+        mL = m * kLog2e;
+        small = fabsf(m) <= 16.f;
+        s2 = f2_pack(1.f, 0.f);
+        mn = rx;
+      }
+      const bool take = in && k > 0 && rx >= tf;
+      const uint32_t mask = __ballot_sync(0xffffffffu, take);
+      if (take) {
+        const int slot = wcnt + __popc(mask & ((1u << lane) - 1u));
+        if (slot < regsize) {
+          rgv[slot] = make_float4(rx, kNaN, kNaN, kNaN);
+          rgi[slot] = e;
+        }
+      }
+      wcnt += __popc(mask);
+    }
+
     for (int it = 0; it < wit; it += kStages) {
       step(I0{}, it);
       if (it + 1 < wit) step(I1{}, it + 1);
@@ -2045,8 +2128,8 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
     __syncthreads();  // every thread's candidate groups and statistics are written
     if (tid == 0) {
       __threadfence();  // ... and visible before the count (release)
-      const uint32_t done = atomicAdd(&a.row_done[row], 1u);
-      const bool last = done == (uint32_t)(a.nch - 1);
+      const bool last =
+          a.whole || atomicAdd(&a.row_done[row], 1u) == (uint32_t)(a.nch - 1);
       // A unit that completes a row asks for its successor only after the finish, so a
       // CTA busy finishing never holds on to a unit other CTAs could take.
       if (!last) {
@@ -2201,6 +2284,7 @@ cudaError_t plan_rows(int32_t sms, int32_t rows, int32_t vocab, int32_t cap, Row
   g.chunk = round_up((vocab + nch - 1) / nch, 4);
   g.nch = (vocab + g.chunk - 1) / g.chunk;
   g.grid = (int32_t)std::min<int64_t>((int64_t)rows * g.nch, ctas);
+  g.whole = g.nch == 1 ? 1 : 0;
   g.smem_bytes = row_smem_bytes();
   *geo = g;
   return cudaSuccess;
@@ -2228,6 +2312,7 @@ cudaError_t launch_rows(const RowLaunch &l, const RowGeometry &geo, const Scratc
   a.vocab = l.vocab;
   a.nch = geo.nch;
   a.chunk = geo.chunk;
+  a.whole = geo.whole;
   a.mode = l.mode;
   a.cap = l.cap;
   a.fixed_k = l.fixed_k;
