@@ -264,6 +264,8 @@ struct Shared {
   uint32_t above;
   uint32_t inb;
   uint32_t last;  // this CTA finishes the row
+  float2 wst[kWarps];        // whole rows: each warp's (max, sum-exp)
+  uint32_t wgroups[kWarps];  // whole rows: candidate groups in each warp's region
   uint32_t unit;  // the unit this CTA works on
   int32_t urow, uk;  // its row and pool size
   int32_t plan_red[3][kWarps];  // plan: per-warp counts for the row order
@@ -1444,8 +1446,16 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
   // Everything the finish reads from global memory, issued together.
   const int np = a.nch * kWarps;
   float2 st = make_float2(-3.40282347e38f, 0.f);
-  if (tid < np) st = __ldcg(&a.warp_stats[(int64_t)row * np + tid]);
-  const int rcount = tid < np ? (int)__ldcg(&a.warp_cnt[(int64_t)row * np + tid]) : 0;
+  int rcount = 0;
+  if (a.whole) {  // the CTA's own warps: their tables are in shared memory
+    if (tid < kWarps) {
+      st = sh->wst[tid];
+      rcount = (int)sh->wgroups[tid];
+    }
+  } else if (tid < np) {
+    st = __ldcg(&a.warp_stats[(int64_t)row * np + tid]);
+    rcount = (int)__ldcg(&a.warp_cnt[(int64_t)row * np + tid]);
+  }
   const uint32_t rflags = __ldcg(&a.row_flags[row]);
   const float tf = a.row_tf[row];
   tabby_sampling_params prm = {};
@@ -2118,16 +2128,21 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
                        !(s <= 3.40282347e38f);
       const bool wbad = __any_sync(0xffffffffu, bad);
       if (lane == 0) {
-        const int64_t at = ((int64_t)row * a.nch + chunk) * kWarps + warp;
-        a.warp_stats[at] = make_float2(wm, ws);
-        a.warp_cnt[at] = (uint32_t)min(wcnt, regsize);
+        if (a.whole) {
+          sh->wst[warp] = make_float2(wm, ws);
+          sh->wgroups[warp] = (uint32_t)min(wcnt, regsize);
+        } else {
+          const int64_t at = ((int64_t)row * a.nch + chunk) * kWarps + warp;
+          a.warp_stats[at] = make_float2(wm, ws);
+          a.warp_cnt[at] = (uint32_t)min(wcnt, regsize);
+        }
         const uint32_t f = (wbad ? kFlagBadInput : 0u) | (wcnt > regsize ? kRowOverflow : 0u);
         if (f) atomicOr(&a.row_flags[row], f);
       }
     }
     __syncthreads();  // every thread's candidate groups and statistics are written
     if (tid == 0) {
-      __threadfence();  // ... and visible before the count (release)
+      if (!a.whole) __threadfence();  // ... and visible before the count (release)
       const bool last =
           a.whole || atomicAdd(&a.row_done[row], 1u) == (uint32_t)(a.nch - 1);
       // A unit that completes a row asks for its successor only after the finish, so a
