@@ -1033,6 +1033,8 @@ __device__ __forceinline__ void rank_sort_small(const uint64_t *cand, int n, int
   __syncthreads();
 }
 
+constexpr int kRankSortMax = 160;  // lists ranked by all-pairs counting (rank_sort_small)
+
 // Exact top-R (R = min(k, n)) with its order. Candidates are binned on their key
 // relative to the smallest one (2048 bins, the shift set by the key range); bins are
 // counted and turned into offsets in descending order; the bins down to the one that
@@ -1128,7 +1130,7 @@ __device__ __noinline__ int bin_rank_topk(uint64_t *cand, int n, int k, int capa
 }
 
 // The min(k, n) largest of cand[0, n) (k <= 1024), sorted descending, at cand[0, ...);
-// returns how many. Block-uniform call. Lists of at most 512 are ranked directly,
+// returns how many. Block-uniform call. Lists of at most kRankSortMax are ranked directly,
 // longer ones through the binned ranking; long runs of equal logits fall back to the
 // per-warp top-64 tree (pools up to 64) or the exact radix select and a sort.
 __device__ __forceinline__ int top_sorted(uint64_t *cand, int n, int k, int capacity,
@@ -1137,9 +1139,10 @@ __device__ __forceinline__ int top_sorted(uint64_t *cand, int n, int k, int capa
     __syncthreads();
     return 0;
   }
-  if (n <= kThreads && 2 * n <= capacity) {
-    // Small lists: rank every element against all the others, then move the result
-    // to the front.
+  if (n <= kRankSortMax && 2 * n <= capacity) {
+    // Short lists: rank every element against all the others (a pass over the list per
+    // thread; the binned ranking's fixed cost is lower from about 160 elements on), then
+    // move the result to the front.
     rank_sort_small(cand, n, min(k, n), cand + n);
     const int R = min(k, n);
     for (int i = threadIdx.x; i < R; i += kThreads) cand[i] = cand[n + i];
