@@ -117,6 +117,24 @@ TABBY_API int tabby_sample_rows_async(tabby_sampler *sampler, const float *d_log
                             void *stream);
 
 /*
+ * tabby_sample_rows_async with the draws made on the device: d_rng_state[r] is row r's
+ * SeededRandom state (sampler.ts:105-119; a new generator of seed s starts at s as
+ * uint32). Where sampleFromTopK calls random.next() -- a row with temperature > 0, a
+ * non-empty pool and no error -- the kernel advances d_rng_state[r] by one mulberry32
+ * step and uses u32 / 2^32 as u; greedy and failed rows leave it unchanged (the
+ * reference returns before drawing, sampler.ts:153,159-167). Nothing in the call
+ * depends on host state that changes between calls, so a decode step that calls it can
+ * be captured once in a CUDA graph and replayed (the per-launch epoch lives in the
+ * handle's device scratch). Moves the worker's per-token draw (inference.worker.ts:142,
+ * 165) onto the GPU.
+ */
+TABBY_API int tabby_sample_rows_rng_async(tabby_sampler *sampler, const float *d_logits,
+                                int64_t row_stride, int32_t rows, int32_t vocab,
+                                const tabby_sampling_params *d_params, uint32_t *d_rng_state,
+                                tabby_sample_outcome *d_out, int32_t *d_topk_ids,
+                                float *d_topk_values, int32_t topk_ld, void *stream);
+
+/*
  * Same computation from and to HOST buffers: copies logits/params/uniforms in, runs,
  * copies outcomes (and candidates when h_topk_ids/h_topk_values are non-NULL) back and
  * synchronises. Returns the first failing row's status (TABBY_EINPUT, ...) if any.

@@ -29,7 +29,6 @@ struct tabby_sampler {
   int32_t sms;
   Scratch scratch;     // per-row state of the row pass, carved from scratch_mem
   void *scratch_mem;
-  uint32_t epoch;      // launches on the scratch so far (the next launch is epoch + 1)
   cudaStream_t stream;  // used by the host-buffer entry points
   float *d_logits;
   tabby_sampling_params *d_params;
@@ -101,6 +100,7 @@ cudaError_t plan_and_launch(tabby_sampler *s, const RowLaunch &l, cudaStream_t s
     b.logits = l.logits + (int64_t)r0 * l.row_stride;
     if (b.params) b.params = l.params + r0;
     if (b.uniforms) b.uniforms = l.uniforms + r0;
+    if (b.rng_state) b.rng_state = l.rng_state + r0;
     if (b.out) b.out = l.out + r0;
     if (b.topk_ids) b.topk_ids = l.topk_ids + (int64_t)r0 * l.topk_ld;
     if (b.topk_values) b.topk_values = l.topk_values + (int64_t)r0 * l.topk_ld;
@@ -108,8 +108,6 @@ cudaError_t plan_and_launch(tabby_sampler *s, const RowLaunch &l, cudaStream_t s
     RowGeometry geo;
     cudaError_t err = tabby::plan_rows(s->sms, b.rows, b.vocab, s->cap, &geo);
     if (err != cudaSuccess) return err;
-    s->epoch = s->epoch + 1 == 0 ? 1 : s->epoch + 1;
-    b.epoch = s->epoch;
     err = tabby::launch_rows(b, geo, s->scratch, stream);
     if (err != cudaSuccess) return err;
   }
@@ -236,6 +234,38 @@ int tabby_sample_rows_async(tabby_sampler *s, const float *d_logits, int64_t row
   l.cap = s->cap;
   l.params = d_params;
   l.uniforms = d_uniforms;
+  l.out = d_out;
+  l.topk_ids = d_topk_ids;
+  l.topk_values = d_topk_values;
+  l.topk_ld = topk_ld;
+  cudaError_t err = plan_and_launch(s, l, (cudaStream_t)stream);
+  if (err != cudaSuccess) return cuda_fail(err, "row_kernel launch");
+  return TABBY_OK;
+}
+
+int tabby_sample_rows_rng_async(tabby_sampler *s, const float *d_logits, int64_t row_stride,
+                                int32_t rows, int32_t vocab, const tabby_sampling_params *d_params,
+                                uint32_t *d_rng_state, tabby_sample_outcome *d_out,
+                                int32_t *d_topk_ids, float *d_topk_values, int32_t topk_ld,
+                                void *stream) {
+  int st = check_rows(s, d_logits, row_stride, rows, vocab);
+  if (st) return st;
+  if (rows > 0 && (!d_params || !d_rng_state || !d_out))
+    return fail(TABBY_EINVAL, "params, rng_state and out must not be NULL");
+  if ((d_topk_ids || d_topk_values) && topk_ld < s->cap)
+    return fail(TABBY_EINVAL, "topk_ld (%d) must be >= max_top_k (%d)", topk_ld, s->cap);
+  if ((st = check_vocab_capacity(s, vocab))) return st;
+  DeviceScope scope(s->device);
+  if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+  RowLaunch l;
+  l.logits = d_logits;
+  l.row_stride = row_stride;
+  l.rows = rows;
+  l.vocab = vocab;
+  l.mode = tabby::kModeSample;
+  l.cap = s->cap;
+  l.params = d_params;
+  l.rng_state = d_rng_state;
   l.out = d_out;
   l.topk_ids = d_topk_ids;
   l.topk_values = d_topk_values;

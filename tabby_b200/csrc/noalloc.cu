@@ -36,7 +36,6 @@ struct DeviceState {
   bool ready = false;
   unsigned char *scratch = nullptr;  // device address of g_noalloc_scratch on this device
   int sms = 0;
-  uint32_t epoch = 0;  // launches on the array so far (calls on a device are serialised)
 };
 DeviceState g_devices[kMaxDevices];
 std::mutex g_setup_mutex;
@@ -135,8 +134,6 @@ extern "C" int tabby_sample_rows_noalloc(const float *d_logits, int64_t row_stri
     RowGeometry geo;
     err = plan_rows(st->sms, b.rows, vocab, max_top_k, &geo);
     if (err != cudaSuccess) return fail(TABBY_ECUDA, "row pass setup: %s", cudaGetErrorString(err));
-    st->epoch = st->epoch + 1 == 0 ? 1 : st->epoch + 1;
-    b.epoch = st->epoch;
     err = launch_rows(b, geo, scr, q);
     if (err != cudaSuccess)
       return fail(TABBY_ECUDA, "row kernel launch: %s", cudaGetErrorString(err));

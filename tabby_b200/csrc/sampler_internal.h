@@ -32,7 +32,8 @@ struct RowLaunch {
   int32_t topk_ld = 0;
   float *block = nullptr;
   int32_t block_ld = 0;
-  uint32_t epoch = 1;  // launch number on this scratch, never 0 (see Scratch)
+  uint32_t *rng_state = nullptr;  // kModeSample: per-row mulberry32 state on the device; u
+                                  // is drawn and the state advanced in place (no uniforms)
 };
 
 struct MergeLaunch {
@@ -64,11 +65,15 @@ constexpr int32_t kScratchWarps = 16;         // warps a CTA has
 
 // Global scratch of the row pass for up to max_rows rows, carved from one device
 // allocation (every section 256-byte aligned). It must be zero when first used; after
-// that every launch resets the row counters it plans and the unit counter of the next
-// launch, and tags its plan entries with its epoch (the caller's launch count on this
-// scratch, starting at 1 and never 0), so no clearing is needed between launches.
+// that every launch resets the row counters it plans, the launch's last take of a unit
+// resets the unit counter, and plan entries carry the launch's epoch, so no clearing is
+// needed between launches. The epoch lives in the scratch itself (sched[2]): a chunked
+// launch runs as epoch sched[2] + 1 (never 0) and its last take stores that number, so
+// the kernel's arguments do not change from call to call and a captured CUDA graph
+// replays correctly.
 struct Scratch {
-  uint32_t *sched = nullptr;                 // [2] unit counters (by launch parity)
+  uint32_t *sched = nullptr;                 // [4] unit counter, -, the last chunked
+                                             // launch's epoch, -
   unsigned long long *pos_entry = nullptr;   // [max_rows][2] epoch-tagged plan by position
   uint32_t *row_done = nullptr;              // [max_rows] chunks finished
   uint32_t *warp_cnt = nullptr;              // [max_rows][kScratchChunks * kScratchWarps]
@@ -82,7 +87,7 @@ struct Scratch {
 
   static constexpr size_t section(size_t bytes) { return (bytes + 255) / 256 * 256; }
   static constexpr size_t layout_bytes(int32_t rows) {
-    return section(8) + section(16 * (size_t)rows) + 4 * section(4 * (size_t)rows) +
+    return section(16) + section(16 * (size_t)rows) + 4 * section(4 * (size_t)rows) +
            section(4 * (size_t)rows * kScratchChunks * kScratchWarps) +
            section(8 * (size_t)rows * kScratchChunks * kScratchWarps) +
            section(16 * (size_t)rows * kScratchGroups) + section(4 * (size_t)rows * kScratchGroups);
@@ -93,7 +98,7 @@ struct Scratch {
     unsigned char *p = static_cast<unsigned char *>(base);
     const size_t r = (size_t)rows;
     s.sched = reinterpret_cast<uint32_t *>(p);
-    p += section(8);
+    p += section(16);
     s.pos_entry = reinterpret_cast<unsigned long long *>(p);
     p += section(16 * r);
     s.row_done = reinterpret_cast<uint32_t *>(p);

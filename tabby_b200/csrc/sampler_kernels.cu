@@ -288,6 +288,8 @@ struct Shared {
   uint64_t samp[64];  // sorted sample of the candidate buffer
   int32_t off[32];  // merge: first candidate of each slice
   int32_t cnt[32];  // merge: candidates of each slice
+  double rng_u;     // the row's draw in device-RNG mode
+  uint32_t epoch;   // this launch's number (thread 0's copy for the plan)
 };
 
 // ------------------------------------------------------------------------------------
@@ -1198,10 +1200,11 @@ struct PassArgs {
   int32_t topk_ld;
   float *block;
   int32_t block_ld;
-  uint32_t *sched;       // [2] unit counters; launch e uses sched[e & 1], clears the other
+  uint32_t *sched;       // [0] unit counter, [2] the last chunked launch's epoch (the
+                         // launch's last take of a unit resets [0] and stores [2])
   unsigned long long *pos_entry;  // [rows][2] by processing position, each word tagged
                                  // with the epoch: (epoch, row << 12 | k), (epoch, tf)
-  uint32_t epoch;        // this launch's number (never 0)
+  uint32_t *rng_state;   // kModeSample: per-row mulberry32 state, or NULL (uniforms)
   uint32_t *row_done;    // [rows] chunks finished
   uint32_t *warp_cnt;    // [rows][nch * kWarps] candidate groups of each (chunk, warp)
   uint32_t *row_flags;   // [rows] kFlagBadInput | kRowOverflow
@@ -1373,7 +1376,7 @@ __device__ __noinline__ void plan_row(const PassArgs &a, int row, uint64_t *cand
     a.row_tf[row] = tf;
     a.row_tf_lo[row] = tf_lo;
     __threadfence();
-    const unsigned long long tag = (unsigned long long)a.epoch << 32;
+    const unsigned long long tag = (unsigned long long)sh->epoch << 32;
     st_release_u64(&a.pos_entry[2 * pos], tag | ((unsigned long long)row << 12) | (uint32_t)k);
     st_release_u64(&a.pos_entry[2 * pos + 1], tag | __float_as_uint(tf));
   }
@@ -1438,6 +1441,17 @@ __device__ __noinline__ int rescan_row(const float *rowp, int vocab, int k, floa
   return (int)sh->count;
 }
 
+// SeededRandom.next() (sampler.ts:112-118, mulberry32) on a device-resident state: advances
+// the state and returns u32 / 2^32.
+__device__ __forceinline__ double rng_next(uint32_t *state) {
+  const uint32_t s = *state + 0x6d2b79f5u;
+  *state = s;
+  uint32_t t = s;
+  t = (t ^ (t >> 15)) * (t | 1u);
+  t ^= t + (t ^ (t >> 7)) * (t | 61u);
+  return (double)(t ^ (t >> 14)) / 4294967296.0;
+}
+
 // The finish of one row, run by the CTA whose unit completed it (block-uniform call).
 __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint64_t *cand,
                                         uint32_t *hist, Shared *sh) {
@@ -1465,7 +1479,7 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
   double uni = 0.0;
   if (a.mode == kModeSample) {
     prm = a.params[row];
-    uni = a.uniforms[row];
+    if (!a.rng_state) uni = a.uniforms[row];
     if (isnan(prm.temperature) || isnan(prm.top_p)) pflags = kFlagBadParams;
   }
   // Region counts (one a thread) and their exclusive offsets in the gathered list, kept
@@ -1665,6 +1679,16 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
       if (2 * lane + 1 < kk) a.topk_values[(int64_t)row * a.topk_ld + 2 * lane + 1] = x1;
     }
     FTRACE(row, 3);
+#ifndef TABBY_NORNG
+    if (a.rng_state) {
+      // The reference draws only when it samples: after the empty-pool throw and the
+      // greedy return (sampler.ts:153,159-167).
+      double un = 0.0;
+      if (lane == 0 && status == TABBY_OK && kk > 0 && prm.temperature > 0)
+        un = rng_next(&a.rng_state[row]);
+      uni = __shfl_sync(0xffffffffu, un, 0);
+    }
+#endif
     finalize_warp(id0, id1, x0, x1, kk, max_logit, sum_exp, prm, uni,
                   reinterpret_cast<double *>(hist), &a.out[row], status);
     FTRACE(row, 4);
@@ -1716,6 +1740,16 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
   if (a.topk_values)
     for (int i = tid; i < kk; i += kThreads) a.topk_values[(int64_t)row * a.topk_ld + i] = vals[i];
   FTRACE(row, 3);
+#ifndef TABBY_NORNG
+  if (a.rng_state) {  // drawn only when the reference draws (see the warp path)
+    if (tid == 0)
+      sh->rng_u = status == TABBY_OK && kk > 0 && prm.temperature > 0
+                      ? rng_next(&a.rng_state[row])
+                      : 0.0;
+    __syncthreads();
+    uni = sh->rng_u;
+  }
+#endif
   finalize_sample(ids, vals, kk, max_logit, sum_exp, prm, uni, cum, scaled, sh,
                   &a.out[row], status);
   FTRACE(row, 4);
@@ -1835,8 +1869,24 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
   // publishes each as an epoch-tagged position entry; a unit waits only for its own row's entry, so
   // streaming starts as soon as the first rows are planned. The launch is cooperative:
   // every CTA is resident, so every awaited row gets planned.
-  if (blockIdx.x == 0 && tid == 0) a.sched[(a.epoch + 1) & 1] = 0;  // the next launch's
-  uint32_t *sched = a.sched + (a.epoch & 1);
+  uint32_t *sched = a.sched;  // the unit counter
+  // Chunked rows need this launch's epoch (one more than the last chunked launch's, kept
+  // in the scratch; never 0), which tags the plan entries; whole rows have no plan.
+  if (tid == 0 && !a.whole) {
+    uint32_t e = __ldcg(&a.sched[2]) + 1u;
+    sh->epoch = e == 0u ? 1u : e;  // read before this CTA's first unit is taken
+  }
+  // Every CTA takes units until one lies past the end, so a launch makes exactly
+  // units + gridDim.x takes; the last one resets the counter for the next launch and
+  // records the epoch (every CTA has read it by then).
+  auto take = [&]() -> int {  // thread 0 only
+    const uint32_t t = atomicAdd(sched, 1u);
+    if (t == (uint32_t)(a.rows * a.nch) + gridDim.x - 1u) {
+      *sched = 0u;
+      if (!a.whole) a.sched[2] = sh->epoch;
+    }
+    return (int)t;
+  };
   if (!a.whole)
     for (int r = blockIdx.x; r < a.rows; r += gridDim.x) plan_row(a, r, fin, hist, sh);
 
@@ -1868,8 +1918,9 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
     for (;;) {  // both words of this launch's entry: one round trip once planned
       w0 = ld_acquire_u64(&a.pos_entry[2 * ri]);
       w1 = ld_acquire_u64(&a.pos_entry[2 * ri + 1]);
-      if ((uint32_t)(w0 >> 32) == a.epoch && (uint32_t)(w1 >> 32) == a.epoch) break;
+      if ((uint32_t)(w0 >> 32) == sh->epoch && (uint32_t)(w1 >> 32) == sh->epoch) break;
       if (++spins > (1u << 24)) {
+        take();  // this CTA's take past the end, so the count of takes stays exact
         nid = units;
         return;
       }
@@ -1880,7 +1931,7 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
     ntf = __uint_as_float((uint32_t)w1);
   };
   if (tid == 0) {
-    nid = (int)atomicAdd(sched, 1u);
+    nid = take();
     unit_info();
     sh->unit = (uint32_t)nid;
     sh->urow = nrow;
@@ -1894,7 +1945,7 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
       // a CTA busy finishing never holds on to a unit other CTAs could take.
       __syncthreads();
       if (tid == 0) {
-        nid = (int)atomicAdd(sched, 1u);
+        nid = take();
         unit_info();
         sh->unit = (uint32_t)nid;
         sh->urow = nrow;
@@ -2151,7 +2202,7 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
       // A unit that completes a row asks for its successor only after the finish, so a
       // CTA busy finishing never holds on to a unit other CTAs could take.
       if (!last) {
-        nid = (int)atomicAdd(sched, 1u);
+        nid = take();
         unit_info();  // the next unit's row data
       }
       sh->last = last ? 1u : 0u;
@@ -2353,7 +2404,7 @@ cudaError_t launch_rows(const RowLaunch &l, const RowGeometry &geo, const Scratc
   a.warp_stats = scr.warp_stats;
   a.row_gval = scr.row_gval;
   a.row_gidx = scr.row_gidx;
-  a.epoch = l.epoch;
+  a.rng_state = l.rng_state;
   cudaError_t err = prepare_row_kernel(geo.smem_bytes);
   if (err != cudaSuccess) return err;
   // Cooperative launch: all CTAs resident at once (units wait on rows other CTAs plan).

@@ -213,6 +213,22 @@ class Sampler:
             topk_values.data_ptr() if topk_values is not None else None, ld,
             self._stream() if stream is None else stream))
 
+    def sample_rows_rng_async(self, logits, params_dev, rng_state_dev, out_dev, topk_ids=None,
+                              topk_values=None, stream: Optional[int] = None) -> None:
+        """tabby_sample_rows_rng_async on torch tensors (no sync): u drawn on the device
+        from ``rng_state_dev`` (uint32 mulberry32 state per row, advanced in place exactly
+        where SeededRandom.next() would be called). Graph-capturable."""
+        logits = self._check_logits(logits)
+        rows, vocab = logits.shape
+        ld = topk_ids.shape[1] if topk_ids is not None else (
+            topk_values.shape[1] if topk_values is not None else 0)
+        check(lib().tabby_sample_rows_rng_async(
+            self._h, logits.data_ptr(), logits.stride(0), rows, vocab, params_dev.data_ptr(),
+            rng_state_dev.data_ptr(), out_dev.data_ptr(),
+            topk_ids.data_ptr() if topk_ids is not None else None,
+            topk_values.data_ptr() if topk_values is not None else None, ld,
+            self._stream() if stream is None else stream))
+
     def sample_batch(self, logits, params: Union[SamplingParams, Sequence[SamplingParams]],
                      rng, return_topk: bool = False) -> SampleBatch:
         """Sample one token per row. ``logits`` is a CUDA tensor [rows, vocab] (device

@@ -20,8 +20,9 @@ def declared_symbols():
 
 def test_header_declares_the_entry_points():
     names = declared_symbols()
-    assert len(names) == 12, names
+    assert len(names) == 13, names
     for n in ("tabby_sampler_create", "tabby_sample_rows_async", "tabby_topk_rows_async",
+              "tabby_sample_rows_rng_async",
               "tabby_shard_local_async", "tabby_shard_merge_async", "tabby_sample_from_topk",
               "tabby_sample_rows_noalloc", "tabby_last_error"):
         assert n in names
@@ -81,6 +82,11 @@ def test_argument_errors_without_a_device():
     # Zero rows is a no-op.
     assert L.tabby_sample_rows_noalloc(None, 100, 0, 100, 64, None, None, None, None, None, 0,
                                        None) == _lib.TABBY_OK
+    # Device-RNG entry point: a NULL handle is refused before any CUDA call.
+    rc = L.tabby_sample_rows_rng_async(None, ctypes.c_void_p(16), 100, 1, 100,
+                                       ctypes.c_void_p(16), ctypes.c_void_p(16),
+                                       ctypes.c_void_p(16), None, None, 0, None)
+    assert rc == _lib.TABBY_EINVAL and b"NULL" in L.tabby_last_error()
 
 
 def test_sampler_create_without_gpu_fails_cleanly():
