@@ -1679,7 +1679,6 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
       if (2 * lane + 1 < kk) a.topk_values[(int64_t)row * a.topk_ld + 2 * lane + 1] = x1;
     }
     FTRACE(row, 3);
-#ifndef TABBY_NORNG
     if (a.rng_state) {
       // The reference draws only when it samples: after the empty-pool throw and the
       // greedy return (sampler.ts:153,159-167).
@@ -1688,7 +1687,6 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
         un = rng_next(&a.rng_state[row]);
       uni = __shfl_sync(0xffffffffu, un, 0);
     }
-#endif
     finalize_warp(id0, id1, x0, x1, kk, max_logit, sum_exp, prm, uni,
                   reinterpret_cast<double *>(hist), &a.out[row], status);
     FTRACE(row, 4);
@@ -1740,7 +1738,6 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
   if (a.topk_values)
     for (int i = tid; i < kk; i += kThreads) a.topk_values[(int64_t)row * a.topk_ld + i] = vals[i];
   FTRACE(row, 3);
-#ifndef TABBY_NORNG
   if (a.rng_state) {  // drawn only when the reference draws (see the warp path)
     if (tid == 0)
       sh->rng_u = status == TABBY_OK && kk > 0 && prm.temperature > 0
@@ -1749,7 +1746,6 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
     __syncthreads();
     uni = sh->rng_u;
   }
-#endif
   finalize_sample(ids, vals, kk, max_logit, sum_exp, prm, uni, cum, scaled, sh,
                   &a.out[row], status);
   FTRACE(row, 4);
