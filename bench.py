@@ -389,65 +389,6 @@ def run_sweep(args):
     x, p, u = synth.config("c4", seed=0)
     pool_rows = 420
     reps = (pool_rows + ROWS - 1) // ROWS
-    xp = np.ascontiguousarray(np.tile(x, (reps, 1))[:pool_rows])
-    pool = torch.from_numpy(xp).to(dev)
-    sampler = Sampler(0, max_top_k=CAP, max_rows=ROWS, max_vocab=VOCAB)
-    L = lib()
-    sptr = torch.cuda.current_stream(dev).cuda_stream
-    peak, peak_kind = measured_peak()
-    points = []
-    for b in SWEEP_ROWS:
-        pb = torch.from_numpy(p[:b].view(np.uint8).copy()).to(dev)
-        ub = torch.from_numpy(u[:b].copy()).to(dev)
-        out = torch.empty(b * OUTCOME_DTYPE.itemsize, dtype=torch.uint8, device=dev)
-        windows = pool_rows - b + 1
-        stride = max(1, b)
-
-        def step(i):
-            r0 = (i * stride) % windows
-            check(L.tabby_sample_rows_async(sampler.handle, pool[r0].data_ptr(), VOCAB, b, VOCAB,
-                                            pb.data_ptr(), ub.data_ptr(), out.data_ptr(), None,
-                                            None, 0, sptr))
-
-        for i in range(max(args.warmup, 3)):
-            step(i)
-        torch.cuda.synchronize(dev)
-        steps = max(50, min(args.steps, 1000))
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for i in range(steps):
-            step(i)
-        e1.record()
-        torch.cuda.synchronize(dev)
-        us = e0.elapsed_time(e1) * 1e3 / steps
-        gbs = b * VOCAB * 4 / (us * 1e-6) / 1e9
-        points.append({"rows": b, "us_per_call": round(us, 2),
-                       "rows_per_s": round(b / (us * 1e-6)), "gbs": round(gbs, 1),
-                       "frac_of_peak": round(gbs / peak, 3)})
-    sampler.close()
-    print(json.dumps({"sweep": "c4 rows, V=151936, pool cap 1024, outcomes only",
-                      "peak_gbs": peak, "peak_kind": peak_kind, "points": points}), flush=True)
-    return 0
-
-
-SWEEP_ROWS = (1, 2, 4, 8, 16, 32, 64, 128, 256)
-
-
-def run_sweep(args):
-    """Batch sweep on one GPU: B rows of the c4 workload per call for B in SWEEP_ROWS.
-    Each call reads a different window of a 420-row resident pool (255 MB > L2), so every
-    call reads HBM; device-timed with CUDA events over the calls."""
-    import torch
-
-    from tabby_b200 import Sampler, synth
-    from tabby_b200._lib import OUTCOME_DTYPE, check, lib
-
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    x, p, u = synth.config("c4", seed=0)
-    pool_rows = 420
-    reps = (pool_rows + ROWS - 1) // ROWS
     pool = torch.from_numpy(np.ascontiguousarray(np.tile(x, (reps, 1))[:pool_rows])).to(dev)
     sampler = Sampler(0, max_top_k=CAP, max_rows=ROWS, max_vocab=VOCAB)
     L = lib()
@@ -496,7 +437,6 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--sweep", action="store_true", help="batch sweep B=1..256 on one GPU")
     ap.add_argument("--sweep", action="store_true", help="batch sweep B=1..256 on one GPU")
     ap.add_argument("--profile", action="store_true",
                     help="only warm-up + timed steps (for ncu): no heat loop, e2e or CPU leg")
