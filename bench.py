@@ -20,6 +20,7 @@ draw for every row -- over one batch of seeded synthetic logits.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--profile]
   python bench.py --sweep    rows/s and HBM rate for B in 1..256 (c4 rows), one JSON line
+  python bench.py --softmax  softmax_rows (attention scores) time and HBM rate, one JSON line
 """
 from __future__ import annotations
 
@@ -429,6 +430,56 @@ def run_sweep(args):
     return 0
 
 
+SOFTMAX_SHAPES = (  # (label, rows, row_len, causal_period, causal_offset)
+    ("decode: 14 heads x 1 query, context 4096", 14, 4096, 1, 4095),
+    ("prefill: 14 heads x 2048 queries, causal", 14 * 2048, 2048, 2048, 0),
+    ("batch 64 x 14 heads x 1 query, context 8192", 64 * 14, 8192, 0, 0),
+)
+
+
+def run_softmax(args):
+    """softmax_rows (the attention-score softmax next to the sampler, softmax_rows.wgsl):
+    device time per call and HBM rate at 8 bytes per element (one read, one write), on
+    inputs rotated over enough copies to exceed L2."""
+    import torch
+
+    from tabby_b200._lib import check, lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L = lib()
+    sptr = torch.cuda.current_stream(dev).cuda_stream
+    peak, peak_kind = measured_peak()
+    points = []
+    for label, rows, n, period, offset in SOFTMAX_SHAPES:
+        nbuf = max(2, -(-256 * 2**20 // (rows * n * 4)))
+        bufs = [torch.randn(rows, n, device=dev) * 4 for _ in range(nbuf)]
+
+        def step(i):
+            check(L.tabby_softmax_rows_async(bufs[i % nbuf].data_ptr(), rows, n, period, offset,
+                                             sptr))
+
+        for i in range(max(args.warmup, 3)):
+            step(i)
+        torch.cuda.synchronize(dev)
+        steps = max(50, min(args.steps, 500))
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(steps):
+            step(i)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) * 1e3 / steps
+        gbs = rows * n * 8 / (us * 1e-6) / 1e9
+        points.append({"shape": label, "us_per_call": round(us, 2), "gbs": round(gbs, 1),
+                       "frac_of_peak": round(gbs / peak, 3)})
+        del bufs
+    print(json.dumps({"softmax_rows": points, "peak_gbs": peak, "peak_kind": peak_kind}),
+          flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -438,6 +489,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="batch sweep B=1..256 on one GPU")
+    ap.add_argument("--softmax", action="store_true", help="softmax_rows shapes on one GPU")
     ap.add_argument("--profile", action="store_true",
                     help="only warm-up + timed steps (for ncu): no heat loop, e2e or CPU leg")
     args = ap.parse_args()
@@ -448,6 +500,8 @@ def main():
         return run_reference(args, rank, world)
     if args.sweep:
         return run_sweep(args) if rank == 0 else 0
+    if args.softmax:
+        return run_softmax(args) if rank == 0 else 0
     return run_ours(args, rank, local_rank, world)
 
 

@@ -192,6 +192,18 @@ TABBY_API int tabby_sample_from_topk(const int32_t *ids, const float *logits, in
                            float sum_exp, const tabby_sampling_params *params, double uniform,
                            tabby_sample_outcome *out);
 
+/*
+ * Row softmax in place over d_x [n_rows, row_len] fp32 (softmax_rows.wgsl, the attention
+ * score softmax of ForwardPass; CPU form cpu.ts softmaxRows). With causal_period != 0 row
+ * r keeps its first causal_offset + (r % causal_period) + 1 entries (rows are (head,
+ * query)) and the rest are set to 0; causal_period == 0 softmaxes whole rows. Entries:
+ * exp(x - max) / sum over the kept part, fp32. Requires row_len >= 1 and
+ * causal_offset + causal_period <= row_len (the shader would read past the row).
+ * No handle needed; asynchronous on `stream`.
+ */
+TABBY_API int tabby_softmax_rows_async(float *d_x, int32_t n_rows, int32_t row_len,
+                                int32_t causal_period, int32_t causal_offset, void *stream);
+
 /* Largest max_top_k tabby_sample_rows_noalloc accepts (its scratch array is fixed). */
 #define TABBY_NOALLOC_MAX_TOP_K 256
 

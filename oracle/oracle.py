@@ -269,3 +269,25 @@ def shard_merge(blocks: np.ndarray, shards: int, params: np.ndarray, uniforms: n
         tids[r, :k] = ids
         tvals[r, :k] = vals
     return out, tids, tvals
+
+
+def softmax_rows(x: np.ndarray, n_rows: int, row_len: int, causal_period: int = 0,
+                 causal_offset: int = 0) -> np.ndarray:
+    """Restatement of cpu.ts:238-264 (softmaxRows, the CPU form of softmax_rows.wgsl) with
+    its fp32 rounding (f32 = Math.fround, cpu.ts:17): per row, max over the kept prefix,
+    e = f32(exp(f32(x - max))) with the exp in float64, sum = f32(sum + e) left to right,
+    inv = f32(1 / sum), out = f32(e * inv); entries past the prefix become 0."""
+    src = np.ascontiguousarray(x, np.float32).reshape(n_rows, row_len)
+    out = src.copy()
+    for r in range(n_rows):
+        valid = causal_offset + (r % causal_period) + 1 if causal_period else row_len
+        row = src[r, :valid]
+        mx = np.float32(row.max())
+        e = np.exp((row - mx).astype(np.float32).astype(np.float64)).astype(np.float32)
+        s = np.float32(0.0)
+        for v in e:  # left to right, every step rounded to fp32
+            s = np.float32(s + v)
+        inv = np.float32(np.float64(1.0) / np.float64(s))
+        out[r, :valid] = (e * inv).astype(np.float32)
+        out[r, valid:] = 0.0
+    return out

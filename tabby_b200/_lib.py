@@ -70,6 +70,7 @@ SIGNATURES = {
     "tabby_sampler_destroy": ([_P], ctypes.c_int),
     "tabby_sample_rows_async": (
         [_P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _I32, _P], ctypes.c_int),
+    "tabby_softmax_rows_async": ([_P, _I32, _I32, _I32, _I32, _P], ctypes.c_int),
     "tabby_sample_rows_rng_async": (
         [_P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _I32, _P], ctypes.c_int),
     "tabby_sample_rows": ([_P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _I32], ctypes.c_int),

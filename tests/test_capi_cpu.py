@@ -20,9 +20,9 @@ def declared_symbols():
 
 def test_header_declares_the_entry_points():
     names = declared_symbols()
-    assert len(names) == 13, names
+    assert len(names) == 14, names
     for n in ("tabby_sampler_create", "tabby_sample_rows_async", "tabby_topk_rows_async",
-              "tabby_sample_rows_rng_async",
+              "tabby_sample_rows_rng_async", "tabby_softmax_rows_async",
               "tabby_shard_local_async", "tabby_shard_merge_async", "tabby_sample_from_topk",
               "tabby_sample_rows_noalloc", "tabby_last_error"):
         assert n in names
@@ -82,6 +82,10 @@ def test_argument_errors_without_a_device():
     # Zero rows is a no-op.
     assert L.tabby_sample_rows_noalloc(None, 100, 0, 100, 64, None, None, None, None, None, 0,
                                        None) == _lib.TABBY_OK
+    # Row softmax: shapes the shader would read past are refused before any CUDA call.
+    assert L.tabby_softmax_rows_async(ctypes.c_void_p(16), 4, 8, 4, 5, None) == _lib.TABBY_EINVAL
+    assert L.tabby_softmax_rows_async(ctypes.c_void_p(16), 4, 0, 0, 0, None) == _lib.TABBY_EINVAL
+    assert L.tabby_softmax_rows_async(None, 0, 8, 0, 0, None) == _lib.TABBY_OK
     # Device-RNG entry point: a NULL handle is refused before any CUDA call.
     rc = L.tabby_sample_rows_rng_async(None, ctypes.c_void_p(16), 100, 1, 100,
                                        ctypes.c_void_p(16), ctypes.c_void_p(16),
