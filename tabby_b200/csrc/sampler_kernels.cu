@@ -5,22 +5,28 @@
 // topk_partial + topk_select, i.e. k+4 passes over the row. Here every logit is read
 // from HBM once, in one streaming pass:
 //
-//   row_kernel     one cooperative launch, two 512-thread CTAs per SM.
-//     plan phase   CTA c plans rows c, c + grid, ...: resets the row's counters, fixes
-//                  its pool size and its place in the processing order, estimates a
-//                  filter threshold from 2048 logits sampled in 32 runs spread over the
-//                  row, and publishes the row with a per-launch ready flag.
-//     units        CTAs take (row, chunk) units from a global counter, waiting only for
-//                  their own row's plan. Each warp streams its part of the chunk through
-//                  a 3-stage cp.async ring in shared memory, keeps online max and
-//                  sum(exp(x - max)) per thread (packed f32x2 arithmetic) and appends
-//                  every float4 group holding a logit at or above the threshold to its
-//                  own region of the row's candidate list; no block barrier until the
-//                  chunk ends. The unit that completes a row finishes it: merges the
-//                  per-warp statistics, expands the groups into 64-bit composites
-//                  (order-preserving key, inverted index), checks the estimate (falling
-//                  back to an exact re-filter), keeps and sorts the k best (binned
-//                  ranking) and runs sampleFromTopK in float64 (finalize.cuh).
+//   row_kernel     one launch, at most two 512-thread CTAs per SM. Rows are cut into
+//                  chunks only until the units cover ~0.8 of the resident CTAs.
+//     whole rows   (large batches) CTAs take rows from a counter; each warp streams its
+//                  16th of the row; the threshold comes from every warp's first
+//                  iteration (8192 logits spread over the row) while the second is in
+//                  flight; the CTA finishes its own row. No inter-CTA waits.
+//     chunked      (small batches) a plan phase (CTA c plans rows c, c + grid, ...:
+//                  resets the row's counters, fixes its pool size and its place in the
+//                  processing order, estimates the threshold from 2048 logits sampled
+//                  in 32 runs, publishes epoch-tagged entries), then CTAs take (row,
+//                  chunk) units, waiting only for their own row's entry (cooperative
+//                  launch: all CTAs resident); the unit that completes a row finishes it.
+//     streaming    each warp streams through a 3-stage cp.async ring in shared memory,
+//                  keeps online max and sum(exp(x - max)) per thread (packed f32x2
+//                  arithmetic) and appends every float4 group holding a logit at or
+//                  above the threshold to its own region of the row's candidate list;
+//                  no block barrier until the segment ends.
+//     finish       merges the per-warp statistics, expands the groups into 64-bit
+//                  composites (order-preserving key, inverted index), checks the
+//                  estimate (falling back to an exact re-filter), keeps and sorts the k
+//                  best (binned ranking) and runs sampleFromTopK in float64
+//                  (finalize.cuh); with a device RNG state the draw is made here.
 //   merge_kernel   the vocab-sharded finish: merges all-gathered per-shard blocks.
 //
 // Selection works on the raw logits; temperature only enters the float64 finalize,
