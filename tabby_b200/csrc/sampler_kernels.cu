@@ -2087,30 +2087,23 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
       // Groups holding a logit >= tf go to the warp's region whole (the value check per
       // logit happens in the finish).
       if (k > 0 && __any_sync(0xffffffffu, im >= tf)) {
-        uint32_t hg = 0;
         const int rem = full ? kWarpIter : wn - it * kWarpIter - lane;
-#pragma unroll
-        for (int q = 0; q < kVec; q++) hg |= (gm[q] >= tf && q * 32 < rem) ? (1u << q) : 0u;
-        const int nh = __popc(hg);
-        int incl = nh;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int t = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += t;
-        }
-        int slot = wcnt + incl - nh;
         const int base0 = gbase + 4 * (it * kWarpIter + lane);
+        const uint32_t below = (1u << lane) - 1u;
+        // One ballot a column of groups: slots in (column, lane) order.
 #pragma unroll
         for (int q = 0; q < kVec; q++) {
-          if ((hg >> q) & 1u) {
+          const bool hit = gm[q] >= tf && q * 32 < rem;
+          const uint32_t mask = __ballot_sync(0xffffffffu, hit);
+          if (hit) {
+            const int slot = wcnt + __popc(mask & below);
             if (slot < regsize) {
               rgv[slot] = v[q];
               rgi[slot] = base0 + 4 * 32 * q;
             }
-            slot++;
           }
+          wcnt += __popc(mask);
         }
-        wcnt += __shfl_sync(0xffffffffu, incl, 31);
       }
     };
     using I0 = std::integral_constant<int, 0>;
