@@ -1794,9 +1794,8 @@ __device__ __forceinline__ unsigned long long f2_ex2(unsigned long long v) {
 // stage 0 holds when this runs (block-uniform call). Each thread keeps the top two
 // composites of its up to 16 logits; the rr-th largest of those 1024 is at or below the
 // sample's rr-th largest, so the estimate errs towards more candidates. The rank rule is
-// the plan's (rr = min(k, ceil(mu + 4 sqrt(mu) + 6)), mu = k * sample / vocab;
-// rr2 = min(4 rr, 1023) for the re-filter). buf (2048 slots) and hist must not overlap
-// stages 0 and 1.
+// the plan's (rr = min(k, ceil(mu + 4 sqrt(mu) + 6)), mu = k * sample / vocab). buf
+// (2048 slots) and hist must not overlap stages 0 and 1.
 __device__ __noinline__ float whole_threshold(const PassArgs &a, int row, int k, uint32_t sslot0,
                                               int wn, int seg, int ngroups, int gbase,
                                               uint64_t *buf, uint32_t *hist, Shared *sh) {
@@ -1828,26 +1827,23 @@ __device__ __noinline__ float whole_threshold(const PassArgs &a, int row, int k,
   }
   __syncthreads();
   float tf = -__int_as_float(0x7f800000);  // no estimate: every logit is a candidate
-  float tf_lo = tf;
   if (k > 0) {
     const float mu = (float)k * (float)ns / (float)a.vocab;
     const int rr = min(k, (int)ceilf(mu + 4.f * sqrtf(mu) + 6.f));
     if (rr >= 1 && rr < 2 * kThreads && rr < ns) {
-      const int rr2 = min(4 * rr, 2 * kThreads - 1);
-      uint64_t thr, thr2;
-      if (bin_rank_topk(buf, 2 * kThreads, rr2, 4 * kThreads, hist, sh) >= 0) {
+      // Only rank rr is ranked (a ranking down to a safer rank cost more than the rare
+      // re-filter it would shorten): the re-filter of a whole row starts from every logit.
+      uint64_t thr;
+      if (bin_rank_topk(buf, 2 * kThreads, rr, 4 * kThreads, hist, sh) >= 0)
         thr = buf[rr - 1];
-        thr2 = buf[rr2 - 1];
-      } else {
-        thr = thr2 = select_top(buf, 2 * kThreads, rr, hist, sh);
-      }
+      else
+        thr = select_top(buf, 2 * kThreads, rr, hist, sh);
       if ((thr >> 32) != 0ull) tf = float_of_key((uint32_t)(thr >> 32));
-      if ((thr2 >> 32) != 0ull) tf_lo = float_of_key((uint32_t)(thr2 >> 32));
     }
   }
   if (tid == 0) {
     a.row_tf[row] = tf;
-    a.row_tf_lo[row] = tf_lo;
+    a.row_tf_lo[row] = -__int_as_float(0x7f800000);
   }
   __syncthreads();  // buf and hist are free again
   return tf;
