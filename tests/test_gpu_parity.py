@@ -284,7 +284,8 @@ def test_threshold_estimate_failures(torch_cuda, oracle, rows):
     32 runs of 16 spread over the row) is wrong in both directions: too high (the sampled
     groups hold the largest logits, so fewer than k logits pass) and too low (they hold the
     smallest, so the candidates overflow the row's list). Both must end in the exact result
-    through the re-filter. Small batches split rows into more chunks than 256 rows do."""
+    through the re-filter. Small batches split rows into chunks (plan sample); 256 rows are
+    taken whole (the first iteration of every warp is the sample): both layouts are marked."""
     g = np.random.default_rng(17)
     vocab = 151936
     ngroups = vocab // 4
@@ -292,6 +293,10 @@ def test_threshold_estimate_failures(torch_cuda, oracle, rows):
     for run in range(32):
         start = min(max((2 * run + 1) * ngroups // 64 - 8, 0), ngroups - 16)
         sampled[4 * start:4 * (start + 16)] = True
+    # Whole rows (256 rows a launch) sample the first 128 groups of each warp's 16th.
+    seg = (ngroups + 15) // 16
+    for w in range(16):
+        sampled[4 * w * seg:4 * min(w * seg + 128, ngroups)] = True
     x = g.standard_normal((rows, vocab)).astype(np.float32)
     x[0::2, sampled] += 20.0   # too-high estimate
     x[1::2, sampled] -= 20.0   # too-low estimate
