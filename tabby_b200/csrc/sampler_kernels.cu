@@ -1959,6 +1959,11 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
     if (unit >= units) break;
 #ifdef TABBY_TRACE
     UTRACE(uj, 0, NOW());
+    if (tid == 0 && blockIdx.x < kUnitTraceCtas && uj < kUnitTraceUnits) {
+      uint32_t smid;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+      g_lcyc[(blockIdx.x * kUnitTraceUnits + uj) * 4] = smid | ((unsigned long long)row << 32);
+    }
 #endif
     const int ri = unit / a.nch;
     const int chunk = unit - ri * a.nch;
