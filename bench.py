@@ -439,8 +439,8 @@ SOFTMAX_SHAPES = (  # (label, rows, row_len, causal_period, causal_offset)
 
 def run_softmax(args):
     """softmax_rows (the attention-score softmax next to the sampler, softmax_rows.wgsl):
-    device time per call and HBM rate at 8 bytes per element (one read, one write), on
-    inputs rotated over enough copies to exceed L2."""
+    device time per call and HBM rate (4 bytes read per kept entry, 4 written per entry),
+    on inputs rotated over enough copies to exceed L2."""
     import torch
 
     from tabby_b200._lib import check, lib
@@ -471,7 +471,12 @@ def run_softmax(args):
         e1.record()
         torch.cuda.synchronize(dev)
         us = e0.elapsed_time(e1) * 1e3 / steps
-        gbs = rows * n * 8 / (us * 1e-6) / 1e9
+        # Bytes: the kept prefix of every row is read, every entry is written.
+        if period:
+            kept = sum(min(offset + (r % period) + 1, n) for r in range(period)) * (rows // period)
+        else:
+            kept = rows * n
+        gbs = (kept * 4 + rows * n * 4) / (us * 1e-6) / 1e9
         points.append({"shape": label, "us_per_call": round(us, 2), "gbs": round(gbs, 1),
                        "frac_of_peak": round(gbs / peak, 3)})
         del bufs
