@@ -85,6 +85,59 @@ __global__ void __launch_bounds__(kSmThreads) softmax_rows_reg(float *x, int n_r
   for (int i = valid + tid; i < row_len; i += kSmThreads) p[i] = 0.f;  // masked tail
 }
 
+// The same with float4 loads and stores (row_len a multiple of 4, x 16-byte aligned):
+// V4 groups of four a thread; kept entries and the zeroed tail are written together.
+template <int V4>
+__global__ void __launch_bounds__(kSmThreads) softmax_rows_reg4(float *x, int n_rows,
+                                                                int row_len, int period,
+                                                                int offset) {
+  __shared__ float red[kSmWarps];
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  float4 *p = reinterpret_cast<float4 *>(x + (int64_t)row * row_len);
+  const int valid = min(valid_len(row, row_len, period, offset), row_len);
+  const int nv4 = (valid + 3) >> 2;    // groups holding kept entries
+  const int n4 = row_len >> 2;         // groups of the row
+  const float ninf = -__int_as_float(0x7f800000);
+  float4 v[V4];
+  float m = ninf;
+#pragma unroll
+  for (int j = 0; j < V4; j++) {
+    const int g = tid + j * kSmThreads;
+    v[j] = make_float4(ninf, ninf, ninf, ninf);
+    if (g < nv4) {
+      v[j] = p[g];
+      const int e = 4 * g;  // entries past the prefix do not count
+      if (e + 1 >= valid) v[j].y = ninf;
+      if (e + 2 >= valid) v[j].z = ninf;
+      if (e + 3 >= valid) v[j].w = ninf;
+    }
+    m = fmaxf(m, fmaxf(fmaxf(v[j].x, v[j].y), fmaxf(v[j].z, v[j].w)));
+  }
+  m = block_max(m, red);
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < V4; j++) {
+    const int g = tid + j * kSmThreads;
+    const int e = 4 * g;
+    v[j].x = e < valid ? expf(v[j].x - m) : 0.f;
+    v[j].y = e + 1 < valid ? expf(v[j].y - m) : 0.f;
+    v[j].z = e + 2 < valid ? expf(v[j].z - m) : 0.f;
+    v[j].w = e + 3 < valid ? expf(v[j].w - m) : 0.f;
+    s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+  }
+  s = block_sum(s, red);
+  const float inv = 1.0f / s;
+#pragma unroll
+  for (int j = 0; j < V4; j++) {
+    const int g = tid + j * kSmThreads;
+    if (g < n4)  // zeros past the prefix come from the masked exps above
+      p[g] = make_float4(v[j].x * inv, v[j].y * inv, v[j].z * inv, v[j].w * inv);
+  }
+  for (int g = V4 * kSmThreads + tid; g < n4; g += kSmThreads)
+    p[g] = make_float4(0.f, 0.f, 0.f, 0.f);  // masked tail beyond the registers
+}
+
 // Longer rows: max, then sum of exp, then the write, each a pass over the row.
 __global__ void __launch_bounds__(kSmThreads) softmax_rows_loop(float *x, int n_rows, int row_len,
                                                                 int period, int offset) {
@@ -124,7 +177,17 @@ extern "C" int tabby_softmax_rows_async(float *d_x, int32_t n_rows, int32_t row_
   const int max_valid = causal_period != 0 ? causal_offset + causal_period : row_len;
   cudaStream_t s = (cudaStream_t)stream;
   const dim3 grid((unsigned)n_rows);
-  if (max_valid <= 4 * kSmThreads)
+  const bool vec = (row_len & 3) == 0 && (reinterpret_cast<uintptr_t>(d_x) & 15u) == 0;
+  if (vec && max_valid <= 4 * kSmThreads)
+    softmax_rows_reg4<1><<<grid, kSmThreads, 0, s>>>(d_x, n_rows, row_len, causal_period,
+                                                     causal_offset);
+  else if (vec && max_valid <= 16 * kSmThreads)
+    softmax_rows_reg4<4><<<grid, kSmThreads, 0, s>>>(d_x, n_rows, row_len, causal_period,
+                                                     causal_offset);
+  else if (vec && max_valid <= 32 * kSmThreads)
+    softmax_rows_reg4<8><<<grid, kSmThreads, 0, s>>>(d_x, n_rows, row_len, causal_period,
+                                                     causal_offset);
+  else if (max_valid <= 4 * kSmThreads)
     softmax_rows_reg<4><<<grid, kSmThreads, 0, s>>>(d_x, n_rows, row_len, causal_period,
                                                     causal_offset);
   else if (max_valid <= 16 * kSmThreads)

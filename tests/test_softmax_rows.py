@@ -61,6 +61,10 @@ CASES = [
     (4, 20000, 0, 0),
     (6, 9000, 3, 8000),
     (5, 8192, 0, 0),
+    # Lengths that are not a multiple of 4 take the scalar kernels.
+    (10, 1001, 0, 0),
+    (6, 4099, 2, 4000),
+    (3, 8191, 0, 0),
 ]
 
 
