@@ -115,9 +115,12 @@ def sample_from_topk(top: TopKResult, params: SamplingParams,
     vals = np.ascontiguousarray(top.logits, dtype=np.float32)
     p = params_array(params, 1)
     out = np.zeros(1, OUTCOME_DTYPE)
+    # The reference draws only when it samples: a greedy call returns before
+    # random.next() (sampler.ts:159-167, the draw at :194), leaving the generator as it was.
+    u = random.next() if float(params.temperature) > 0 else 0.0
     check(lib().tabby_sample_from_topk(ids.ctypes.data, vals.ctypes.data, n,
                                        float(top.maxLogit), float(top.sumExp), p.ctypes.data,
-                                       random.next(), out.ctypes.data))
+                                       u, out.ctypes.data))
     o = out[0]
     return SampleOutcome(int(o["id"]), float(o["probability"]), int(o["considered_count"]),
                          float(o["pool_mass"]), bool(o["pool_exhausted"]))
@@ -188,9 +191,17 @@ class Sampler:
             logits = logits.contiguous()
         return logits
 
-    def _uniforms(self, rows: int, rng: Union[SeededRandom, Sequence[float], np.ndarray, None]):
+    @staticmethod
+    def _uniforms(rows: int, rng: Union[SeededRandom, Sequence[float], np.ndarray, None],
+                  p: Optional[np.ndarray] = None):
+        """Per-row u. With a SeededRandom, rows are drawn in row order and only where
+        sampleFromTopK itself would call random.next(): rows with temperature > 0. Greedy
+        rows return before the draw in the reference (sampler.ts:159-167) and get u = 0
+        without advancing the generator, exactly as the device-RNG entry point does."""
         if isinstance(rng, SeededRandom):
-            return np.array([rng.next() for _ in range(rows)], np.float64)
+            temps = p["temperature"] if p is not None else np.ones(rows)
+            return np.array([rng.next() if float(t) > 0 else 0.0 for t in temps[:rows]],
+                            np.float64)
         if rng is None:
             raise ValueError("a SeededRandom or per-row uniforms are required")
         u = np.ascontiguousarray(rng, dtype=np.float64).reshape(-1)
@@ -239,7 +250,7 @@ class Sampler:
         logits = self._check_logits(logits)
         rows = logits.shape[0]
         p = params_array(params, rows)
-        u = self._uniforms(rows, rng)
+        u = self._uniforms(rows, rng, p)
         dev = logits.device
         p_dev = torch.from_numpy(p.view(np.uint8)).to(dev, non_blocking=False)
         u_dev = torch.from_numpy(u).to(dev)
@@ -261,7 +272,7 @@ class Sampler:
             logits = logits[None, :]
         rows, vocab = logits.shape
         p = params_array(params, rows)
-        u = self._uniforms(rows, rng)
+        u = self._uniforms(rows, rng, p)
         out = np.zeros(rows, OUTCOME_DTYPE)
         ids = vals = None
         if return_topk:

@@ -247,3 +247,56 @@ def test_pool_rule(oracle, t, k, cap, want):
 
     assert oracle.pool_size(t, k, cap) == want
     assert pool_size(t, k, cap) == want
+
+
+# --- generator consumption: greedy calls do not draw ------------------------------------
+def py_sample_from_topk_rng(top, temperature, top_p, nxt):
+    """sampleFromTopK(top, params, random) as sampler.ts:147-212 calls random.next(): once,
+    after the greedy return (:159-167), at :194."""
+    if temperature <= 0:
+        return py_sample_from_topk(top, temperature, top_p, 0.0)
+    return py_sample_from_topk(top, temperature, top_p, nxt())
+
+
+def test_greedy_call_leaves_the_generator_alone(oracle):
+    """T=0 call, then T=1 call, then a bare next(): the reference's first draw goes to the
+    T=1 call and the second to the bare next(). The Python mirror, the oracle and the
+    library's host entry must agree id for id and leave the same generator state."""
+    from tabby_b200 import SamplingParams, SeededRandom, sample_from_topk
+    from tabby_b200.sampler import TopKResult
+
+    top = TopKResult(FIXTURE["maxLogit"], FIXTURE["sumExp"], FIXTURE["ids"],
+                     FIXTURE["logits"])
+    for seed in (0, 7, 12345):
+        nxt = py_mulberry32(seed)
+        want = [py_sample_from_topk_rng(FIXTURE, 0.0, 1.0, nxt)["id"],
+                py_sample_from_topk_rng(FIXTURE, 1.0, 1.0, nxt)["id"]]
+        want_next = nxt()
+
+        ro = oracle.SeededRandom(seed)
+        got_or = []
+        for t in (0.0, 1.0):
+            u = ro.next() if t > 0 else 0.0
+            got_or.append(oracle.sample_from_topk(FIXTURE["ids"], FIXTURE["logits"],
+                                                  FIXTURE["maxLogit"], FIXTURE["sumExp"],
+                                                  t, 1.0, u)["id"])
+        rl = SeededRandom(seed)
+        got_lib = [sample_from_topk(top, SamplingParams(t, 4, 1.0), rl).id for t in (0.0, 1.0)]
+        assert got_lib == want and got_or == want, (seed, want, got_or, got_lib)
+        assert rl.next() == want_next == ro.next()
+
+
+def test_batch_uniforms_draw_only_for_sampling_rows():
+    """Sampler's per-row uniforms from one SeededRandom: rows in order, a draw only where
+    sampleFromTopK draws (temperature > 0), the same rule as the device-RNG entry."""
+    from tabby_b200 import SeededRandom
+    from tabby_b200.sampler import Sampler, params_array, SamplingParams
+
+    temps = [0.0, 0.7, 0.0, 1.3, -1.0, 0.2]
+    p = params_array([SamplingParams(t, 40, 0.9) for t in temps], len(temps))
+    rng = SeededRandom(99)
+    u = Sampler._uniforms(len(temps), rng, p)
+    nxt = py_mulberry32(99)
+    want = [nxt() if t > 0 else 0.0 for t in temps]
+    assert list(u) == want
+    assert rng.next() == nxt()
