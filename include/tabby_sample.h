@@ -204,6 +204,21 @@ TABBY_API int tabby_sample_from_topk(const int32_t *ids, const float *logits, in
 TABBY_API int tabby_softmax_rows_async(float *d_x, int32_t n_rows, int32_t row_len,
                                 int32_t causal_period, int32_t causal_offset, void *stream);
 
+/*
+ * Test entry for the failure path of the row pass: tabby_sample_rows_async (in the chunked
+ * schedule, which batches below the resident CTA count use) with the bounded wait for a
+ * row's plan limited to `spin_limit` polls and the plan of row `withhold_row` never
+ * published (-1: none). The waits for that row run out; the kernel still returns, the row
+ * reports TABBY_ETIMEOUT in its outcome, every other row is sampled normally and the
+ * handle stays usable. The reference surfaces device failure as an error the same way
+ * (src/worker/inference.worker.ts:55-58, onDeviceLost -> fail). Not for production use.
+ */
+TABBY_API int tabby_sample_rows_debug_async(tabby_sampler *sampler, const float *d_logits,
+                                  int64_t row_stride, int32_t rows, int32_t vocab,
+                                  const tabby_sampling_params *d_params,
+                                  const double *d_uniforms, tabby_sample_outcome *d_out,
+                                  uint32_t spin_limit, int32_t withhold_row, void *stream);
+
 /* Largest max_top_k tabby_sample_rows_noalloc accepts (its scratch array is fixed). */
 #define TABBY_NOALLOC_MAX_TOP_K 256
 

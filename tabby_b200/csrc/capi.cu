@@ -275,6 +275,36 @@ int tabby_sample_rows_rng_async(tabby_sampler *s, const float *d_logits, int64_t
   return TABBY_OK;
 }
 
+int tabby_sample_rows_debug_async(tabby_sampler *s, const float *d_logits, int64_t row_stride,
+                                  int32_t rows, int32_t vocab,
+                                  const tabby_sampling_params *d_params,
+                                  const double *d_uniforms, tabby_sample_outcome *d_out,
+                                  uint32_t spin_limit, int32_t withhold_row, void *stream) {
+  int st = check_rows(s, d_logits, row_stride, rows, vocab);
+  if (st) return st;
+  if (rows > 0 && (!d_params || !d_uniforms || !d_out))
+    return fail(TABBY_EINVAL, "params, uniforms and out must not be NULL");
+  if (spin_limit < 1) return fail(TABBY_EINVAL, "spin_limit must be >= 1");
+  if ((st = check_vocab_capacity(s, vocab))) return st;
+  DeviceScope scope(s->device);
+  if (scope.err != cudaSuccess) return cuda_fail(scope.err, "cudaSetDevice");
+  RowLaunch l;
+  l.logits = d_logits;
+  l.row_stride = row_stride;
+  l.rows = rows;
+  l.vocab = vocab;
+  l.mode = tabby::kModeSample;
+  l.cap = s->cap;
+  l.params = d_params;
+  l.uniforms = d_uniforms;
+  l.out = d_out;
+  l.spin_limit = spin_limit;
+  l.withhold_row = withhold_row;
+  cudaError_t err = plan_and_launch(s, l, (cudaStream_t)stream);
+  if (err != cudaSuccess) return cuda_fail(err, "row_kernel launch");
+  return TABBY_OK;
+}
+
 int tabby_sample_rows(tabby_sampler *s, const float *h_logits, int64_t row_stride, int32_t rows,
                       int32_t vocab, const tabby_sampling_params *h_params,
                       const double *h_uniforms, tabby_sample_outcome *h_out,

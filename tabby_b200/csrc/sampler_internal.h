@@ -34,6 +34,8 @@ struct RowLaunch {
   int32_t block_ld = 0;
   uint32_t *rng_state = nullptr;  // kModeSample: per-row mulberry32 state on the device; u
                                   // is drawn and the state advanced in place (no uniforms)
+  uint32_t spin_limit = 1u << 24;  // polls of the bounded wait for a row's plan entry
+  int32_t withhold_row = -1;       // tests only: the plan of this row is never published
 };
 
 struct MergeLaunch {

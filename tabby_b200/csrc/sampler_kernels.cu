@@ -37,6 +37,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <mutex>
 #include <type_traits>
 
 #include "finalize.cuh"
@@ -1219,6 +1220,8 @@ struct PassArgs {
   float2 *warp_stats;    // [rows][nch][kWarps] (max, sum-exp)
   float4 *row_gval;      // [rows][kRowGroups] candidate groups: warp w of chunk c owns the
   int32_t *row_gidx;     //   region (c * kWarps + w) of region_slots() slots
+  uint32_t spin_limit;   // polls of the bounded wait for a row's plan entry
+  int32_t withhold_row;  // tests only: this row's plan entry is never published (-1: none)
 };
 
 // Candidate slots of the row's list each chunk owns.
@@ -1269,6 +1272,26 @@ __device__ __forceinline__ Span aligned_span(const float *rowp, int lo, int hi) 
   s.a1 = s.a0 + ((hi - s.a0) & ~3);
   s.ngroups = (s.a1 - s.a0) >> 2;
   return s;
+}
+
+// The row the plan puts at processing position `pos` (thread-level call): rows with pools
+// above 64 first, each group in row order, as plan_row orders them. Used only when the
+// wait for a plan entry runs out.
+__device__ __noinline__ int row_at_position(const PassArgs &a, int pos) {
+  int large = 0;
+  for (int r = 0; r < a.rows; r++) {
+    uint32_t f = 0;
+    large += row_pool(a, r, &f) > 64 ? 1 : 0;
+  }
+  int lb = 0, sb = 0;
+  for (int r = 0; r < a.rows; r++) {
+    uint32_t f = 0;
+    const bool lg = row_pool(a, r, &f) > 64;
+    if ((lg ? lb : large + sb) == pos) return r;
+    lb += lg ? 1 : 0;
+    sb += lg ? 0 : 1;
+  }
+  return 0;
 }
 
 // Plans one row (block-uniform call): resets its counters, fixes its pool size and its
@@ -1377,7 +1400,7 @@ __device__ __noinline__ void plan_row(const PassArgs &a, int row, uint64_t *cand
     }
   }
   PPHASE(row, 2);
-  if (tid == 0) {
+  if (tid == 0 && row != a.withhold_row) {
     const int pos = (int)sh->unit;
     a.row_tf[row] = tf;
     a.row_tf_lo[row] = tf_lo;
@@ -1525,7 +1548,7 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
   FTRACE(row, 5);
 
   int n = 0;
-  if (k > 0) {
+  if (k > 0 && !(rflags & kFlagTimeout)) {
     bool ok = !(rflags & kRowOverflow);
     if (ok) {
       // Expand the groups into composites of their logits >= tf. Every group is one
@@ -1644,8 +1667,9 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
 #endif
   const int kk = top_sorted(cand, n, k, kFinishCap, hist, sh);
   FTRACE(row, 2);
-  const uint32_t flags = (rflags & kFlagBadInput) | pflags;
-  const uint32_t status = (flags & kFlagBadInput)    ? (uint32_t)TABBY_EINPUT
+  const uint32_t flags = (rflags & (kFlagBadInput | kFlagTimeout)) | pflags;
+  const uint32_t status = (flags & kFlagTimeout)     ? (uint32_t)TABBY_ETIMEOUT
+                          : (flags & kFlagBadInput)  ? (uint32_t)TABBY_EINPUT
                           : (flags & kFlagBadParams) ? (uint32_t)TABBY_EINVAL
                                                      : (uint32_t)TABBY_OK;
   if (k <= 64) {
@@ -1899,8 +1923,10 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
   // row data.
   int nid = 0, nrow = 0, nk = 0;
   float ntf = 0.f;
-  // Thread 0: the row data of unit nid, once its row is planned (bounded wait; a wait
-  // that runs out ends this CTA's work, leaving the unit undone).
+  // Thread 0: the row data of unit nid, once its row is planned. The wait is bounded:
+  // when it runs out, the unit's row is worked out from the parameters, flagged with
+  // kFlagTimeout and the unit streamed with no candidates (threshold +inf), so the row
+  // still completes and its finish reports TABBY_ETIMEOUT; the counters stay exact.
   auto unit_info = [&]() {
     if (nid >= units) return;
     if (a.whole) {  // unit = row; the threshold comes from the stream
@@ -1917,9 +1943,12 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
       w0 = ld_acquire_u64(&a.pos_entry[2 * ri]);
       w1 = ld_acquire_u64(&a.pos_entry[2 * ri + 1]);
       if ((uint32_t)(w0 >> 32) == sh->epoch && (uint32_t)(w1 >> 32) == sh->epoch) break;
-      if (++spins > (1u << 24)) {
-        take();  // this CTA's take past the end, so the count of takes stays exact
-        nid = units;
+      if (++spins > a.spin_limit) {
+        uint32_t f = 0;
+        nrow = row_at_position(a, ri);
+        nk = row_pool(a, nrow, &f);
+        ntf = __int_as_float(0x7f800000);
+        atomicOr(&a.row_flags[nrow], kFlagTimeout);
         return;
       }
       __nanosleep(100);
@@ -2324,23 +2353,47 @@ static size_t row_smem_bytes() {
 // with whole rows).
 constexpr int kUnitsPerCtaX10 = 8;
 
-static cudaError_t prepare_row_kernel(size_t smem_bytes);
+constexpr int kMaxDevices = 64;
+
+namespace {
+// Per-device set-up of the row kernel: the dynamic shared-memory attribute and the
+// occupancy are properties of the kernel on one device, so each device is set up once,
+// with that device current (the callers make it current), under std::call_once.
+struct RowKernelSetup {
+  std::once_flag once;
+  cudaError_t err = cudaSuccess;
+  int per_sm = 0;
+};
+RowKernelSetup g_row_setup[kMaxDevices];
+
+cudaError_t row_kernel_setup(int *per_sm) {
+  int dev = -1;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  RowKernelSetup &s = g_row_setup[dev];
+  std::call_once(s.once, [&]() {
+    s.err = cudaFuncSetAttribute(row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)row_smem_bytes());
+    int occ = 0;
+    if (s.err == cudaSuccess)
+      s.err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, row_kernel, kThreads,
+                                                            row_smem_bytes());
+    if (s.err == cudaSuccess && occ < 1) s.err = cudaErrorInvalidConfiguration;
+    if (s.err == cudaSuccess) s.per_sm = std::min(occ, 2);
+  });
+  *per_sm = s.per_sm;
+  return s.err;
+}
+}  // namespace
 
 cudaError_t plan_rows(int32_t sms, int32_t rows, int32_t vocab, int32_t cap, RowGeometry *geo) {
   (void)cap;
   // Resident CTAs a SM (two 512-thread CTAs by design); the cooperative launch needs the
   // grid to fit at once.
-  static int per_sm = 0;
-  if (per_sm == 0) {
-    cudaError_t err = prepare_row_kernel(row_smem_bytes());
-    if (err != cudaSuccess) return err;
-    int occ = 0;
-    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, row_kernel, kThreads,
-                                                        row_smem_bytes());
-    if (err != cudaSuccess) return err;
-    if (occ < 1) return cudaErrorInvalidConfiguration;
-    per_sm = std::min(occ, 2);
-  }
+  int per_sm = 0;
+  cudaError_t err = row_kernel_setup(&per_sm);
+  if (err != cudaSuccess) return err;
   const int ctas = per_sm * std::max(sms, 1);
   const int max_by_size = std::max(1, vocab / kMinChunk);
   int nch = (kUnitsPerCtaX10 * ctas + 10 * std::max(rows, 1) - 1) / (10 * std::max(rows, 1));
@@ -2352,17 +2405,6 @@ cudaError_t plan_rows(int32_t sms, int32_t rows, int32_t vocab, int32_t cap, Row
   g.whole = g.nch == 1 ? 1 : 0;
   g.smem_bytes = row_smem_bytes();
   *geo = g;
-  return cudaSuccess;
-}
-
-static cudaError_t prepare_row_kernel(size_t smem_bytes) {
-  static size_t configured = 0;
-  if (smem_bytes > configured) {
-    cudaError_t err = cudaFuncSetAttribute(
-        row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes);
-    if (err != cudaSuccess) return err;
-    configured = smem_bytes;
-  }
   return cudaSuccess;
 }
 
@@ -2401,7 +2443,10 @@ cudaError_t launch_rows(const RowLaunch &l, const RowGeometry &geo, const Scratc
   a.row_gval = scr.row_gval;
   a.row_gidx = scr.row_gidx;
   a.rng_state = l.rng_state;
-  cudaError_t err = prepare_row_kernel(geo.smem_bytes);
+  a.spin_limit = l.spin_limit;
+  a.withhold_row = l.withhold_row;
+  int per_sm = 0;
+  cudaError_t err = row_kernel_setup(&per_sm);
   if (err != cudaSuccess) return err;
   // Cooperative launch: all CTAs resident at once (units wait on rows other CTAs plan).
   cudaLaunchConfig_t cfg = {};
