@@ -234,9 +234,11 @@ TABBY_API int tabby_sample_rows_debug_async(tabby_sampler *sampler, const float 
  * 1..TABBY_NOALLOC_MAX_TOP_K, larger values are rejected with TABBY_EINVAL.
  * Runs on the current device. The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress): make that first call before any stream capture.
- * All calls on a device share the one array (each call first clears the counters it
- * needs at zero), so calls that overlap on the GPU -- concurrent streams or threads --
- * race and must be serialised by the caller.
+ * All calls on a device share the one array. No call clears it: it is zero when the
+ * library loads, and every launch leaves it ready for the next (the launch's last unit
+ * take resets the unit counter, each row's counters are reset before the row is used,
+ * and plan entries carry a launch number kept in the array). Calls that overlap on the
+ * GPU -- concurrent streams or threads -- race and must be serialised by the caller.
  */
 TABBY_API int tabby_sample_rows_noalloc(const float *d_logits, int64_t row_stride, int32_t rows,
                                         int32_t vocab, int32_t max_top_k,

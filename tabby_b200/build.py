@@ -47,7 +47,7 @@ def _stale() -> bool:
 def build(force: bool = False, verbose: bool = False, out: str | None = None,
           defines: tuple = ()) -> str:
     """Compile SOURCES into `out` (default: the in-tree library). `defines` adds -D flags
-    (e.g. TABBY_TRACE=1 for the phase-timestamp build used while tuning)."""
+    (e.g. TABBY_CHECKS=1 for the self-checking debug build)."""
     lib_path = out or LIB
     if out is None and not force and not _stale():
         return LIB

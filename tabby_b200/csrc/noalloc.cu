@@ -119,8 +119,10 @@ extern "C" int tabby_sample_rows_noalloc(const float *d_logits, int64_t row_stri
   l.topk_values = d_topk_values;
   l.topk_ld = topk_ld;
 
-  // The row pass resets the counters of the rows it plans (its plan phase), so no clearing
-  // is needed here.
+  // No clearing is needed: the array is zero when the library loads; every launch resets
+  // a row's counters before using the row (the plan phase of chunked launches, the unit
+  // start of whole-row launches), its last unit take resets the unit counter, and plan
+  // entries carry the launch number kept in the array.
   cudaError_t err = cudaSuccess;
   for (int32_t r0 = 0; r0 < rows; r0 += kNoAllocRows) {
     RowLaunch b = l;

@@ -66,75 +66,10 @@ constexpr float kNegSentinel = -3.0e38f;  // NEG_INF of reduce_max.wgsl:13
 
 enum Flags : uint32_t { kFlagBadInput = 1u, kFlagTimeout = 2u, kFlagBadParams = 4u };
 
-// Opt-in phase timestamps for tuning builds (-DTABBY_TRACE=1); compiled out otherwise.
-#ifdef TABBY_TRACE
-constexpr int kTraceSlots = 16;
-constexpr int kTraceCtas = 16384;
-__device__ unsigned long long g_trace[kTraceCtas * kTraceSlots];
-__device__ __forceinline__ unsigned long long globaltimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-constexpr int kUnitTraceCtas = 512, kUnitTraceUnits = 32;
-__device__ unsigned long long g_utrace[kUnitTraceCtas * kUnitTraceUnits * 4];
-__device__ unsigned long long g_ptrace[4096 * 2];
-__device__ unsigned long long g_ftrace[4096 * 8];
-__device__ unsigned long long g_pphase[4096 * 4];
-__device__ unsigned long long g_lcyc[kUnitTraceCtas * kUnitTraceUnits * 4];
-__device__ unsigned long long g_fz[4096 * 8];
-#define FZ(slot)                                                                    \
-  do {                                                                              \
-    if (threadIdx.x == 0 && sh->trace_row >= 0 && sh->trace_row < 4096)             \
-      g_fz[sh->trace_row * 8 + (slot)] = clock64();                                 \
-  } while (0)
-#define PPHASE(row, slot)                                                  \
-  do {                                                                     \
-    if (threadIdx.x == 0 && (row) < 4096) g_pphase[(row) * 4 + (slot)] = clock64(); \
-  } while (0)
-#define FTRACE(row, slot)                                                  \
-  do {                                                                     \
-    if (threadIdx.x == 0 && (row) < 4096) g_ftrace[(row) * 8 + (slot)] = clock64(); \
-  } while (0)
-#define UTRACE(j, slot, val)                                                          \
-  do {                                                                                \
-    if (threadIdx.x == 0 && blockIdx.x < kUnitTraceCtas && (j) < kUnitTraceUnits)     \
-      g_utrace[(blockIdx.x * kUnitTraceUnits + (j)) * 4 + (slot)] = (val);            \
-  } while (0)
-#define TRACE(ph)                                                  \
-  do {                                                             \
-    if (threadIdx.x == 0 && blockIdx.x < kTraceCtas)               \
-      g_trace[blockIdx.x * kTraceSlots + (ph)] = globaltimer();    \
-  } while (0)
-#define TRACE_VAL(ph, v)                                                    \
-  do {                                                                      \
-    if (threadIdx.x == 0 && blockIdx.x < kTraceCtas)                        \
-      g_trace[blockIdx.x * kTraceSlots + (ph)] = (unsigned long long)(v);   \
-  } while (0)
-#else
-#define UTRACE(j, slot, val) \
-  do {                       \
-  } while (0)
-#define FTRACE(row, slot) \
-  do {                    \
-  } while (0)
-#define PPHASE(row, slot) \
-  do {                    \
-  } while (0)
-#define FZ(slot) \
-  do {           \
-  } while (0)
-#define TRACE(ph) \
-  do {            \
-  } while (0)
-#define TRACE_VAL(ph, v) \
-  do {                   \
-  } while (0)
-#endif
 
-// Opt-in self-checks for debugging builds (-DTABBY_CHECKS=1): every shared-memory
-// candidate / histogram write and every TMA copy is validated first; a violation is
-// recorded (first one wins) and the access is skipped instead of faulting.
+// Opt-in self-checks for debugging builds (-DTABBY_CHECKS=1): shared-memory candidate
+// writes of the selection are validated first; a violation is recorded (first one wins)
+// and the access is skipped instead of faulting.
 #ifdef TABBY_CHECKS
 __device__ unsigned long long g_check[4];  // code, blockIdx, a, b
 __device__ __forceinline__ bool check_ok(bool ok, unsigned code, unsigned long long x,
@@ -277,7 +212,6 @@ struct Shared {
   int32_t urow, uk;  // its row and pool size
   int32_t plan_red[3][kWarps];  // plan: per-warp counts for the row order
   float utf;         // its threshold
-  int32_t trace_row;  // row being finished (tuning traces only)
   uint32_t base;  // where the unit's candidates go in the row's list
   int32_t cut_claim;
   int32_t chosen_claim;
@@ -716,7 +650,6 @@ __device__ __noinline__ void finalize_sample(const int32_t *ids, const float *va
     return;
   }
   const bool sample = p.temperature > 0;
-  FZ(0);
   const double inv_sum = 1.0 / (double)sum_exp;
   const double inv_t = sample ? 1.0 / p.temperature : 0.0;
   // Two consecutive candidates a thread (n <= 2 * blockDim.x).
@@ -730,9 +663,7 @@ __device__ __noinline__ void finalize_sample(const int32_t *ids, const float *va
     e1 = approx_exact(vals[i1], max_logit, inv_sum);
     if (sample) s1 = approx_scaled(vals[i1], max_logit, inv_t);
   }
-  FZ(1);
   const double pool_mass = block_sum_f64(e0 + e1, sh);
-  FZ(2);
   const double bound = decision_bound(n);
 
   int32_t cut = 1, chosen = 0, exhausted = 0;
@@ -742,9 +673,7 @@ __device__ __noinline__ void finalize_sample(const int32_t *ids, const float *va
     const double inv_st = 1.0 / st;
     const double w0 = i0 < n ? s0 * inv_st : 0.0;
     const double w1 = i1 < n ? s1 * inv_st : 0.0;
-    FZ(3);
     const double before = block_exclusive_scan_f64(w0 + w1, sh);
-    FZ(4);
     const double c0 = before + w0;
     const double c1 = c0 + w1;
     if (i0 < n) cum[i0] = c0;
@@ -794,7 +723,6 @@ __device__ __noinline__ void finalize_sample(const int32_t *ids, const float *va
     chosen = ch < cut ? ch : cut - 1;
     fallback = sh->fallback != 0;
   }
-  FZ(5);
   if (tid == 0) {
     tabby_sample_outcome o;
     double pm = pool_mass;
@@ -818,7 +746,6 @@ __device__ __noinline__ void finalize_sample(const int32_t *ids, const float *va
     o.reserved = fallback ? 1 : 0;  // 1 when the sequential replay decided
     *out = o;
   }
-  FZ(6);
 }
 
 // Merges the sorted 64-list (w0, w1) into the sorted 64-list (v0, v1) (both descending,
@@ -1302,11 +1229,7 @@ __device__ __noinline__ void plan_row(const PassArgs &a, int row, uint64_t *cand
   int (*red)[kWarps] = sh->plan_red;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float *rowp = a.logits + (int64_t)row * a.row_stride;
-  PPHASE(row, 0);
   uint32_t pf = 0;
-#ifdef TABBY_TRACE
-  if (tid == 0 && row < 4096) g_ptrace[row * 2] = globaltimer();
-#endif
   const int k = row_pool(a, row, &pf);
   if (tid == 0) {
     a.row_done[row] = 0;
@@ -1365,7 +1288,6 @@ __device__ __noinline__ void plan_row(const PassArgs &a, int row, uint64_t *cand
   cand[2 * tid] = t1;
   cand[2 * tid + 1] = t2;
   __syncthreads();
-  PPHASE(row, 1);
   if (tid == 0) {
     int lt = 0, lb = 0, sb = 0;
     for (int w = 0; w < kWarps; w++) {
@@ -1399,7 +1321,6 @@ __device__ __noinline__ void plan_row(const PassArgs &a, int row, uint64_t *cand
       if ((thr2 >> 32) != 0ull) tf_lo = float_of_key((uint32_t)(thr2 >> 32));
     }
   }
-  PPHASE(row, 2);
   if (tid == 0 && row != a.withhold_row) {
     const int pos = (int)sh->unit;
     a.row_tf[row] = tf;
@@ -1410,9 +1331,6 @@ __device__ __noinline__ void plan_row(const PassArgs &a, int row, uint64_t *cand
     st_release_u64(&a.pos_entry[2 * pos + 1], tag | __float_as_uint(tf));
   }
   __syncthreads();  // the slots and sh are free again
-#ifdef TABBY_TRACE
-  if (tid == 0 && row < 4096) g_ptrace[row * 2 + 1] = globaltimer();
-#endif
 }
 
 // Filters a whole row again, exactly (block-uniform call): candidates are the logits
@@ -1487,8 +1405,6 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const float *rowp = a.logits + (int64_t)row * a.row_stride;
   uint32_t pflags = 0;
-  if (tid == 0) sh->trace_row = row;
-  FTRACE(row, 0);
   // Everything the finish reads from global memory, issued together.
   const int np = a.nch * kWarps;
   float2 st = make_float2(-3.40282347e38f, 0.f);
@@ -1545,7 +1461,6 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
   if (tid < np) roff[tid] = (uint32_t)(rbefore + rincl - rcount);
   const int total = (int)partials_sum_above_u32(sh->red_u2, -1);  // candidate groups of the row
   __syncthreads();
-  FTRACE(row, 5);
 
   int n = 0;
   if (k > 0 && !(rflags & kFlagTimeout)) {
@@ -1563,13 +1478,7 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
       const int32_t *gi = a.row_gidx + (int64_t)row * kRowGroups;
       // Four groups a thread in flight at once, then their logits >= tf as composites.
       constexpr int kBatch = 4;
-#ifdef TABBY_TRACE
-      long long tl = 0, tp = 0, tq0;
-#endif
       for (int r0 = 0; r0 < total; r0 += kBatch * kThreads) {
-#ifdef TABBY_TRACE
-        tq0 = clock64();
-#endif
         float4 xb[kBatch];
         int bb[kBatch];
 #pragma unroll
@@ -1592,15 +1501,6 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
             bb[j] = __ldcg(gi + at);
           }
         }
-#ifdef TABBY_TRACE
-        {
-          float z = 0.f;
-          for (int j = 0; j < kBatch; j++) z += xb[j].x + (float)bb[j];
-          if (z == 1.2345f) sh->flags = 9;
-          tl += clock64() - tq0;
-          tq0 = clock64();
-        }
-#endif
         // This thread's logits >= tf over its batch, one warp scan and one atomic.
         uint32_t hm = 0;  // 4 bits a group
 #pragma unroll
@@ -1641,16 +1541,7 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
             }
           }
         }
-#ifdef TABBY_TRACE
-        tp += clock64() - tq0;
-#endif
       }
-#ifdef TABBY_TRACE
-      if (tid == 0 && row < 4096) {
-        g_ftrace[row * 8 + 7] = tl;
-        g_fz[row * 8 + 7] = tp;
-      }
-#endif
       __syncthreads();
       n = (int)sh->count;
       ok = sh->overflow == 0u && n >= k;
@@ -1658,15 +1549,7 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
     }
     if (!ok) n = rescan_row(rowp, a.vocab, k, __ldcg(&a.row_tf_lo[row]), cand, hist, sh);
   }
-  FTRACE(row, 1);
-#ifdef TABBY_TRACE
-  if (tid == 0 && row < 4096)
-    g_ftrace[row * 8 + 6] = (unsigned long long)n | ((unsigned long long)total << 20) |
-                            ((unsigned long long)rflags << 40) |
-                            ((unsigned long long)(__float_as_uint(tf) >> 16) << 44);
-#endif
   const int kk = top_sorted(cand, n, k, kFinishCap, hist, sh);
-  FTRACE(row, 2);
   const uint32_t flags = (rflags & (kFlagBadInput | kFlagTimeout)) | pflags;
   const uint32_t status = (flags & kFlagTimeout)     ? (uint32_t)TABBY_ETIMEOUT
                           : (flags & kFlagBadInput)  ? (uint32_t)TABBY_EINPUT
@@ -1708,7 +1591,6 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
       if (2 * lane < kk) a.topk_values[(int64_t)row * a.topk_ld + 2 * lane] = x0;
       if (2 * lane + 1 < kk) a.topk_values[(int64_t)row * a.topk_ld + 2 * lane + 1] = x1;
     }
-    FTRACE(row, 3);
     if (a.rng_state) {
       // The reference draws only when it samples: after the empty-pool throw and the
       // greedy return (sampler.ts:153,159-167).
@@ -1719,7 +1601,6 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
     }
     finalize_warp(id0, id1, x0, x1, kk, max_logit, sum_exp, prm, uni,
                   reinterpret_cast<double *>(hist), &a.out[row], status);
-    FTRACE(row, 4);
     return;
   }
   // Unpack into (id, value) in the histogram space; once that is done the candidate
@@ -1767,7 +1648,6 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
     for (int i = tid; i < kk; i += kThreads) a.topk_ids[(int64_t)row * a.topk_ld + i] = ids[i];
   if (a.topk_values)
     for (int i = tid; i < kk; i += kThreads) a.topk_values[(int64_t)row * a.topk_ld + i] = vals[i];
-  FTRACE(row, 3);
   if (a.rng_state) {  // drawn only when the reference draws (see the warp path)
     if (tid == 0)
       sh->rng_u = status == TABBY_OK && kk > 0 && prm.temperature > 0
@@ -1778,7 +1658,6 @@ __device__ __noinline__ void finish_row(const PassArgs &a, int row, int k, uint6
   }
   finalize_sample(ids, vals, kk, max_logit, sum_exp, prm, uni, cum, scaled, sh,
                   &a.out[row], status);
-  FTRACE(row, 4);
 }
 
 // Packed pair arithmetic of sm_100 (two fp32 lanes in one 64-bit register pair).
@@ -1912,12 +1791,6 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
   if (!a.whole)
     for (int r = blockIdx.x; r < a.rows; r += gridDim.x) plan_row(a, r, fin, hist, sh);
 
-#ifdef TABBY_TRACE
-  int uj = 0;
-#define NOW() globaltimer()
-#else
-#define NOW() 0ull
-#endif
   // Unit schedule, kept by thread 0: at the end of a unit it counts the unit into its row
   // (the unit that completes a row finishes it at once), then takes the next unit and its
   // row data.
@@ -1986,14 +1859,6 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
     const int k = sh->uk;
     float tf = sh->utf;
     if (unit >= units) break;
-#ifdef TABBY_TRACE
-    UTRACE(uj, 0, NOW());
-    if (tid == 0 && blockIdx.x < kUnitTraceCtas && uj < kUnitTraceUnits) {
-      uint32_t smid;
-      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-      g_lcyc[(blockIdx.x * kUnitTraceUnits + uj) * 4] = smid | ((unsigned long long)row << 32);
-    }
-#endif
     const int ri = unit / a.nch;
     const int chunk = unit - ri * a.nch;
     const float *rowp = a.logits + (int64_t)row * a.row_stride;
@@ -2186,9 +2051,6 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
       if (it + 2 < wit) step(I2{}, it + 2);
     }
     cp_async_wait_group<0>();
-#ifdef TABBY_TRACE
-    UTRACE(uj, 1, NOW());
-#endif
 
     // Per-warp statistics into the row's table.
     {
@@ -2237,20 +2099,11 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
       sh->utf = ntf;
     }
     __syncthreads();
-#ifdef TABBY_TRACE
-    UTRACE(uj, 2, NOW());
-#endif
     if (sh->last) {
       __threadfence();
       finish_row(a, row, k, fin, hist, sh);
       __syncthreads();  // the finish is done with the stage region before the loads reuse it
-#ifdef TABBY_TRACE
-      UTRACE(uj, 3, NOW());
-#endif
     }
-#ifdef TABBY_TRACE
-    uj++;
-#endif
   }
 }
 
@@ -2495,30 +2348,6 @@ int host_sample_from_topk(const int32_t *ids, const float *logits, int32_t n, fl
 
 }  // namespace tabby
 
-#ifdef TABBY_TRACE
-extern "C" __attribute__((visibility("default"))) int tabby_debug_trace(unsigned long long *host,
-                                                                        int n) {
-  return (int)cudaMemcpyFromSymbol(host, tabby::g_trace, (size_t)n * 8);
-}
-extern "C" __attribute__((visibility("default"))) int tabby_debug_utrace(unsigned long long *u,
-                                                                         unsigned long long *p) {
-  int e = (int)cudaMemcpyFromSymbol(u, tabby::g_utrace, sizeof(tabby::g_utrace));
-  if (e) return e;
-  return (int)cudaMemcpyFromSymbol(p, tabby::g_ptrace, sizeof(tabby::g_ptrace));
-}
-extern "C" __attribute__((visibility("default"))) int tabby_debug_ftrace(unsigned long long *f) {
-  return (int)cudaMemcpyFromSymbol(f, tabby::g_ftrace, sizeof(tabby::g_ftrace));
-}
-extern "C" __attribute__((visibility("default"))) int tabby_debug_fz(unsigned long long *f) {
-  return (int)cudaMemcpyFromSymbol(f, tabby::g_fz, sizeof(tabby::g_fz));
-}
-extern "C" __attribute__((visibility("default"))) int tabby_debug_lcyc(unsigned long long *f) {
-  return (int)cudaMemcpyFromSymbol(f, tabby::g_lcyc, sizeof(tabby::g_lcyc));
-}
-extern "C" __attribute__((visibility("default"))) int tabby_debug_pphase(unsigned long long *f) {
-  return (int)cudaMemcpyFromSymbol(f, tabby::g_pphase, sizeof(tabby::g_pphase));
-}
-#endif
 
 #ifdef TABBY_CHECKS
 extern "C" __attribute__((visibility("default"))) int tabby_debug_checks(unsigned long long *host) {

@@ -1,4 +1,4 @@
-"""softmax_rows (SURVEY next-row 4): the CUDA kernel through the C ABI against the
+"""softmax_rows (the attention-score softmax next to the sampler): the CUDA kernel through the C ABI against the
 oracle restatement of cpu.ts softmaxRows (fp32 rounding as the reference's CPU form).
 
 Bar: masked tail exactly 0; every entry within the reference's own kernel tolerance of the
@@ -33,6 +33,55 @@ def py_softmax_rows(x, n_rows, row_len, period, offset):
         for i in range(valid, row_len):
             out[base + i] = 0.0
     return np.array(out).reshape(n_rows, row_len)
+
+
+def ref_random_f32(count, seed, scale=1.0):
+    """randomF32 of the reference's tests (tests/support.ts:7-24): mulberry32 draws mapped
+    to (u * 2 - 1) * scale in float64, stored as float32."""
+    a = seed & 0xFFFFFFFF
+    out = np.zeros(count, np.float32)
+    for i in range(count):
+        a = (a + 0x6D2B79F5) & 0xFFFFFFFF
+        t = a
+        t = ((t ^ (t >> 15)) * (t | 1)) & 0xFFFFFFFF
+        t ^= (t + (((t ^ (t >> 7)) * (t | 61)) & 0xFFFFFFFF)) & 0xFFFFFFFF
+        u = ((t ^ (t >> 14)) & 0xFFFFFFFF) / 4294967296
+        out[i] = (u * 2 - 1) * scale
+    return out
+
+
+def test_oracle_on_the_reference_fixture():
+    """The reference test's own input: randomF32(3 * 5 * 5, 0x50f7, 4), 15 rows of 5,
+    causal period 5 (kernels.test.ts:457-485)."""
+    x = ref_random_f32(75, 0x50F7, 4)
+    assert x.min() >= -4 and x.max() <= 4
+    got = orc.softmax_rows(x, 15, 5, 5, 0)
+    want = py_softmax_rows(x, 15, 5, 5, 0)
+    np.testing.assert_allclose(got, want, rtol=1e-6, atol=1e-7)
+    for r in range(15):
+        valid = (r % 5) + 1
+        assert (got[r, valid:] == 0).all()
+        assert abs(float(got[r].astype(np.float64).sum()) - 1.0) < 1e-5
+
+
+@pytest.mark.gpu
+def test_gpu_on_the_reference_fixture():
+    if not gpu_available():
+        pytest.skip("no CUDA device")
+    import torch
+
+    from tabby_b200._lib import check, lib
+
+    x = ref_random_f32(75, 0x50F7, 4)
+    d = torch.from_numpy(x.copy()).cuda()
+    check(lib().tabby_softmax_rows_async(d.data_ptr(), 15, 5, 5, 0,
+                                         torch.cuda.current_stream().cuda_stream))
+    got = d.cpu().numpy().reshape(15, 5)
+    want = orc.softmax_rows(x, 15, 5, 5, 0)
+    np.testing.assert_allclose(got, want, rtol=0, atol=1e-4)  # kernels.test.ts expectClose
+    for r in range(15):
+        assert (got[r, (r % 5) + 1:] == 0).all()
+        assert abs(float(got[r].astype(np.float64).sum()) - 1.0) < 1e-5
 
 
 @pytest.mark.parametrize("n_heads,n_tokens,period,offset", [(3, 5, 5, 0), (2, 7, 0, 0),

@@ -62,7 +62,7 @@ def test_noalloc_matches_handle_entry_point_twice():
 
     L = lib()
     cap = 256
-    sampler = Sampler(0, max_top_k=cap, max_rows=64, max_vocab=151936)
+    sampler = Sampler(0, max_top_k=cap, max_rows=128, max_vocab=151936)
 
     def with_handle(logits, pd, ud, out, ids, vals, stream):
         rows, vocab = logits.shape
@@ -76,13 +76,22 @@ def test_noalloc_matches_handle_entry_point_twice():
                                           pd.data_ptr(), ud.data_ptr(), out.data_ptr(),
                                           ids.data_ptr(), vals.data_ptr(), cap, stream))
 
-    # Small batches split every row into slices, so the scratch array is really used.
-    for call, (rows, seed) in enumerate([(8, 1), (5, 2)]):
+    # Small batches split every row into slices, so the scratch array is really used; the
+    # 100-row call runs as four launches over the same array (32 rows a launch).
+    from oracle import oracle as orc
+
+    for call, (rows, seed) in enumerate([(8, 1), (5, 2), (100, 3)]):
         x, p, u = synth.config("c4", seed=seed, rows=rows)
-        p["top_k"] = np.array([0, 20, 100, 256, 1, 40, 7, 200])[:rows]
+        p["top_k"] = np.resize(np.array([0, 20, 100, 256, 1, 40, 7, 200]), rows)
         a = _run(torch, without_alloc, x, p, u, cap)
         b = _run(torch, with_handle, x, p, u, cap)
         _same(a, b)
+        ref, rids, rvals = orc.sample_rows(x, p, u, cap)
+        np.testing.assert_array_equal(a[0]["id"], ref["id"])
+        for r in range(rows):
+            k = int(ref[r]["pool_size"])
+            np.testing.assert_array_equal(a[1][r, :k], rids[r, :k])
+        np.testing.assert_allclose(a[0]["probability"], ref["probability"], rtol=REL)
     sampler.close()
 
 
