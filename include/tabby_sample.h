@@ -5,7 +5,7 @@
  * splits that path in two:
  *   - device side: ForwardPass.encodeSampling (src/engine/forward.ts:520-601) records
  *     reduce_max, reduce_sumexp and k rounds of topk_partial/topk_select
- *     (src/shaders/*.wgsl) and reads back [maxLogit, sumExp, (value, index) * k]
+ *     (the WGSL files under src/shaders) and reads back [maxLogit, sumExp, (value, index) * k]
  *     (forward.ts:126-157) as a TopKResult (forward.ts:94-103);
  *   - host side: sampleFromTopK(top, params, random) (src/engine/sampler.ts:147-212)
  *     turns that block into a SampleOutcome, with the candidate pool sized by the
