@@ -48,6 +48,41 @@ METRIC = "sampled rows/s (B=256 x V=151936 fp32 logits, heterogeneous T/top-k/to
 NOMINAL_HBM_GBS = 8000.0
 
 
+def bench_config(world):
+    """The workload both arms report (identical dicts, so the records compare)."""
+    return {"workload": WORKLOAD, "rows_per_gpu": ROWS, "vocab": VOCAB, "max_top_k": CAP,
+            "parallelism": f"rows split x{world}, no collective",
+            "l2": f"inputs rotate over {ROTATE} resident batches "
+                  f"({ROTATE * ROWS * VOCAB * 4 / 1e6:.0f} MB > 126 MB L2)"}
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def node_probe():
+    """Node.js on this box (the reference's own CPU sampler would run under it); the
+    reference's TypeScript is not shipped with this repository, so without it the CPU
+    baseline is the C restatement of sampler.ts."""
+    import shutil
+
+    path = shutil.which("node")
+    if not path:
+        return {"node": None}
+    try:
+        v = subprocess.run([path, "--version"], capture_output=True, text=True, timeout=10)
+        return {"node": path, "version": v.stdout.strip()}
+    except Exception as e:  # noqa: BLE001
+        return {"node": path, "error": str(e)}
+
+
 def dist_env():
     return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
             int(os.environ.get("WORLD_SIZE", "1")))
@@ -132,12 +167,13 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_reference(x, params, u, seconds=10.0):
+def cpu_reference(x, params, u, seconds=10.0, threads=None):
     """The reference CPU path (full sort + sampleFromTopK per row, oracle restatement)
-    on all host cores over a bounded sample of the workload's rows."""
+    on `threads` host cores (all of them by default) over a bounded sample of the
+    workload's rows."""
     from oracle import oracle
 
-    threads = os.cpu_count() or 1
+    threads = threads or os.cpu_count() or 1
     rows_done, elapsed, reps = 0, 0.0, 0
     chunk = max(threads * 2, 16)
     r0 = 0
@@ -170,10 +206,12 @@ def run_reference(args, rank, world):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * ROWS / value, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32/f64", "data": "synthetic (seeded)",
-        "config": {"workload": WORKLOAD, "rows": ROWS, "vocab": VOCAB, "max_top_k": CAP},
+        "config": bench_config(world),
         "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port",
+                         "cpu_model": cpu_model(),
                          "sample": sample + " per step (C restatement of sampler.ts topK "
-                         "full sort + sampleFromTopK; Node is absent)"},
+                         "full sort + sampleFromTopK)"},
+        "reference_runtime": node_probe(),
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -273,8 +311,11 @@ def run_ours(args, rank, local_rank, world):
         e2e_value = world * ROWS * e2e_steps / e2e_s
 
     sharded = None
-    if pg is not None and not args.profile:
+    if not args.profile:
         sharded = run_sharded(args, rank, local_rank, world, dev, pg)
+    sweep = None
+    if world == 1 and not args.profile:
+        sweep = sweep_points(sampler, x, p, u, dev, steps=200)
 
     result = None
     if rank == 0:
@@ -287,10 +328,7 @@ def run_ours(args, rank, local_rank, world):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32 (selection, sum-exp) / f64 (sampleFromTopK)",
             "data": "synthetic (seeded bf16-valued N(0,4^2) logits, heterogeneous params)",
-            "config": {"workload": WORKLOAD, "rows_per_gpu": ROWS, "vocab": VOCAB,
-                       "max_top_k": CAP, "parallelism": f"rows split x{world}, no collective",
-                       "l2": f"inputs rotate over {ROTATE} resident batches "
-                             f"({ROTATE * bytes_per_launch / 1e6:.0f} MB > 126 MB L2)"},
+            "config": bench_config(world),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS,
@@ -307,15 +345,23 @@ def run_ours(args, rank, local_rank, world):
         }
         if sharded is not None:
             result["sharded"] = sharded
+        if sweep is not None:
+            result["sweep"] = {"what": "c4 rows, V=151936, pool cap 1024, outcomes only; "
+                                       "each call on a different window of a 255 MB pool",
+                               "points": sweep}
     if pg is not None:
         pg.barrier()
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline and not args.profile:
             rate, threads, sample = cpu_reference(x, p, u, seconds=args.cpu_seconds)
+            rate1, _, sample1 = cpu_reference(x, p, u, seconds=max(2.0, args.cpu_seconds / 3),
+                                              threads=1)
             result["cpu_baseline"] = {
                 "value": rate, "unit": "rows/s", "cores": threads, "kind": "port",
+                "single_thread_value": rate1, "cpu_model": cpu_model(),
                 "sample": sample + " (C restatement of sampler.ts topK full sort + "
-                "sampleFromTopK, all host threads)"}
+                "sampleFromTopK, all host threads); single thread: " + sample1,
+                "reference_runtime": node_probe()}
         print(json.dumps(result), flush=True)
     sampler.close()
     if pg is not None:
@@ -328,14 +374,15 @@ SHARD_ROWS = 512  # the c5 configuration: B=512 x V=151936 split over the GPUs
 
 def run_sharded(args, rank, local_rank, world, dev, pg):
     """Vocab-sharded sampling (c5): every rank holds columns [r*V/N, (r+1)*V/N) of 512
-    rows; a step is the local top-64 blocks, one NCCL all-gather of the blocks and the
-    merge (every rank ends with the same tokens). Strong scaling: the job is 512 rows of
-    the full vocabulary whatever N is. Device-timed with CUDA events, max over ranks."""
+    rows; a step is the local top-64 blocks (row_kernel), one NCCL all-gather of the
+    blocks (none at N=1) and the merge (merge_kernel); every rank ends with the same
+    tokens. Strong scaling: the job is 512 rows of the full vocabulary whatever N is.
+    Device-timed with CUDA events on the launch stream, max over ranks, also per phase."""
     import torch
 
     from tabby_b200 import synth
-    from tabby_b200._lib import OUTCOME_DTYPE, check, lib
-    from tabby_b200.sharded import BLOCK_WORDS, SHARD_TOP_K, ShardedSampler, gather_blocks
+    from tabby_b200._lib import OUTCOME_DTYPE
+    from tabby_b200.sharded import SHARD_TOP_K, ShardedSampler, gather_blocks
 
     x, p, u = synth.config("c5", seed=0, rows=SHARD_ROWS)
     s = ShardedSampler(VOCAB, device=local_rank, max_rows=SHARD_ROWS)
@@ -344,57 +391,71 @@ def run_sharded(args, rank, local_rank, world, dev, pg):
     u_dev = torch.from_numpy(u).to(dev)
     out = torch.empty(SHARD_ROWS * OUTCOME_DTYPE.itemsize, dtype=torch.uint8, device=dev)
     ids = torch.empty((SHARD_ROWS, SHARD_TOP_K), dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
 
-    def step():
+    def step(ev=None):
+        if ev:
+            ev[0].record(stream)
         block = s.local_blocks(local)
-        gathered = gather_blocks(block)
+        if ev:
+            ev[1].record(stream)
+        gathered = gather_blocks(block) if pg is not None else block
+        if ev:
+            ev[2].record(stream)
         s.merge_async(gathered, world, p_dev, u_dev, out, ids, None)
+        if ev:
+            ev[3].record(stream)
 
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize(dev)
-    pg.barrier()
+    if pg is not None:
+        pg.barrier()
     steps = max(10, min(args.steps, 200))
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
+    e0.record(stream)
     for _ in range(steps):
         step()
-    e1.record()
+    e1.record(stream)
     torch.cuda.synchronize(dev)
-    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    pg.all_reduce(t, op=pg.ReduceOp.MAX)
-    ms = float(t.item()) / steps
+    total = e0.elapsed_time(e1) / steps
+    # Per phase, on separate steps (events between the launches of each step).
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(20)]
+    for ev in evs:
+        step(ev)
+    torch.cuda.synchronize(dev)
+    phase = [sum(ev[j].elapsed_time(ev[j + 1]) for ev in evs) / len(evs) for j in range(3)]
+    t = torch.tensor([total] + phase, dtype=torch.float64, device=dev)
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    total, *phase = [float(v) for v in t.tolist()]
     s.close()
     return {"metric": "sampled rows/s, vocab-sharded (c5: B=512 x V=151936 split over "
-                      f"{world} GPUs, local top-64, NCCL all-gather, merge)",
-            "value": SHARD_ROWS / (ms / 1e3), "unit": "rows/s", "ms_per_step": ms,
-            "steps": steps, "scaling": "strong",
-            "launches_per_step": "row_kernel + NCCL all-gather + merge_kernel"}
+                      f"{world} GPU(s), local top-64, NCCL all-gather, merge)",
+            "value": SHARD_ROWS / (total / 1e3), "unit": "rows/s", "ms_per_step": total,
+            "steps": steps, "scaling": "strong", "n_gpus": world,
+            "phases_us": {"local_row_kernel": 1e3 * phase[0],
+                          "all_gather": 1e3 * phase[1] if pg is not None else 0.0,
+                          "merge_kernel": 1e3 * phase[2]},
+            "local_columns": s.hi - s.lo,
+            "launches_per_step": "row_kernel + merge_kernel" + (
+                " + NCCL all-gather" if pg is not None else "")}
 
 
-SWEEP_ROWS = (1, 2, 4, 8, 16, 32, 64, 128, 256)
-
-
-def run_sweep(args):
-    """Batch sweep on one GPU: B rows of the c4 workload per call for B in SWEEP_ROWS.
-    Each call reads a different window of a 420-row resident pool (255 MB > L2), so every
-    call reads HBM; device-timed with CUDA events over the calls."""
+def sweep_points(sampler, x, p, u, dev, steps):
+    """B rows of the c4 workload per call for B in SWEEP_ROWS; each call reads a different
+    window of a 420-row resident pool (255 MB > L2). CUDA-event timed over the calls."""
     import torch
 
-    from tabby_b200 import Sampler, synth
     from tabby_b200._lib import OUTCOME_DTYPE, check, lib
 
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    x, p, u = synth.config("c4", seed=0)
     pool_rows = 420
     reps = (pool_rows + ROWS - 1) // ROWS
     pool = torch.from_numpy(np.ascontiguousarray(np.tile(x, (reps, 1))[:pool_rows])).to(dev)
-    sampler = Sampler(0, max_top_k=CAP, max_rows=ROWS, max_vocab=VOCAB)
     L = lib()
     sptr = torch.cuda.current_stream(dev).cuda_stream
-    peak, peak_kind = measured_peak()
+    peak, _ = measured_peak()
     points = []
     for b in SWEEP_ROWS:
         pb = torch.from_numpy(p[:b].view(np.uint8).copy()).to(dev)
@@ -404,14 +465,13 @@ def run_sweep(args):
 
         def step(i):
             r0 = (i * b) % windows
-            check(L.tabby_sample_rows_async(sampler.handle, pool[r0].data_ptr(), VOCAB, b, VOCAB,
-                                            pb.data_ptr(), ub.data_ptr(), out.data_ptr(), None,
-                                            None, 0, sptr))
+            check(L.tabby_sample_rows_async(sampler.handle, pool[r0].data_ptr(), VOCAB, b,
+                                            VOCAB, pb.data_ptr(), ub.data_ptr(),
+                                            out.data_ptr(), None, None, 0, sptr))
 
-        for i in range(max(args.warmup, 3)):
+        for i in range(3):
             step(i)
         torch.cuda.synchronize(dev)
-        steps = max(50, min(args.steps, 1000))
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -424,7 +484,26 @@ def run_sweep(args):
         points.append({"rows": b, "us_per_call": round(us, 2),
                        "rows_per_s": round(b / (us * 1e-6)), "gbs": round(gbs, 1),
                        "frac_of_peak": round(gbs / peak, 3)})
+    del pool
+    return points
+
+
+SWEEP_ROWS = (1, 2, 4, 8, 16, 32, 64, 128, 256)
+
+
+def run_sweep(args):
+    """Batch sweep on one GPU (one JSON line)."""
+    import torch
+
+    from tabby_b200 import Sampler, synth
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    x, p, u = synth.config("c4", seed=0)
+    sampler = Sampler(0, max_top_k=CAP, max_rows=ROWS, max_vocab=VOCAB)
+    points = sweep_points(sampler, x, p, u, dev, steps=max(50, min(args.steps, 1000)))
     sampler.close()
+    peak, peak_kind = measured_peak()
     print(json.dumps({"sweep": "c4 rows, V=151936, pool cap 1024, outcomes only",
                       "peak_gbs": peak, "peak_kind": peak_kind, "points": points}), flush=True)
     return 0
