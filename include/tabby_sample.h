@@ -247,6 +247,38 @@ TABBY_API int tabby_sample_rows_noalloc(const float *d_logits, int64_t row_strid
                                         int32_t *d_topk_ids, float *d_topk_values,
                                         int32_t topk_ld, void *stream);
 
+/*
+ * Fused LM head + sampling for the decode step (new in this build): replaces the
+ * reference's lm_head matmul into `this.logits` (src/engine/forward.ts:418-428,
+ * src/shaders/matmul_f16.wgsl / matvec_q4.wgsl) followed by the sampling dispatches
+ * (forward.ts:520-601) and sampleFromTopK (src/engine/sampler.ts:147-212). Logits
+ * hidden[r] . weight[v] (bf16 inputs, fp32 accumulation on the tensor cores) are consumed
+ * in the GEMM's epilogue and never written to HBM; the pool cap is the reference's
+ * MAX_TOP_K = 64 (kernels.ts:448).
+ * A handle holds the per-CTA partials for up to max_rows (<= TABBY_LMHEAD_MAX_ROWS) rows of
+ * a fixed vocab (<= TABBY_MAX_VOCAB_LMHEAD) and hidden size (a multiple of 64).
+ */
+#define TABBY_LMHEAD_MAX_ROWS 128
+#define TABBY_MAX_VOCAB_LMHEAD 16777216
+typedef struct tabby_lmhead tabby_lmhead;
+TABBY_API int tabby_lmhead_create(int32_t device, int32_t max_rows, int32_t vocab,
+                                  int32_t hidden, tabby_lmhead **out);
+TABBY_API int tabby_lmhead_destroy(tabby_lmhead *lmhead);
+/*
+ * d_hidden: bf16 [rows][hidden] row-major; d_weight: bf16 [vocab][hidden] row-major (the
+ * lm_head / tied embedding matrix); both 16-byte aligned. Per row: pool rule with cap 64,
+ * max and sum-exp of the row's logits, exact top-k (value desc, index asc), then
+ * sampleFromTopK with d_uniforms[r]; writes d_out[r] and, when non-NULL, the candidates
+ * (d_topk_ids / d_topk_values at stride topk_ld >= 64). d_logits_out (tests; normally
+ * NULL) receives the fp32 logits [rows][vocab] the epilogue saw. Asynchronous on `stream`.
+ */
+TABBY_API int tabby_lmhead_sample_async(tabby_lmhead *lmhead, const void *d_hidden,
+                                        const void *d_weight, int32_t rows,
+                                        const tabby_sampling_params *d_params,
+                                        const double *d_uniforms, tabby_sample_outcome *d_out,
+                                        int32_t *d_topk_ids, float *d_topk_values,
+                                        int32_t topk_ld, float *d_logits_out, void *stream);
+
 /* Pool-size rule of the worker (inference.worker.ts:120-123) with the handle's cap. */
 TABBY_API int32_t tabby_pool_size(double temperature, int32_t top_k, int32_t max_top_k);
 

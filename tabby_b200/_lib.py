@@ -75,6 +75,10 @@ SIGNATURES = {
         [_P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _I32, _P], ctypes.c_int),
     "tabby_sample_rows_debug_async": (
         [_P, _P, _I64, _I32, _I32, _P, _P, _P, ctypes.c_uint32, _I32, _P], ctypes.c_int),
+    "tabby_lmhead_create": ([_I32, _I32, _I32, _I32, ctypes.POINTER(_P)], ctypes.c_int),
+    "tabby_lmhead_destroy": ([_P], ctypes.c_int),
+    "tabby_lmhead_sample_async": (
+        [_P, _P, _P, _I32, _P, _P, _P, _P, _P, _I32, _P, _P], ctypes.c_int),
     "tabby_sample_rows": ([_P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _I32], ctypes.c_int),
     "tabby_topk_rows_async": ([_P, _P, _I64, _I32, _I32, _I32, _P, _I32, _P], ctypes.c_int),
     "tabby_shard_local_async": ([_P, _P, _I64, _I32, _I32, _I64, _P, _I32, _P], ctypes.c_int),

@@ -51,6 +51,27 @@ struct MergeLaunch {
   int32_t topk_ld = 0;
 };
 
+// Partial results of the fused LM-head kernel (lmhead.cu), per (row, CTA): the CTA's
+// (max, sum-exp) of the row over its vocabulary range and its kLmCands best logits of the
+// row as (raw float bits << 32 | vocab index); unused slots hold index 0xffffffff.
+constexpr int32_t kLmCands = 64;
+struct LmheadMergeLaunch {
+  const float2 *stats = nullptr;               // [rows][parts]
+  const unsigned long long *cands = nullptr;   // [rows][parts][kLmCands]
+  int32_t parts = 0;
+  int32_t rows = 0;
+  int32_t vocab = 0;
+  const tabby_sampling_params *params = nullptr;
+  const double *uniforms = nullptr;
+  uint32_t *rng_state = nullptr;
+  tabby_sample_outcome *out = nullptr;
+  int32_t *topk_ids = nullptr;
+  float *topk_values = nullptr;
+  int32_t topk_ld = 0;
+  const uint32_t *error = nullptr;  // non-zero: a bounded wait of the fused kernel ran out
+};
+cudaError_t launch_lmhead_merge(const LmheadMergeLaunch &l, cudaStream_t stream);
+
 // Geometry of one row pass: rows are cut into `nch` chunks of `chunk` logits; `grid`
 // persistent CTAs work through the rows * nch (row, chunk) units.
 struct RowGeometry {

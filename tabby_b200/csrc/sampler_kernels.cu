@@ -2323,6 +2323,127 @@ cudaError_t launch_merge(const MergeLaunch &l, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+
+// ------------------------------------------------------------------------------------
+// Fused LM-head finish: one CTA a row over the per-CTA partials of lmhead_kernel
+// (lmhead.cu). M = max m_c, S = sum s_c exp(m_c - M) in a fixed order, the global top-k
+// (k <= kLmCands, the reference's MAX_TOP_K) of the CTAs' best logits by (value desc,
+// index asc), then sampleFromTopK exactly as the row pass does.
+// ------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) lmhead_merge_kernel(LmheadMergeLaunch a) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ Shared sh_s;
+  Shared *sh = &sh_s;
+  uint64_t *cand = reinterpret_cast<uint64_t *>(smem_raw);
+  uint32_t *hist = reinterpret_cast<uint32_t *>(cand + kFinishCap);
+  const int row = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const tabby_sampling_params prm = a.params[row];
+  uint32_t pflags = (isnan(prm.temperature) || isnan(prm.top_p)) ? kFlagBadParams : 0u;
+  const int k = min(pool_rule(prm.temperature, prm.top_k, kLmCands), a.vocab);
+  double uni = (!a.rng_state && a.uniforms) ? a.uniforms[row] : 0.0;
+  // (max, sum-exp) of the CTAs, merged in CTA order.
+  float2 st = make_float2(-3.40282347e38f, 0.f);
+  if (tid < a.parts) st = a.stats[(int64_t)row * a.parts + tid];
+  float bm = st.x;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+  if (lane == 0) sh->red_f[warp] = bm;
+  if (tid == 0) sh->count = 0;
+  __syncthreads();
+  float M = lane < kWarps ? sh->red_f[lane] : -3.40282347e38f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float contrib = (tid < a.parts && st.y > 0.f) ? st.y * __expf(st.x - M) : 0.f;
+  const bool bad_part = tid < a.parts && (st.y != st.y || !(st.x <= 3.40282347e38f));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) contrib += __shfl_xor_sync(0xffffffffu, contrib, o);
+  const bool wbad = __any_sync(0xffffffffu, bad_part);
+  if (lane == 0) {
+    sh->red_f2[warp] = contrib;
+    sh->red_u[warp] = wbad ? 1u : 0u;
+  }
+  // The CTAs' candidates as composites (order-preserving key, inverted index).
+  const int total = a.parts * kLmCands;
+  const unsigned long long *rc = a.cands + (int64_t)row * total;
+  for (int i = tid; i < total; i += kThreads) {
+    const unsigned long long w = rc[i];
+    const uint32_t idx = (uint32_t)w;
+    if (idx != 0xffffffffu) {
+      const uint32_t slot = atomicAdd(&sh->count, 1u);
+      if (slot < (uint32_t)kFinishCap) cand[slot] = composite(key_of(__uint_as_float((uint32_t)(w >> 32))), idx);
+    }
+  }
+  __syncthreads();
+  float S = lane < kWarps ? sh->red_f2[lane] : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+  const bool bad = __any_sync(0xffffffffu, lane < kWarps && sh->red_u[lane] != 0u) ||
+                   !(S <= 3.40282347e38f) || !(M <= 3.40282347e38f);
+  const int n = min((int)sh->count, kFinishCap);
+  const bool timed_out = a.error && *a.error != 0u;
+  int kk = 0;
+  if (!timed_out && !bad && k > 0) kk = top_sorted(cand, n, k, kFinishCap, hist, sh);
+  else __syncthreads();
+  const uint32_t status = timed_out ? (uint32_t)TABBY_ETIMEOUT
+                          : bad     ? (uint32_t)TABBY_EINPUT
+                          : pflags  ? (uint32_t)TABBY_EINVAL
+                                    : (uint32_t)TABBY_OK;
+  if (warp != 0) return;
+  const uint64_t c0 = cand[2 * lane], c1 = cand[2 * lane + 1];
+  const int32_t id0 = (int32_t)~(uint32_t)c0, id1 = (int32_t)~(uint32_t)c1;
+  float x0 = float_of_key((uint32_t)(c0 >> 32)), x1 = float_of_key((uint32_t)(c1 >> 32));
+  // A zero logit keeps its sign: look its raw bits up among the partials (rare).
+  for (int e = 0; e < 2; e++) {
+    const int i = 2 * lane + e;
+    const uint64_t c = e ? c1 : c0;
+    if (i < kk && (uint32_t)(c >> 32) == 0x80000000u) {
+      const uint32_t want = ~(uint32_t)c;
+      for (int j = 0; j < total; j++)
+        if ((uint32_t)rc[j] == want) {
+          if (e) x1 = __uint_as_float((uint32_t)(rc[j] >> 32));
+          else x0 = __uint_as_float((uint32_t)(rc[j] >> 32));
+          break;
+        }
+    }
+  }
+  const float max_logit = kk > 0 ? __shfl_sync(0xffffffffu, x0, 0) : M;
+  if (a.topk_ids) {
+    if (2 * lane < kk) a.topk_ids[(int64_t)row * a.topk_ld + 2 * lane] = id0;
+    if (2 * lane + 1 < kk) a.topk_ids[(int64_t)row * a.topk_ld + 2 * lane + 1] = id1;
+  }
+  if (a.topk_values) {
+    if (2 * lane < kk) a.topk_values[(int64_t)row * a.topk_ld + 2 * lane] = x0;
+    if (2 * lane + 1 < kk) a.topk_values[(int64_t)row * a.topk_ld + 2 * lane + 1] = x1;
+  }
+  if (a.rng_state) {  // drawn only where sampleFromTopK draws (sampler.ts:153,159-167,194)
+    double un = 0.0;
+    if (lane == 0 && status == TABBY_OK && kk > 0 && prm.temperature > 0)
+      un = rng_next(&a.rng_state[row]);
+    uni = __shfl_sync(0xffffffffu, un, 0);
+  }
+  double *scratch = reinterpret_cast<double *>(hist);
+  finalize_warp(id0, id1, x0, x1, kk, max_logit, S, prm, uni, scratch, &a.out[row], status);
+}
+
+cudaError_t launch_lmhead_merge(const LmheadMergeLaunch &l, cudaStream_t stream) {
+  if (l.rows == 0) return cudaSuccess;
+  if (l.parts < 1 || l.parts > kThreads) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)kFinishCap * 8 + (size_t)kBins * 4;
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  cudaError_t set = cudaSuccess;
+  std::call_once(once[dev], [&]() {
+    set = cudaFuncSetAttribute(lmhead_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)smem);
+  });
+  if (set != cudaSuccess) return set;
+  lmhead_merge_kernel<<<l.rows, kThreads, smem, stream>>>(l);
+  return cudaGetLastError();
+}
+
 int host_sample_from_topk(const int32_t *ids, const float *logits, int32_t n, float max_logit,
                           float sum_exp, double temperature, double top_p, double u,
                           tabby_sample_outcome *out) {
