@@ -564,6 +564,84 @@ def run_softmax(args):
     return 0
 
 
+LMHEAD_ROWS = (1, 8, 32, 64, 128)
+
+
+def run_lmhead(args):
+    """Fused LM head + sampling (tabby_lmhead_sample_async) at V=151936, hidden 896
+    (Qwen2.5-0.5B's lm_head, bf16 weights, 272 MB: every call reads them from HBM), against
+    the unfused path of the same library: torch.matmul (cuBLAS bf16 -> fp32 logits) then
+    tabby_sample_rows_async. Device time per call with CUDA events; roofline against the
+    weight bytes (the dominant traffic) and the tensor FLOPs."""
+    import ctypes
+
+    import torch
+
+    from tabby_b200 import Sampler
+    from tabby_b200._lib import OUTCOME_DTYPE, check, lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    L = lib()
+    V, H = VOCAB, 896
+    g = torch.Generator(device="cuda").manual_seed(0)
+    w = (torch.randn(V, H, device=dev, generator=g) * (3.0 / H ** 0.5)).to(torch.bfloat16)
+    peak, peak_kind = measured_peak()
+    sampler = Sampler(0, max_top_k=64, max_rows=128, max_vocab=V)
+    sptr = torch.cuda.current_stream(dev).cuda_stream
+    points = []
+    for b in LMHEAD_ROWS:
+        h = torch.randn(b, H, device=dev, generator=g).to(torch.bfloat16)
+        p = np.zeros(b, [("temperature", "<f8"), ("top_p", "<f8"), ("top_k", "<i4"),
+                         ("reserved", "<i4")])
+        p["temperature"], p["top_p"], p["top_k"] = 0.8, 0.95, 40
+        pd = torch.from_numpy(p.view(np.uint8).copy()).to(dev)
+        ud = torch.rand(b, dtype=torch.float64, device=dev)
+        out = torch.empty(b * OUTCOME_DTYPE.itemsize, dtype=torch.uint8, device=dev)
+        handle = ctypes.c_void_p()
+        check(L.tabby_lmhead_create(0, b, V, H, ctypes.byref(handle)))
+
+        def fused():
+            check(L.tabby_lmhead_sample_async(handle, h.data_ptr(), w.data_ptr(), b,
+                                              pd.data_ptr(), ud.data_ptr(), out.data_ptr(),
+                                              None, None, 0, None, sptr))
+
+        def unfused():
+            logits = torch.matmul(h, w.T).float()
+            check(L.tabby_sample_rows_async(sampler.handle, logits.data_ptr(), V, b, V,
+                                            pd.data_ptr(), ud.data_ptr(), out.data_ptr(),
+                                            None, None, 0, sptr))
+
+        res = {}
+        for name, fn in (("fused_us", fused), ("unfused_us", unfused)):
+            for _ in range(5):
+                fn()
+            torch.cuda.synchronize(dev)
+            n = max(20, min(args.steps, 200))
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(n):
+                fn()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            res[name] = e0.elapsed_time(e1) * 1e3 / n
+        L.tabby_lmhead_destroy(handle)
+        wbytes = V * H * 2
+        gbs = wbytes / (res["fused_us"] * 1e-6) / 1e9
+        tflops = 2.0 * b * V * H / (res["fused_us"] * 1e-6) / 1e12
+        points.append({"rows": b, "fused_us": round(res["fused_us"], 2),
+                       "unfused_us": round(res["unfused_us"], 2),
+                       "speedup": round(res["unfused_us"] / res["fused_us"], 3),
+                       "weight_gbs": round(gbs, 1), "hbm_frac": round(gbs / peak, 3),
+                       "tensor_tflops": round(tflops, 1)})
+    sampler.close()
+    print(json.dumps({"lmhead": "fused LM head + sampling, V=151936 x hidden 896 bf16 "
+                                "(272 MB of weights a call), pool cap 64",
+                      "peak_gbs": peak, "peak_kind": peak_kind, "points": points}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -574,6 +652,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="batch sweep B=1..256 on one GPU")
     ap.add_argument("--softmax", action="store_true", help="softmax_rows shapes on one GPU")
+    ap.add_argument("--lmhead", action="store_true", help="fused LM head + sampling on one GPU")
     ap.add_argument("--profile", action="store_true",
                     help="only warm-up + timed steps (for ncu): no heat loop, e2e or CPU leg")
     args = ap.parse_args()
@@ -586,6 +665,8 @@ def main():
         return run_sweep(args) if rank == 0 else 0
     if args.softmax:
         return run_softmax(args) if rank == 0 else 0
+    if args.lmhead:
+        return run_lmhead(args) if rank == 0 else 0
     return run_ours(args, rank, local_rank, world)
 
 

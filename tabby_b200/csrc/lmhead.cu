@@ -7,20 +7,23 @@
 // dispatches (forward.ts:520-601) and sampleFromTopK (src/engine/sampler.ts:147-212).
 //
 //   lmhead_kernel   one CTA a SM, each a contiguous range of vocabulary tiles of 128 rows.
-//                   warp 0 (one lane)  TMA producer: cp.async.bulk.tensor 2-D loads of the
-//                                      hidden tile (128 x 64 bf16) and the weight tile
-//                                      (128 x 64 bf16), 128-byte swizzle, into a 4-stage
-//                                      ring (mbarrier transaction counts). No multicast.
+//                   warps 0 and 10     TMA producers (one lane each): cp.async.bulk.tensor 2-D loads of the
+//                                      weight tiles (128 x 64 bf16, an 8-stage ring: they
+//                                      come from HBM) and of the hidden-state tiles (128 x
+//                                      64 bf16, a 4-stage ring: they stay in L2), 128-byte
+//                                      swizzle, mbarrier transaction counts. No multicast.
 //                   warp 1 (one lane)  tcgen05.mma.cta_group::1.kind::f16, M = 128 token rows
 //                                      (rows past the batch are zero-filled by TMA), N = 128
 //                                      vocabulary rows, K = 16 a step, fp32 accumulators in
 //                                      TMEM, double-buffered (2 x 128 columns); tcgen05.commit
 //                                      frees a stage and hands a finished tile over.
 //                   warps 2-5          epilogue: tcgen05.ld 32x32b of the accumulator, one
-//                                      thread a token row: online max and sum(exp(x - max)),
-//                                      and the row's 64 best logits of the CTA's range kept
-//                                      in shared memory (replace-the-minimum), then the
-//                                      CTA's (max, sum-exp) and candidates to a partials
+//                                      thread a token row: online max and sum(exp(x - max));
+//                                      logits above the row's 64th best so far are appended
+//                                      to the row's pending list in shared memory, and the
+//                                      warp merges a row's pending list into its sorted best
+//                                      64 (bitonic networks) once 32 are pending; then the
+//                                      CTA's (max, sum-exp) and best 64 go to a partials
 //                                      buffer (optionally the logits themselves, for tests).
 //   lmhead_merge_kernel (sampler_kernels.cu) finishes every row: merged statistics, the
 //                   global top-k of the candidates, sampleFromTopK in float64.
@@ -38,6 +41,7 @@
 
 #include "sampler_internal.h"
 #include "tabby_sample.h"
+#include "warp_sort.cuh"
 
 namespace tabby {
 namespace {
@@ -45,14 +49,38 @@ namespace {
 constexpr int kLmM = 128;          // token rows of a tile (the MMA's M)
 constexpr int kLmN = 128;          // vocabulary rows of a tile (the MMA's N)
 constexpr int kLmK = 64;           // hidden elements a stage (128 bytes of bf16: one swizzle row)
-constexpr int kLmStages = 4;
-constexpr int kTileBytes = kLmM * kLmK * 2;  // 16 KB, A and B alike
+constexpr int kTileBytes = kLmM * kLmK * 2;   // 16 KB: a hidden-state tile
+constexpr int kWTileBytes = kLmN * kLmK * 2;  // 8 KB: a weight tile
 constexpr int kStageBytes2 = 2 * kTileBytes;
-constexpr int kLmThreads = 192;    // producer warp, MMA warp, 4 epilogue warps
+constexpr int kLmThreads = 352;    // weight producer, MMA, 8 epilogue warps, hidden producer
+constexpr int kEpiThreads = 256;   // two epilogue warps a TMEM lane quarter
 constexpr int kTmemCols = 2 * kLmN;
 constexpr unsigned long long kWaitNs = 500000000ull;  // a bounded wait gives up after 0.5 s
-// Dynamic shared memory: the stages, the candidate table [kLmCands][kLmM], barriers.
-constexpr size_t kLmSmem = 1024 + (size_t)kLmStages * kStageBytes2 + (size_t)kLmCands * kLmM * 8 + 256;
+// Candidate slots a row: its best 64 so far, sorted (slots 0-63), then up to 63 pending
+// composites above the 64th (slots 64-127), merged in by the warp once 32 are pending.
+constexpr int kLmBuf = 128;
+// The two variants of the kernel: the fast pass keeps a row's best kFastKeep logits of a
+// CTA's range in registers; the exact pass (run only for rows the fast pass could not
+// settle) keeps the best kLmCands in a shared-memory table.
+constexpr int kFastKeep = 16;
+template <int KL> struct LmVariant;
+// The weight tiles (from HBM) get a deeper ring than the hidden-state tiles (from L2).
+template <> struct LmVariant<kFastKeep> {
+  static constexpr int kWStages = 8;
+  static constexpr int kAStages = 4;
+  static constexpr size_t kTable = (size_t)32 * kEpiThreads * 4;  // staged logits [32][256]
+};
+template <> struct LmVariant<kLmCands> {
+  static constexpr int kWStages = 4;
+  static constexpr int kAStages = 2;
+  static constexpr size_t kTable = (size_t)kLmBuf * kLmM * 8;  // [kLmBuf][kLmM]
+};
+// Dynamic shared memory: the stages, the candidate table, barriers.
+template <int KL>
+constexpr size_t lm_smem() {
+  return 1024 + (size_t)LmVariant<KL>::kWStages * kWTileBytes +
+         (size_t)LmVariant<KL>::kAStages * kTileBytes + LmVariant<KL>::kTable + 256;
+}
 
 struct LmArgs {
   int32_t rows, vocab, hidden;
@@ -62,6 +90,7 @@ struct LmArgs {
   unsigned long long *cands;     // [rows][gridDim.x][kLmCands]
   float *logits_out;             // tests only: [rows][vocab] fp32, or NULL
   uint32_t *error;
+  const uint32_t *gate;          // non-NULL: run only when *gate != 0 (the exact pass)
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
@@ -149,6 +178,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -168,33 +202,66 @@ __device__ __forceinline__ uint64_t lm_comp(uint64_t raw_idx) {  // raw << 32 | 
          (uint64_t)(~(uint32_t)raw_idx);
 }
 
+// Index of (slot, row) in the candidate table. Rows are XOR-swizzled by the slot pair so
+// that both access patterns are free of bank conflicts: a warp's threads each on their own
+// row at one slot, and one warp walking one row's slots (two a lane).
+__device__ __forceinline__ int cidx(int slot, int row) {
+  return slot * kLmM + (row ^ ((slot >> 1) & 31));
+}
+
+// Merges the pending composites of row `rr` (one of this warp's 32 rows; `np` of them)
+// into its sorted best 64 (warp-uniform call): the pending ones are sorted by a bitonic
+// network, the two sorted lists merged keeping the 64 largest. Returns the 64th largest
+// (0 while fewer than 64 are kept).
+__device__ __forceinline__ uint64_t merge_pending(unsigned long long *tab, int rr, int np) {
+  const int lane = threadIdx.x & 31;
+  uint64_t w0 = 2 * lane < np ? tab[cidx(kLmCands + 2 * lane, rr)] : 0ull;
+  uint64_t w1 = 2 * lane + 1 < np ? tab[cidx(kLmCands + 2 * lane + 1, rr)] : 0ull;
+  warp_sort64_desc(w0, w1);
+  uint64_t a0 = tab[cidx(2 * lane, rr)], a1 = tab[cidx(2 * lane + 1, rr)];
+  warp_merge64_desc(a0, a1, w0, w1);
+  tab[cidx(2 * lane, rr)] = a0;
+  tab[cidx(2 * lane + 1, rr)] = a1;
+  return __shfl_sync(0xffffffffu, a1, 31);
+}
+
+template <int KL>
 __global__ void __launch_bounds__(kLmThreads, 1)
     lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__ CUtensorMap map_w,
                   const __grid_constant__ LmArgs a) {
+  constexpr int kW = LmVariant<KL>::kWStages, kA = LmVariant<KL>::kAStages;
+  if (a.gate && *a.gate == 0u) return;  // the exact pass, not needed this call
   extern __shared__ unsigned char smem_dyn[];
   unsigned char *base = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~(uintptr_t)1023);
-  unsigned char *stages = base;  // [stage]{A 16 KB, B 16 KB}
+  unsigned char *wring = base;                      // [kW] weight tiles
+  unsigned char *aring = base + kW * kWTileBytes;   // [kA] hidden-state tiles
   unsigned long long *cand =
-      reinterpret_cast<unsigned long long *>(base + kLmStages * kStageBytes2);  // [64][128]
-  uint64_t *bars = reinterpret_cast<uint64_t *>(cand + kLmCands * kLmM);
-  uint64_t *full = bars, *empty = bars + kLmStages;
-  uint64_t *tfull = bars + 2 * kLmStages, *tempty = tfull + 2;
+      reinterpret_cast<unsigned long long *>(aring + kA * kTileBytes);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(aring + kA * kTileBytes + LmVariant<KL>::kTable);
+  uint64_t *wfull = bars, *wempty = bars + kW;
+  uint64_t *afull = bars + 2 * kW, *aempty = afull + kA;
+  uint64_t *tfull = aempty + kA, *tempty = tfull + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
   volatile uint32_t *err = tmem_slot + 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int t0 = blockIdx.x * a.tiles_per_cta;
-  const int nt = max(0, min(a.tiles_per_cta, a.ntiles - t0));
+  // This CTA's tiles: an even share of them, contiguous.
+  const int t0 = (int)(((int64_t)blockIdx.x * a.ntiles) / gridDim.x);
+  const int nt = (int)(((int64_t)(blockIdx.x + 1) * a.ntiles) / gridDim.x) - t0;
   const int kb_n = a.hidden / kLmK;
 
   if (tid == 0) {
-    for (int s = 0; s < kLmStages; s++) {
-      mb_init(&full[s], 1);
-      mb_init(&empty[s], 1);
+    for (int s = 0; s < kW; s++) {
+      mb_init(&wfull[s], 1);
+      mb_init(&wempty[s], 1);
+    }
+    for (int s = 0; s < kA; s++) {
+      mb_init(&afull[s], 1);
+      mb_init(&aempty[s], 1);
     }
     for (int b = 0; b < 2; b++) {
       mb_init(&tfull[b], 1);
-      mb_init(&tempty[b], 128);
+      mb_init(&tempty[b], kEpiThreads);
     }
     *err = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -211,27 +278,33 @@ __global__ void __launch_bounds__(kLmThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ---- TMA producer ----
+  if (warp == 0 || warp == 10) {
+    // ---- TMA producers, one lane of their own warp each (a lane blocked on one ring must
+    // not hold up the other): warp 0 the weight tiles, warp 10 the hidden-state tiles ----
     if (lane == 0) {
+      const bool wt = warp == 0;
+      const int depth = wt ? kW : kA;
+      uint64_t *full = wt ? wfull : afull, *empty = wt ? wempty : aempty;
+      unsigned char *ring = wt ? wring : aring;
+      const int bytes = wt ? kWTileBytes : kTileBytes;
       int it = 0;
       for (int t = 0; t < nt && !*err; t++) {
         const int v0 = (t0 + t) * kLmN;
         for (int kb = 0; kb < kb_n; kb++, it++) {
-          const int s = it % kLmStages;
-          if (it >= kLmStages && !mb_wait(&empty[s], ((it / kLmStages) - 1) & 1)) {
+          const int s = it % depth;
+          if (it >= depth && !mb_wait(&empty[s], ((it / depth) - 1) & 1)) {
             *err = 1u;
             break;
           }
-          unsigned char *st = stages + s * kStageBytes2;
-          mb_arrive_expect(&full[s], kStageBytes2);
-          tma_load_2d(st, &map_h, kb * kLmK, 0, &full[s]);
-          tma_load_2d(st + kTileBytes, &map_w, kb * kLmK, v0, &full[s]);
+          mb_arrive_expect(&full[s], (uint32_t)bytes);
+          if (wt)
+            tma_load_2d(ring + s * bytes, &map_w, kb * kLmK, v0, &full[s]);
+          else
+            tma_load_2d(ring + s * bytes, &map_h, kb * kLmK, 0, &full[s]);
         }
       }
       // Every issued load has landed before the CTA may exit (bounded).
-      for (int j = max(0, it - kLmStages); j < it; j++)
-        mb_wait(&full[j % kLmStages], (j / kLmStages) & 1);
+      for (int j = max(0, it - depth); j < it; j++) mb_wait(&full[j % depth], (j / depth) & 1);
     }
   } else if (warp == 1) {
     // ---- MMA issuer ----
@@ -246,32 +319,153 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(b * kLmN);
         for (int kb = 0; kb < kb_n; kb++, it++) {
-          const int s = it % kLmStages;
-          if (!mb_wait(&full[s], (it / kLmStages) & 1)) {
+          const int sw = it % kW, sa = it % kA;
+          if (!mb_wait(&wfull[sw], (it / kW) & 1) || !mb_wait(&afull[sa], (it / kA) & 1)) {
             *err = 1u;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_addr(stages + s * kStageBytes2);
+          const uint32_t wa = smem_addr(wring + sw * kWTileBytes);
+          const uint32_t ha = smem_addr(aring + sa * kTileBytes);
 #pragma unroll
           for (int kk = 0; kk < kLmK / 16; kk++)  // 16 bf16 = 32 bytes a step along K
-            mma_bf16(d, smem_desc(sa + 32 * kk), smem_desc(sa + kTileBytes + 32 * kk),
-                     (kb | kk) != 0 ? 1u : 0u);
-          mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+            mma_bf16(d, smem_desc(ha + 32 * kk), smem_desc(wa + 32 * kk), (kb | kk) != 0 ? 1u : 0u);
+          mma_commit(&wempty[sw]);  // the stages are free once these MMAs have read them
+          mma_commit(&aempty[sa]);
         }
         if (*err) break;
         mma_commit(&tfull[b]);  // the tile's accumulator is complete
       }
     }
   } else {
-    // ---- epilogue: thread = token row (TMEM lane 32 * (warp % 4) + lane) ----
+    // ---- epilogue: thread = token row (TMEM lane 32 * (warp % 4) + lane); the two warps
+    // of a lane quarter take the two halves of every tile's columns, each its own part ----
     const int q = warp & 3;
     const int row = 32 * q + lane;
+    const int et = tid - 64;        // epilogue thread
+    const int hf = et >> 7;         // which half of the columns
+    const int parts = 2 * gridDim.x;
+    const int pi = 2 * blockIdx.x + hf;
     const bool live = row < a.rows;
     float m = -3.40282347e38f, s = 0.f;
-    int filled = 0, min_slot = 0;
-    uint64_t min_c = 0ull;  // composite of the smallest kept candidate
     constexpr float kLog2e = 1.44269504088896341f;
+    if constexpr (KL == kFastKeep) {
+      // The row's best kFastKeep composites of this CTA's range, sorted in registers;
+      // a logit above the last one is inserted by one branch-free pass.
+      float *stage_f = reinterpret_cast<float *>(cand);  // the variant's table: [32][256]
+      uint64_t best[kFastKeep];
+#pragma unroll
+      for (int e = 0; e < kFastKeep; e++) best[e] = 0ull;
+      float thr_val = -3.40282347e38f;
+      for (int t = 0; t < nt; t++) {
+        const int b = t & 1;
+        if (!mb_wait(&tfull[b], (t >> 1) & 1)) {
+          *err = 1u;
+          break;
+        }
+        tc_fence_after();
+        const int v0 = (t0 + t) * kLmN;
+#pragma unroll 1
+        for (int c = hf * (kLmN / 64); c < (hf + 1) * (kLmN / 64); c++) {
+          uint32_t r[32];
+          tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kLmN + 32 * c), r);
+          const int vb = v0 + 32 * c;
+          const int nv = live ? min(32, a.vocab - vb) : 0;
+          if (nv <= 0) continue;
+          float cm = -3.40282347e38f;
+#pragma unroll
+          for (int j = 0; j < 32; j++)
+            if (j < nv) cm = fmaxf(cm, __uint_as_float(r[j]));
+          if (cm > m) {
+            s *= ex2_fast((m - cm) * kLog2e);
+            m = cm;
+          }
+          const float mL = m * kLog2e;
+          float acc = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; j++)
+            if (j < nv) acc += ex2_fast(fmaf(__uint_as_float(r[j]), kLog2e, -mL));
+          s += acc;
+          if (a.logits_out) {
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+              if (j < nv) a.logits_out[(int64_t)row * a.vocab + vb + j] = __uint_as_float(r[j]);
+          }
+          if (cm >= thr_val) {
+            // The logits at or above the threshold: a mask, then one compact loop over
+            // them (staged in shared memory) for the insertions.
+            uint32_t hits = 0;
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+              hits |= (j < nv && __uint_as_float(r[j]) >= thr_val) ? (1u << j) : 0u;
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+              if ((hits >> j) & 1u) stage_f[j * kEpiThreads + et] = __uint_as_float(r[j]);
+            while (hits) {
+              const int j = __ffs(hits) - 1;
+              hits &= hits - 1;
+              const float x = stage_f[j * kEpiThreads + et];
+              if (x >= thr_val) {
+                uint64_t v = ((uint64_t)lm_key(x) << 32) | (uint64_t)(~(uint32_t)(vb + j));
+                if (v > best[kFastKeep - 1]) {
+#pragma unroll
+                  for (int e = 0; e < kFastKeep; e++) {
+                    const uint64_t hi = best[e] > v ? best[e] : v;
+                    v = best[e] > v ? v : best[e];
+                    best[e] = hi;
+                  }
+                  if (best[kFastKeep - 1] != 0ull) {
+                    const uint32_t kk = (uint32_t)(best[kFastKeep - 1] >> 32);
+                    thr_val = __uint_as_float(kk ^ ((kk >> 31) ? 0x80000000u : 0xffffffffu));
+                  }
+                }
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        mb_arrive(&tempty[b]);  // the accumulator may be overwritten
+      }
+      if (live) {
+        a.stats[(int64_t)row * parts + pi] = make_float2(m, s);
+        unsigned long long *dst = a.cands + ((int64_t)row * parts + pi) * kLmCands;
+#pragma unroll
+        for (int e = 0; e < kLmCands; e++) {
+          const uint64_t c = e < kFastKeep ? best[e < kFastKeep ? e : 0] : 0ull;
+          const uint32_t kk = (uint32_t)(c >> 32);
+          const uint32_t raw = kk ^ ((kk >> 31) ? 0x80000000u : 0xffffffffu);
+          dst[e] = c != 0ull ? (((uint64_t)raw << 32) | (uint64_t)(~(uint32_t)c)) : 0xffffffffull;
+        }
+      }
+    } else {
+    int pend = 0;                     // this row's pending composites
+    uint64_t thr = 0ull;              // candidates must exceed the row's 64th best
+    float thr_val = -3.40282347e38f;  // its value: a cheap first filter (>=)
+    // The exact pass uses the first warp of each lane quarter for all columns; the second
+    // only releases the accumulators and reports an empty part.
+    if (hf == 0)
+      for (int e = 0; e < kLmCands; e++) cand[cidx(e, row)] = 0ull;  // nothing kept yet
+    __syncwarp();
+    // Merges, for every row of this warp with at least `at_least` pending, the pending
+    // composites into the row's best 64, and raises its thresholds.
+    auto merge_rows = [&](int at_least) {
+      uint32_t need = __ballot_sync(0xffffffffu, pend >= at_least && pend > 0);
+      while (need) {
+        const int rr = __ffs(need) - 1;
+        need &= need - 1;
+        const int np = __shfl_sync(0xffffffffu, pend, rr);
+        const uint64_t t = merge_pending(cand, 32 * q + rr, np);
+        if (lane == rr) {
+          pend = 0;
+          if (t != 0ull) {
+            thr = t;
+            const uint32_t kk = (uint32_t)(t >> 32);
+            thr_val = __uint_as_float(kk ^ ((kk >> 31) ? 0x80000000u : 0xffffffffu));
+          }
+        }
+        __syncwarp();
+      }
+    };
     for (int t = 0; t < nt; t++) {
       const int b = t & 1;
       if (!mb_wait(&tfull[b], (t >> 1) & 1)) {
@@ -281,65 +475,60 @@ __global__ void __launch_bounds__(kLmThreads, 1)
       tc_fence_after();
       const int v0 = (t0 + t) * kLmN;
 #pragma unroll 1
-      for (int c = 0; c < kLmN / 32; c++) {
+      for (int c = 0; c < (hf == 0 ? kLmN / 32 : 0); c++) {
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kLmN + 32 * c), r);
-        if (!live) continue;
         const int vb = v0 + 32 * c;
-        const int nv = min(32, a.vocab - vb);
-        if (nv <= 0) continue;
-        float cm = -3.40282347e38f;
-#pragma unroll
-        for (int j = 0; j < 32; j++)
-          if (j < nv) cm = fmaxf(cm, __uint_as_float(r[j]));
-        if (cm > m) {
-          s *= exp2f((m - cm) * kLog2e);
-          m = cm;
-        }
-        const float mL = m * kLog2e;
-#pragma unroll
-        for (int j = 0; j < 32; j++)
-          if (j < nv) s += exp2f(fmaf(__uint_as_float(r[j]), kLog2e, -mL));
-        if (a.logits_out) {
+        const int nv = live ? min(32, a.vocab - vb) : 0;
+        if (nv > 0) {
+          float cm = -3.40282347e38f;
 #pragma unroll
           for (int j = 0; j < 32; j++)
-            if (j < nv) a.logits_out[(int64_t)row * a.vocab + vb + j] = __uint_as_float(r[j]);
-        }
-        // The row's 64 best of this CTA: fill, then replace the smallest.
-#pragma unroll 1
-        for (int j = 0; j < nv; j++) {
-          const uint64_t raw = ((uint64_t)r[j] << 32) | (uint32_t)(vb + j);
-          const uint64_t cmp = lm_comp(raw);
-          if (filled < kLmCands) {
-            cand[filled * kLmM + row] = raw;
-            if (filled == 0 || cmp < min_c) {
-              min_c = cmp;
-              min_slot = filled;
-            }
-            filled++;
-          } else if (cmp > min_c) {
-            cand[min_slot * kLmM + row] = raw;
-            min_c = ~0ull;
-            for (int e = 0; e < kLmCands; e++) {
-              const uint64_t ce = lm_comp(cand[e * kLmM + row]);
-              if (ce < min_c) {
-                min_c = ce;
-                min_slot = e;
+            if (j < nv) cm = fmaxf(cm, __uint_as_float(r[j]));
+          if (cm > m) {
+            s *= ex2_fast((m - cm) * kLog2e);
+            m = cm;
+          }
+          const float mL = m * kLog2e;
+          float acc = 0.f;
+#pragma unroll
+          for (int j = 0; j < 32; j++)
+            if (j < nv) acc += ex2_fast(fmaf(__uint_as_float(r[j]), kLog2e, -mL));
+          s += acc;
+          if (a.logits_out) {
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+              if (j < nv) a.logits_out[(int64_t)row * a.vocab + vb + j] = __uint_as_float(r[j]);
+          }
+          if (cm >= thr_val) {
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+              const float x = __uint_as_float(r[j]);
+              if (j < nv && x >= thr_val) {
+                const uint64_t cmp = ((uint64_t)lm_key(x) << 32) | (uint64_t)(~(uint32_t)(vb + j));
+                if (cmp > thr) cand[cidx(kLmCands + pend++, row)] = cmp;
               }
             }
           }
         }
+        merge_rows(32);  // keeps every row's pending list below 64
       }
       tc_fence_before();
       mb_arrive(&tempty[b]);  // the accumulator may be overwritten
     }
+    if (hf == 0) merge_rows(1);  // the last pending composites of every row
     if (live) {
-      const int parts = gridDim.x;
-      a.stats[(int64_t)row * parts + blockIdx.x] = make_float2(m, s);
-      unsigned long long *dst = a.cands + ((int64_t)row * parts + blockIdx.x) * kLmCands;
-      for (int e = 0; e < kLmCands; e++)
-        dst[e] = e < filled ? cand[e * kLmM + row] : 0xffffffffull;
+      a.stats[(int64_t)row * parts + pi] = make_float2(m, s);
+      unsigned long long *dst = a.cands + ((int64_t)row * parts + pi) * kLmCands;
+      for (int e = 0; e < kLmCands; e++) {
+        const uint64_t c = hf == 0 ? cand[cidx(e, row)] : 0ull;  // composite: raw value bits from the key (+0 for a
+                                           // -0 logit, the one value the key folds)
+        const uint32_t kk = (uint32_t)(c >> 32);
+        const uint32_t raw = kk ^ ((kk >> 31) ? 0x80000000u : 0xffffffffu);
+        dst[e] = c != 0ull ? (((uint64_t)raw << 32) | (uint64_t)(~(uint32_t)c)) : 0xffffffffull;
+      }
     }
+      }
   }
   tc_fence_before();
   __syncthreads();
@@ -372,14 +561,14 @@ EncodeTiled encode_fn() {
   return fn;
 }
 
-// K-major bf16 matrix [outer][inner] with boxes of 64 x 128 (inner x outer), 128-byte
+// K-major bf16 matrix [outer][inner] with boxes of 64 x box_rows (inner x outer), 128-byte
 // swizzle, zero fill out of bounds.
-bool make_map(CUtensorMap *m, const void *ptr, uint64_t inner, uint64_t outer) {
+bool make_map(CUtensorMap *m, const void *ptr, uint64_t inner, uint64_t outer, uint32_t box_rows) {
   EncodeTiled enc = encode_fn();
   if (!enc) return false;
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {inner * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kLmK, 128u};
+  const cuuint32_t box[2] = {(cuuint32_t)kLmK, box_rows};
   const cuuint32_t elem[2] = {1u, 1u};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box,
              elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -400,6 +589,12 @@ int lfail(int status, const char *fmt, ...) {
 }  // namespace tabby
 
 struct tabby_lmhead {
+  void *hidden_pad;        // [kLmM][hidden] bf16: the call's rows are copied in, so no TMA
+                           // box of the hidden states is out of bounds (those are slow);
+                           // rows past the batch hold stale values the epilogue never reads
+  CUtensorMap map_h;       // over hidden_pad
+  CUtensorMap map_w;       // over the last weight pointer
+  const void *map_w_ptr;
   int32_t device;
   int32_t max_rows;
   int32_t vocab;
@@ -409,7 +604,8 @@ struct tabby_lmhead {
   int32_t ntiles;
   float2 *stats;
   unsigned long long *cands;
-  uint32_t *error;
+  uint32_t *error;  // [0] a bounded wait ran out, [1] some row needs the exact pass
+  uint32_t *flags;  // [max_rows] rows the exact pass recomputes
 };
 
 extern "C" {
@@ -444,21 +640,36 @@ int tabby_lmhead_create(int32_t device, int32_t max_rows, int32_t vocab, int32_t
   h->vocab = vocab;
   h->hidden = hidden;
   h->ntiles = (vocab + kLmN - 1) / kLmN;
-  h->tiles_per_cta = (h->ntiles + sms - 1) / std::max(sms, 1);
-  h->grid = (h->ntiles + h->tiles_per_cta - 1) / h->tiles_per_cta;
-  const size_t nst = (size_t)max_rows * h->grid;
+  h->grid = std::min(h->ntiles, std::max(sms, 1));  // every SM, an even share of tiles each
+  h->tiles_per_cta = (h->ntiles + h->grid - 1) / h->grid;
+  const size_t nst = (size_t)max_rows * h->grid * 2;  // two parts a CTA
   if ((err = cudaMalloc(&h->stats, nst * sizeof(float2))) != cudaSuccess ||
       (err = cudaMalloc(&h->cands, nst * kLmCands * 8)) != cudaSuccess ||
       (err = cudaMalloc(&h->error, 16)) != cudaSuccess ||
       (err = cudaMemset(h->error, 0, 16)) != cudaSuccess ||
-      (err = cudaFuncSetAttribute(lmhead_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)kLmSmem)) != cudaSuccess) {
+      (err = cudaMalloc(&h->flags, (size_t)max_rows * 4)) != cudaSuccess ||
+      (err = cudaMalloc(&h->hidden_pad, (size_t)kLmM * hidden * 2)) != cudaSuccess ||
+      (err = cudaMemset(h->hidden_pad, 0, (size_t)kLmM * hidden * 2)) != cudaSuccess ||
+      (err = cudaMemset(h->flags, 0, (size_t)max_rows * 4)) != cudaSuccess ||
+      (err = cudaFuncSetAttribute(lmhead_kernel<kFastKeep>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)lm_smem<kFastKeep>())) != cudaSuccess ||
+      (err = cudaFuncSetAttribute(lmhead_kernel<kLmCands>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)lm_smem<kLmCands>())) != cudaSuccess) {
+    if (h->flags) cudaFree(h->flags);
+    if (h->hidden_pad) cudaFree(h->hidden_pad);
     if (h->stats) cudaFree(h->stats);
     if (h->cands) cudaFree(h->cands);
     if (h->error) cudaFree(h->error);
     delete h;
     if (cur != device) cudaSetDevice(cur);
     return lfail(TABBY_ENOMEM, "LM-head set-up failed: %s", cudaGetErrorString(err));
+  }
+  if (!make_map(&h->map_h, h->hidden_pad, (uint64_t)hidden, (uint64_t)kLmM, (uint32_t)kLmM)) {
+    if (cur != device) cudaSetDevice(cur);
+    tabby_lmhead_destroy(h);
+    return lfail(TABBY_ECUDA, "cuTensorMapEncodeTiled failed");
   }
   if (cur != device) cudaSetDevice(cur);
   *out = h;
@@ -473,6 +684,8 @@ int tabby_lmhead_destroy(tabby_lmhead *h) {
   cudaFree(h->stats);
   cudaFree(h->cands);
   cudaFree(h->error);
+  cudaFree(h->flags);
+  cudaFree(h->hidden_pad);
   if (cur != h->device) cudaSetDevice(cur);
   delete h;
   return TABBY_OK;
@@ -498,13 +711,21 @@ int tabby_lmhead_sample_async(tabby_lmhead *h, const void *d_hidden, const void 
   cudaError_t err = cudaGetDevice(&cur);
   if (err == cudaSuccess && cur != h->device) err = cudaSetDevice(h->device);
   if (err != cudaSuccess) return lfail(TABBY_ECUDA, "cudaSetDevice: %s", cudaGetErrorString(err));
-  CUtensorMap mh, mw;
-  if (!make_map(&mh, d_hidden, (uint64_t)h->hidden, (uint64_t)rows) ||
-      !make_map(&mw, d_weight, (uint64_t)h->hidden, (uint64_t)h->vocab)) {
-    if (cur != h->device) cudaSetDevice(cur);
-    return lfail(TABBY_ECUDA, "cuTensorMapEncodeTiled failed");
+  if (d_weight != h->map_w_ptr) {
+    if (!make_map(&h->map_w, d_weight, (uint64_t)h->hidden, (uint64_t)h->vocab, (uint32_t)kLmN)) {
+      if (cur != h->device) cudaSetDevice(cur);
+      return lfail(TABBY_ECUDA, "cuTensorMapEncodeTiled failed");
+    }
+    h->map_w_ptr = d_weight;
   }
+  const CUtensorMap &mh = h->map_h, &mw = h->map_w;
   cudaStream_t q = (cudaStream_t)stream;
+  err = cudaMemcpyAsync(h->hidden_pad, d_hidden, (size_t)rows * h->hidden * 2,
+                        cudaMemcpyDeviceToDevice, q);
+  if (err != cudaSuccess) {
+    if (cur != h->device) cudaSetDevice(cur);
+    return lfail(TABBY_ECUDA, "copy of the hidden states: %s", cudaGetErrorString(err));
+  }
   LmArgs a;
   a.rows = rows;
   a.vocab = h->vocab;
@@ -515,25 +736,40 @@ int tabby_lmhead_sample_async(tabby_lmhead *h, const void *d_hidden, const void 
   a.cands = h->cands;
   a.logits_out = d_logits_out;
   a.error = h->error;
-  err = cudaMemsetAsync(h->error, 0, 4, q);
+  // The fast pass and its merge; then the exact pass and its merge, which return at once
+  // unless the fast merge flagged a row (a part's 16th best above the row's k-th best).
+  a.gate = nullptr;
+  if (err == cudaSuccess) err = cudaMemsetAsync(h->error, 0, 8, q);
+  LmheadMergeLaunch l;
+  l.stats = h->stats;
+  l.cands = h->cands;
+  l.parts = 2 * h->grid;
+  l.rows = rows;
+  l.vocab = h->vocab;
+  l.params = d_params;
+  l.uniforms = d_uniforms;
+  l.out = d_out;
+  l.topk_ids = d_topk_ids;
+  l.topk_values = d_topk_values;
+  l.topk_ld = topk_ld;
+  l.error = h->error;
+  l.row_flag = h->flags;
+  l.any_flag = h->error + 1;
   if (err == cudaSuccess) {
-    lmhead_kernel<<<h->grid, kLmThreads, kLmSmem, q>>>(mh, mw, a);
+    lmhead_kernel<kFastKeep><<<h->grid, kLmThreads, lm_smem<kFastKeep>(), q>>>(mh, mw, a);
     err = cudaGetLastError();
   }
   if (err == cudaSuccess) {
-    LmheadMergeLaunch l;
-    l.stats = h->stats;
-    l.cands = h->cands;
-    l.parts = h->grid;
-    l.rows = rows;
-    l.vocab = h->vocab;
-    l.params = d_params;
-    l.uniforms = d_uniforms;
-    l.out = d_out;
-    l.topk_ids = d_topk_ids;
-    l.topk_values = d_topk_values;
-    l.topk_ld = topk_ld;
-    l.error = h->error;
+    l.keep = kFastKeep;
+    err = launch_lmhead_merge(l, q);
+  }
+  if (err == cudaSuccess) {
+    a.gate = h->error + 1;
+    lmhead_kernel<kLmCands><<<h->grid, kLmThreads, lm_smem<kLmCands>(), q>>>(mh, mw, a);
+    err = cudaGetLastError();
+  }
+  if (err == cudaSuccess) {
+    l.keep = kLmCands;
     err = launch_lmhead_merge(l, q);
   }
   if (cur != h->device) cudaSetDevice(cur);

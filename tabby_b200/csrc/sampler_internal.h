@@ -69,6 +69,14 @@ struct LmheadMergeLaunch {
   float *topk_values = nullptr;
   int32_t topk_ld = 0;
   const uint32_t *error = nullptr;  // non-zero: a bounded wait of the fused kernel ran out
+  // keep < kLmCands (the fast pass): each part kept only its best `keep`; the merge checks
+  // that no part's last kept candidate lies above the row's k-th best and, where one does,
+  // sets row_flag[row] and *any_flag so the exact pass recomputes the row. keep ==
+  // kLmCands with row_flag set (the exact pass's merge): only flagged rows are finished,
+  // and their flags cleared.
+  int32_t keep = kLmCands;
+  uint32_t *row_flag = nullptr;
+  uint32_t *any_flag = nullptr;
 };
 cudaError_t launch_lmhead_merge(const LmheadMergeLaunch &l, cudaStream_t stream);
 

@@ -41,6 +41,7 @@
 #include <type_traits>
 
 #include "finalize.cuh"
+#include "warp_sort.cuh"
 #include "sampler_internal.h"
 
 namespace tabby {
@@ -389,29 +390,6 @@ __device__ __noinline__ uint64_t select_top(uint64_t *cand, int n, int k, uint32
   return thr;
 }
 
-// Bitonic sort of 64 values held two per lane (lane l holds elements 2l, 2l+1), descending.
-__device__ __forceinline__ void warp_sort64_desc(uint64_t &v0, uint64_t &v1) {
-  const int lane = threadIdx.x & 31;
-  const int j0 = 2 * lane, j1 = j0 + 1;
-#pragma unroll
-  for (int size = 2; size <= 64; size <<= 1) {
-#pragma unroll
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      uint64_t p0, p1;
-      if (stride == 1) {
-        p0 = v1;
-        p1 = v0;
-      } else {
-        p0 = __shfl_xor_sync(0xffffffffu, v0, stride >> 1);
-        p1 = __shfl_xor_sync(0xffffffffu, v1, stride >> 1);
-      }
-      const bool lower0 = (j0 & stride) == 0, desc0 = (j0 & size) == 0;
-      const bool lower1 = (j1 & stride) == 0, desc1 = (j1 & size) == 0;
-      v0 = (lower0 == desc0) ? (v0 > p0 ? v0 : p0) : (v0 < p0 ? v0 : p0);
-      v1 = (lower1 == desc1) ? (v1 > p1 ? v1 : p1) : (v1 < p1 ? v1 : p1);
-    }
-  }
-}
 
 // Bitonic network for N (a power of two, 128..1024) values held two per thread of a
 // 512-thread block (elements 2t, 2t+1), descending. Fully unrolled: strides up to 32
@@ -748,29 +726,6 @@ __device__ __noinline__ void finalize_sample(const int32_t *ids, const float *va
   }
 }
 
-// Merges the sorted 64-list (w0, w1) into the sorted 64-list (v0, v1) (both descending,
-// lane l holding elements 2l and 2l+1), keeping the 64 largest, sorted. The elementwise
-// max of one list and the other reversed holds exactly the 64 largest of both and is
-// bitonic; a bitonic merge sorts it.
-__device__ __forceinline__ void warp_merge64_desc(uint64_t &v0, uint64_t &v1, uint64_t w0,
-                                                  uint64_t w1) {
-  const int lane = threadIdx.x & 31;
-  const uint64_t r0 = __shfl_sync(0xffffffffu, w1, 31 - lane);
-  const uint64_t r1 = __shfl_sync(0xffffffffu, w0, 31 - lane);
-  v0 = v0 > r0 ? v0 : r0;
-  v1 = v1 > r1 ? v1 : r1;
-#pragma unroll
-  for (int stride = 32; stride >= 2; stride >>= 1) {
-    const uint64_t p0 = __shfl_xor_sync(0xffffffffu, v0, stride >> 1);
-    const uint64_t p1 = __shfl_xor_sync(0xffffffffu, v1, stride >> 1);
-    const bool lower = ((2 * lane) & stride) == 0;
-    v0 = lower ? (v0 > p0 ? v0 : p0) : (v0 < p0 ? v0 : p0);
-    v1 = lower ? (v1 > p1 ? v1 : p1) : (v1 < p1 ? v1 : p1);
-  }
-  const uint64_t hi = v0 > v1 ? v0 : v1;
-  v1 = v0 > v1 ? v1 : v0;
-  v0 = hi;
-}
 
 // The min(64, n) largest of cand[0, n), sorted descending, into cand[0, 64) (zeros past
 // n). Block-uniform call. Every warp keeps a running top 64 of its share in registers
@@ -2337,6 +2292,8 @@ __global__ void __launch_bounds__(kThreads) lmhead_merge_kernel(LmheadMergeLaunc
   uint64_t *cand = reinterpret_cast<uint64_t *>(smem_raw);
   uint32_t *hist = reinterpret_cast<uint32_t *>(cand + kFinishCap);
   const int row = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool exact_pass = a.keep >= kLmCands && a.row_flag != nullptr;
+  if (exact_pass && __ldcg(a.row_flag + row) == 0u) return;  // settled by the fast pass
   const tabby_sampling_params prm = a.params[row];
   uint32_t pflags = (isnan(prm.temperature) || isnan(prm.top_p)) ? kFlagBadParams : 0u;
   const int k = min(pool_rule(prm.temperature, prm.top_k, kLmCands), a.vocab);
@@ -2365,8 +2322,9 @@ __global__ void __launch_bounds__(kThreads) lmhead_merge_kernel(LmheadMergeLaunc
   // The CTAs' candidates as composites (order-preserving key, inverted index).
   const int total = a.parts * kLmCands;
   const unsigned long long *rc = a.cands + (int64_t)row * total;
-  for (int i = tid; i < total; i += kThreads) {
-    const unsigned long long w = rc[i];
+  const int keep = min(a.keep, kLmCands);
+  for (int i = tid; i < a.parts * keep; i += kThreads) {  // the entries each part used
+    const unsigned long long w = rc[(i / keep) * kLmCands + i % keep];
     const uint32_t idx = (uint32_t)w;
     if (idx != 0xffffffffu) {
       const uint32_t slot = atomicAdd(&sh->count, 1u);
@@ -2384,6 +2342,26 @@ __global__ void __launch_bounds__(kThreads) lmhead_merge_kernel(LmheadMergeLaunc
   int kk = 0;
   if (!timed_out && !bad && k > 0) kk = top_sorted(cand, n, k, kFinishCap, hist, sh);
   else __syncthreads();
+  if (a.keep < kLmCands && a.row_flag) {
+    // The fast pass: a part whose last kept candidate lies above the k-th best may have
+    // dropped one of the top k; such a row goes to the exact pass.
+    const uint64_t kth = (kk == k && k > 0) ? cand[k - 1] : 0ull;
+    bool unsettled = false;
+    if (tid < a.parts && k > 0 && !timed_out && !bad) {
+      const unsigned long long w = rc[(int64_t)tid * kLmCands + a.keep - 1];
+      if ((uint32_t)w != 0xffffffffu &&
+          composite(key_of(__uint_as_float((uint32_t)(w >> 32))), (uint32_t)w) > kth)
+        unsettled = true;
+    }
+    if (__syncthreads_or(unsettled ? 1 : 0)) {
+      if (tid == 0) {
+        a.row_flag[row] = 1u;
+        atomicOr(a.any_flag, 1u);
+      }
+      return;  // the exact pass writes this row
+    }
+  }
+  if (exact_pass && tid == 0) a.row_flag[row] = 0u;
   const uint32_t status = timed_out ? (uint32_t)TABBY_ETIMEOUT
                           : bad     ? (uint32_t)TABBY_EINPUT
                           : pflags  ? (uint32_t)TABBY_EINVAL
