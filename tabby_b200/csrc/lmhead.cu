@@ -49,8 +49,10 @@ namespace {
 constexpr int kLmM = 128;          // token rows of a tile (the MMA's M)
 constexpr int kLmN = 128;          // vocabulary rows of a tile (the MMA's N)
 constexpr int kLmK = 64;           // hidden elements a stage (128 bytes of bf16: one swizzle row)
+constexpr int kLmUnit = 16;        // CTAs own vocabulary ranges in units of 16 rows (the MMA's
+                                   // smallest N), so the last tile of a range may be narrower
 constexpr int kTileBytes = kLmM * kLmK * 2;   // 16 KB: a hidden-state tile
-constexpr int kWTileBytes = kLmN * kLmK * 2;  // 8 KB: a weight tile
+constexpr int kWTileBytes = kLmN * kLmK * 2;  // 16 KB: a weight tile
 constexpr int kStageBytes2 = 2 * kTileBytes;
 constexpr int kLmThreads = 352;    // weight producer, MMA, 8 epilogue warps, hidden producer
 constexpr int kEpiThreads = 256;   // two epilogue warps a TMEM lane quarter
@@ -63,6 +65,9 @@ constexpr int kLmBuf = 128;
 // CTA's range in registers; the exact pass (run only for rows the fast pass could not
 // settle) keeps the best kLmCands in a shared-memory table.
 constexpr int kFastKeep = 16;
+// The hidden-state ring holds kAStages full (128-row) boxes; smaller batches fit more, up to
+// kAMaxStages boxes of 8 rows, and when every K block fits the states stay resident.
+constexpr int kAMaxStages = 64;
 template <int KL> struct LmVariant;
 // The weight tiles (from HBM) get a deeper ring than the hidden-state tiles (from L2).
 template <> struct LmVariant<kFastKeep> {
@@ -79,18 +84,19 @@ template <> struct LmVariant<kLmCands> {
 template <int KL>
 constexpr size_t lm_smem() {
   return 1024 + (size_t)LmVariant<KL>::kWStages * kWTileBytes +
-         (size_t)LmVariant<KL>::kAStages * kTileBytes + LmVariant<KL>::kTable + 256;
+         (size_t)LmVariant<KL>::kAStages * kTileBytes + LmVariant<KL>::kTable + 2048;
 }
 
 struct LmArgs {
   int32_t rows, vocab, hidden;
-  int32_t tiles_per_cta;
-  int32_t ntiles;
+  int32_t units;                 // vocabulary rows in units of kLmUnit
+  uint32_t a_bytes;              // bytes of a hidden-state box: round_up(rows, 8) x 128
   float2 *stats;                 // [rows][gridDim.x]
   unsigned long long *cands;     // [rows][gridDim.x][kLmCands]
   float *logits_out;             // tests only: [rows][vocab] fp32, or NULL
-  uint32_t *error;
-  const uint32_t *gate;          // non-NULL: run only when *gate != 0 (the exact pass)
+  uint32_t *error;               // set to `epoch` when a bounded wait runs out
+  const uint32_t *gate;          // non-NULL: run only when *gate == epoch (the exact pass)
+  uint32_t epoch;                // the call's tag: flags from earlier calls never match it
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
@@ -112,19 +118,24 @@ __device__ __forceinline__ unsigned long long now_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+__device__ __forceinline__ bool mb_try(uint64_t *b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(b)), "r"(parity)
+      : "memory");
+  return ok != 0u;
+}
+// The clock is read only once a first attempt has failed (reading it costs tens of ns).
 __device__ __forceinline__ bool mb_wait(uint64_t *b, uint32_t parity) {
+  if (mb_try(b, parity)) return true;
   const unsigned long long t0 = now_ns();
   for (uint32_t i = 0;; i++) {
     if ((i & 1023u) == 1023u && now_ns() - t0 > kWaitNs) return false;
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_addr(b)), "r"(parity)
-        : "memory");
-    if (ok) return true;
+    if (mb_try(b, parity)) return true;
   }
 }
 // 2-D TMA load of one box into this CTA's shared memory (coordinates: inner, outer).
@@ -149,14 +160,18 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   return d;
 }
 // Instruction descriptor of kind::f16: bf16 A and B, fp32 accumulate, both K-major.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kLmN >> 3) << 17) |
-                            ((uint32_t)(kLmM >> 4) << 24);
+// N (a multiple of 16, at most kLmN) is the tile's width.
+__device__ __forceinline__ uint32_t idesc_n(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(kLmM >> 4) << 24);
+}
 
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(kIdesc), "r"(acc)
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
@@ -228,9 +243,9 @@ __device__ __forceinline__ uint64_t merge_pending(unsigned long long *tab, int r
 template <int KL>
 __global__ void __launch_bounds__(kLmThreads, 1)
     lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__ CUtensorMap map_w,
-                  const __grid_constant__ LmArgs a) {
+                  const __grid_constant__ CUtensorMap map_w16, const __grid_constant__ LmArgs a) {
   constexpr int kW = LmVariant<KL>::kWStages, kA = LmVariant<KL>::kAStages;
-  if (a.gate && *a.gate == 0u) return;  // the exact pass, not needed this call
+  if (a.gate && *a.gate != a.epoch) return;  // the exact pass, not needed this call
   extern __shared__ unsigned char smem_dyn[];
   unsigned char *base = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~(uintptr_t)1023);
@@ -240,28 +255,37 @@ __global__ void __launch_bounds__(kLmThreads, 1)
       reinterpret_cast<unsigned long long *>(aring + kA * kTileBytes);
   uint64_t *bars = reinterpret_cast<uint64_t *>(aring + kA * kTileBytes + LmVariant<KL>::kTable);
   uint64_t *wfull = bars, *wempty = bars + kW;
-  uint64_t *afull = bars + 2 * kW, *aempty = afull + kA;
-  uint64_t *tfull = aempty + kA, *tempty = tfull + 2;
+  uint64_t *afull = bars + 2 * kW, *aempty = afull + kAMaxStages;
+  uint64_t *tfull = aempty + kAMaxStages, *tempty = tfull + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
   volatile uint32_t *err = tmem_slot + 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // This CTA's tiles: an even share of them, contiguous.
-  const int t0 = (int)(((int64_t)blockIdx.x * a.ntiles) / gridDim.x);
-  const int nt = (int)(((int64_t)(blockIdx.x + 1) * a.ntiles) / gridDim.x) - t0;
+  // This CTA's vocabulary rows: an even share of the 16-row units, contiguous, cut into
+  // tiles of kLmN rows (the last one narrower when the share is not a multiple of kLmN).
+  const int u0 = (int)(((int64_t)blockIdx.x * a.units) / gridDim.x);
+  const int nu = (int)(((int64_t)(blockIdx.x + 1) * a.units) / gridDim.x) - u0;
+  constexpr int kUpt = kLmN / kLmUnit;  // units a full tile
+  const int nt = (nu + kUpt - 1) / kUpt;
+  auto tile_v0 = [&](int t) { return (u0 + t * kUpt) * kLmUnit; };
+  auto tile_n = [&](int t) { return min(kUpt, nu - t * kUpt) * kLmUnit; };
   const int kb_n = a.hidden / kLmK;
+  // Hidden-state ring: as many boxes of the batch's rows as fit; resident when all K blocks do
+  // (loaded once, never released), otherwise refilled once the MMAs of a stage complete.
+  const int dA = min(kAMaxStages, (kA * kTileBytes) / (int)a.a_bytes);
+  const bool a_res = dA >= kb_n;
 
   if (tid == 0) {
     for (int s = 0; s < kW; s++) {
       mb_init(&wfull[s], 1);
       mb_init(&wempty[s], 1);
     }
-    for (int s = 0; s < kA; s++) {
+    for (int s = 0; s < kAMaxStages; s++) {
       mb_init(&afull[s], 1);
       mb_init(&aempty[s], 1);
     }
     for (int b = 0; b < 2; b++) {
       mb_init(&tfull[b], 1);
-      mb_init(&tempty[b], kEpiThreads);
+      mb_init(&tempty[b], kEpiThreads / 32);  // one arrival an epilogue warp
     }
     *err = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -283,24 +307,31 @@ __global__ void __launch_bounds__(kLmThreads, 1)
     // not hold up the other): warp 0 the weight tiles, warp 10 the hidden-state tiles ----
     if (lane == 0) {
       const bool wt = warp == 0;
-      const int depth = wt ? kW : kA;
+      const int depth = wt ? kW : dA;
       uint64_t *full = wt ? wfull : afull, *empty = wt ? wempty : aempty;
       unsigned char *ring = wt ? wring : aring;
-      const int bytes = wt ? kWTileBytes : kTileBytes;
+      const int slot = wt ? kWTileBytes : (int)a.a_bytes;
       int it = 0;
-      for (int t = 0; t < nt && !*err; t++) {
-        const int v0 = (t0 + t) * kLmN;
+      for (int t = 0; t < ((!wt && a_res) ? min(nt, 1) : nt) && !*err; t++) {
+        const int v0 = tile_v0(t), n = tile_n(t);
         for (int kb = 0; kb < kb_n; kb++, it++) {
           const int s = it % depth;
           if (it >= depth && !mb_wait(&empty[s], ((it / depth) - 1) & 1)) {
             *err = 1u;
             break;
           }
-          mb_arrive_expect(&full[s], (uint32_t)bytes);
-          if (wt)
-            tma_load_2d(ring + s * bytes, &map_w, kb * kLmK, v0, &full[s]);
-          else
-            tma_load_2d(ring + s * bytes, &map_h, kb * kLmK, 0, &full[s]);
+          unsigned char *dst = ring + s * slot;
+          if (!wt) {  // only the batch's rows (rounded up to 8) of the hidden states
+            mb_arrive_expect(&full[s], a.a_bytes);
+            tma_load_2d(dst, &map_h, kb * kLmK, 0, &full[s]);
+          } else if (n == kLmN) {
+            mb_arrive_expect(&full[s], (uint32_t)kWTileBytes);
+            tma_load_2d(dst, &map_w, kb * kLmK, v0, &full[s]);
+          } else {  // a narrow last tile: boxes of 16 rows, 2 KB apart (same swizzle phase)
+            mb_arrive_expect(&full[s], (uint32_t)(n * kLmK * 2));
+            for (int j = 0; j < n; j += kLmUnit)
+              tma_load_2d(dst + j * kLmK * 2, &map_w16, kb * kLmK, v0 + j, &full[s]);
+          }
         }
       }
       // Every issued load has landed before the CTA may exit (bounded).
@@ -318,20 +349,23 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(b * kLmN);
+        const uint32_t idesc = idesc_n(tile_n(t));
         for (int kb = 0; kb < kb_n; kb++, it++) {
-          const int sw = it % kW, sa = it % kA;
-          if (!mb_wait(&wfull[sw], (it / kW) & 1) || !mb_wait(&afull[sa], (it / kA) & 1)) {
+          const int sw = it % kW, sa = a_res ? kb : it % dA;
+          if (!mb_wait(&wfull[sw], (it / kW) & 1) ||
+              !mb_wait(&afull[sa], a_res ? 0u : (uint32_t)((it / dA) & 1))) {
             *err = 1u;
             break;
           }
           tc_fence_after();
           const uint32_t wa = smem_addr(wring + sw * kWTileBytes);
-          const uint32_t ha = smem_addr(aring + sa * kTileBytes);
+          const uint32_t ha = smem_addr(aring + sa * (int)a.a_bytes);
 #pragma unroll
           for (int kk = 0; kk < kLmK / 16; kk++)  // 16 bf16 = 32 bytes a step along K
-            mma_bf16(d, smem_desc(ha + 32 * kk), smem_desc(wa + 32 * kk), (kb | kk) != 0 ? 1u : 0u);
+            mma_bf16(d, smem_desc(ha + 32 * kk), smem_desc(wa + 32 * kk), idesc,
+                   (kb | kk) != 0 ? 1u : 0u);
           mma_commit(&wempty[sw]);  // the stages are free once these MMAs have read them
-          mma_commit(&aempty[sa]);
+          if (!a_res) mma_commit(&aempty[sa]);
         }
         if (*err) break;
         mma_commit(&tfull[b]);  // the tile's accumulator is complete
@@ -344,8 +378,8 @@ __global__ void __launch_bounds__(kLmThreads, 1)
     const int row = 32 * q + lane;
     const int et = tid - 64;        // epilogue thread
     const int hf = et >> 7;         // which half of the columns
-    const int parts = 2 * gridDim.x;
-    const int pi = 2 * blockIdx.x + hf;
+    const int parts = gridDim.x;  // one part a CTA: the two halves merge at the end
+    const int pi = blockIdx.x;
     const bool live = row < a.rows;
     float m = -3.40282347e38f, s = 0.f;
     constexpr float kLog2e = 1.44269504088896341f;
@@ -353,10 +387,17 @@ __global__ void __launch_bounds__(kLmThreads, 1)
       // The row's best kFastKeep composites of this CTA's range, sorted in registers;
       // a logit above the last one is inserted by one branch-free pass.
       float *stage_f = reinterpret_cast<float *>(cand);  // the variant's table: [32][256]
-      uint64_t best[kFastKeep];
+      // Values and vocabulary ids, best first. The scan visits ids in increasing order, so
+      // a value equal to a kept one ranks after it: the order is (value desc, id asc), the
+      // candidates' order, with value comparisons alone.
+      float bv[kFastKeep];
+      uint32_t bi[kFastKeep];
 #pragma unroll
-      for (int e = 0; e < kFastKeep; e++) best[e] = 0ull;
-      float thr_val = -3.40282347e38f;
+      for (int e = 0; e < kFastKeep; e++) {
+        bv[e] = -INFINITY;
+        bi[e] = 0xffffffffu;
+      }
+      float thr_val = -INFINITY;  // bv[kFastKeep - 1]: a logit must exceed it to enter
       for (int t = 0; t < nt; t++) {
         const int b = t & 1;
         if (!mb_wait(&tfull[b], (t >> 1) & 1)) {
@@ -364,40 +405,57 @@ __global__ void __launch_bounds__(kLmThreads, 1)
           break;
         }
         tc_fence_after();
-        const int v0 = (t0 + t) * kLmN;
+        const int v0 = tile_v0(t), vend = min(a.vocab, v0 + tile_n(t));
 #pragma unroll 1
         for (int c = hf * (kLmN / 64); c < (hf + 1) * (kLmN / 64); c++) {
+          const int vb = v0 + 32 * c;
+          if (vb >= vend) break;  // past a narrow tile's columns (warp-uniform)
           uint32_t r[32];
           tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kLmN + 32 * c), r);
-          const int vb = v0 + 32 * c;
-          const int nv = live ? min(32, a.vocab - vb) : 0;
+          const int nv = live ? min(32, vend - vb) : 0;
           if (nv <= 0) continue;
-          float cm = -3.40282347e38f;
+          if (nv < 32) {  // columns past the vocabulary count as -inf: no max, exp 0, no hit
 #pragma unroll
-          for (int j = 0; j < 32; j++)
-            if (j < nv) cm = fmaxf(cm, __uint_as_float(r[j]));
+            for (int j = 0; j < 32; j++)
+              if (j >= nv) r[j] = 0xff800000u;
+          }
+          // Reductions as trees (independent operations, not one dependent chain).
+          float tm[16];
+#pragma unroll
+          for (int j = 0; j < 16; j++) tm[j] = fmaxf(__uint_as_float(r[j]), __uint_as_float(r[j + 16]));
+#pragma unroll
+          for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+            for (int j = 0; j < w; j++) tm[j] = fmaxf(tm[j], tm[j + w]);
+          const float cm = tm[0];
           if (cm > m) {
             s *= ex2_fast((m - cm) * kLog2e);
             m = cm;
           }
           const float mL = m * kLog2e;
-          float acc = 0.f;
+          float te[16];
 #pragma unroll
-          for (int j = 0; j < 32; j++)
-            if (j < nv) acc += ex2_fast(fmaf(__uint_as_float(r[j]), kLog2e, -mL));
-          s += acc;
+          for (int j = 0; j < 16; j++)
+            te[j] = ex2_fast(fmaf(__uint_as_float(r[j]), kLog2e, -mL)) +
+                    ex2_fast(fmaf(__uint_as_float(r[j + 16]), kLog2e, -mL));
+#pragma unroll
+          for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+            for (int j = 0; j < w; j++) te[j] += te[j + w];
+          s += te[0];
           if (a.logits_out) {
 #pragma unroll
             for (int j = 0; j < 32; j++)
               if (j < nv) a.logits_out[(int64_t)row * a.vocab + vb + j] = __uint_as_float(r[j]);
           }
-          if (cm >= thr_val) {
-            // The logits at or above the threshold: a mask, then one compact loop over
+          if (cm > thr_val) {
+            // The logits above the threshold: a mask, then one compact loop over
             // them (staged in shared memory) for the insertions.
-            uint32_t hits = 0;
+            uint32_t hq[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
             for (int j = 0; j < 32; j++)
-              hits |= (j < nv && __uint_as_float(r[j]) >= thr_val) ? (1u << j) : 0u;
+              hq[j & 3] |= (__uint_as_float(r[j]) > thr_val) ? (1u << j) : 0u;
+            uint32_t hits = (hq[0] | hq[1]) | (hq[2] | hq[3]);
 #pragma unroll
             for (int j = 0; j < 32; j++)
               if ((hits >> j) & 1u) stage_f[j * kEpiThreads + et] = __uint_as_float(r[j]);
@@ -405,37 +463,89 @@ __global__ void __launch_bounds__(kLmThreads, 1)
               const int j = __ffs(hits) - 1;
               hits &= hits - 1;
               const float x = stage_f[j * kEpiThreads + et];
-              if (x >= thr_val) {
-                uint64_t v = ((uint64_t)lm_key(x) << 32) | (uint64_t)(~(uint32_t)(vb + j));
-                if (v > best[kFastKeep - 1]) {
+              if (x > thr_val) {
+                // Insertion with every slot computed from the old list at once (no chain
+                // of dependent compare-and-swaps): slot e keeps its value if that is >= x,
+                // takes x if slot e-1 keeps its own, else shifts down slot e-1's.
+                const uint32_t id = (uint32_t)(vb + j);
+                bool g[kFastKeep];
 #pragma unroll
-                  for (int e = 0; e < kFastKeep; e++) {
-                    const uint64_t hi = best[e] > v ? best[e] : v;
-                    v = best[e] > v ? v : best[e];
-                    best[e] = hi;
-                  }
-                  if (best[kFastKeep - 1] != 0ull) {
-                    const uint32_t kk = (uint32_t)(best[kFastKeep - 1] >> 32);
-                    thr_val = __uint_as_float(kk ^ ((kk >> 31) ? 0x80000000u : 0xffffffffu));
-                  }
+                for (int e = 0; e < kFastKeep; e++) g[e] = bv[e] >= x;
+#pragma unroll
+                for (int e = kFastKeep - 1; e > 0; e--) {
+                  bv[e] = g[e] ? bv[e] : (g[e - 1] ? x : bv[e - 1]);
+                  bi[e] = g[e] ? bi[e] : (g[e - 1] ? id : bi[e - 1]);
                 }
+                bv[0] = g[0] ? bv[0] : x;
+                bi[0] = g[0] ? bi[0] : id;
+                thr_val = bv[kFastKeep - 1];
               }
             }
           }
         }
         tc_fence_before();
-        mb_arrive(&tempty[b]);  // the accumulator may be overwritten
+        __syncwarp();
+        if (lane == 0) mb_arrive(&tempty[b]);  // the accumulator may be overwritten
       }
-      if (live) {
+      // The second half's threads hand their statistics and lists over through shared
+      // memory (the staging area, free now: a barrier of the 256 epilogue threads first);
+      // the first half's merge them, the lists by (value desc, id asc).
+      float2 *xs = reinterpret_cast<float2 *>(stage_f);             // [kLmM]
+      float *xv = stage_f + 2 * kLmM;                                // [kFastKeep][kLmM]
+      uint32_t *xi = reinterpret_cast<uint32_t *>(xv + kFastKeep * kLmM);
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+      if (hf == 1) {
+        xs[row] = make_float2(m, s);
+#pragma unroll
+        for (int e = 0; e < kFastKeep; e++) {
+          xv[e * kLmM + row] = bv[e];
+          xi[e * kLmM + row] = bi[e];
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+      if (hf == 0 && live) {
+        const float2 o = xs[row];
+        const float mm = fmaxf(m, o.x);
+        s = s * ex2_fast((m - mm) * kLog2e) + o.y * ex2_fast((o.x - mm) * kLog2e);
+        m = mm;
+        // Two-pointer merge: this thread's list pops from the front of its registers (a
+        // shift), the other half's list is read from shared memory.
+        float ov[kFastKeep];
+        uint32_t oi[kFastKeep];
+        int jb = 0;
+        float x = xv[row];
+        uint32_t id = xi[row];
+#pragma unroll
+        for (int e = 0; e < kFastKeep; e++) {
+          const bool take_a = bv[0] > x || (bv[0] == x && bi[0] < id);
+          ov[e] = take_a ? bv[0] : x;
+          oi[e] = take_a ? bi[0] : id;
+          if (take_a) {
+#pragma unroll
+            for (int f = 0; f < kFastKeep - 1; f++) {
+              bv[f] = bv[f + 1];
+              bi[f] = bi[f + 1];
+            }
+            bv[kFastKeep - 1] = -INFINITY;
+            bi[kFastKeep - 1] = 0xffffffffu;
+          } else {
+            jb++;
+            x = jb < kFastKeep ? xv[jb * kLmM + row] : -INFINITY;
+            id = jb < kFastKeep ? xi[jb * kLmM + row] : 0xffffffffu;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < kFastKeep; e++) {
+          bv[e] = ov[e];
+          bi[e] = oi[e];
+        }
         a.stats[(int64_t)row * parts + pi] = make_float2(m, s);
         unsigned long long *dst = a.cands + ((int64_t)row * parts + pi) * kLmCands;
 #pragma unroll
-        for (int e = 0; e < kLmCands; e++) {
-          const uint64_t c = e < kFastKeep ? best[e < kFastKeep ? e : 0] : 0ull;
-          const uint32_t kk = (uint32_t)(c >> 32);
-          const uint32_t raw = kk ^ ((kk >> 31) ? 0x80000000u : 0xffffffffu);
-          dst[e] = c != 0ull ? (((uint64_t)raw << 32) | (uint64_t)(~(uint32_t)c)) : 0xffffffffull;
-        }
+        for (int e = 0; e < kFastKeep; e++)  // the merge reads the first kFastKeep entries
+          dst[e] = bi[e] != 0xffffffffu
+                       ? (((uint64_t)__float_as_uint(bv[e]) << 32) | (uint64_t)bi[e])
+                       : 0xffffffffull;
       }
     } else {
     int pend = 0;                     // this row's pending composites
@@ -473,13 +583,13 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         break;
       }
       tc_fence_after();
-      const int v0 = (t0 + t) * kLmN;
+      const int v0 = tile_v0(t), vend = min(a.vocab, v0 + tile_n(t));
 #pragma unroll 1
       for (int c = 0; c < (hf == 0 ? kLmN / 32 : 0); c++) {
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kLmN + 32 * c), r);
         const int vb = v0 + 32 * c;
-        const int nv = live ? min(32, a.vocab - vb) : 0;
+        const int nv = live ? min(32, vend - vb) : 0;
         if (nv > 0) {
           float cm = -3.40282347e38f;
 #pragma unroll
@@ -514,15 +624,16 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         merge_rows(32);  // keeps every row's pending list below 64
       }
       tc_fence_before();
-      mb_arrive(&tempty[b]);  // the accumulator may be overwritten
+      __syncwarp();
+      if (lane == 0) mb_arrive(&tempty[b]);  // the accumulator may be overwritten
     }
     if (hf == 0) merge_rows(1);  // the last pending composites of every row
-    if (live) {
+    if (live && hf == 0) {
       a.stats[(int64_t)row * parts + pi] = make_float2(m, s);
       unsigned long long *dst = a.cands + ((int64_t)row * parts + pi) * kLmCands;
       for (int e = 0; e < kLmCands; e++) {
-        const uint64_t c = hf == 0 ? cand[cidx(e, row)] : 0ull;  // composite: raw value bits from the key (+0 for a
-                                           // -0 logit, the one value the key folds)
+        // composite: raw value bits from the key (+0 for a -0 logit, the one value the key folds)
+        const uint64_t c = cand[cidx(e, row)];
         const uint32_t kk = (uint32_t)(c >> 32);
         const uint32_t raw = kk ^ ((kk >> 31) ? 0x80000000u : 0xffffffffu);
         dst[e] = c != 0ull ? (((uint64_t)raw << 32) | (uint64_t)(~(uint32_t)c)) : 0xffffffffull;
@@ -532,7 +643,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (*err && tid == 0) atomicOr(a.error, 1u);
+  if (*err && tid == 0) *a.error = a.epoch;
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
@@ -589,23 +700,25 @@ int lfail(int status, const char *fmt, ...) {
 }  // namespace tabby
 
 struct tabby_lmhead {
-  void *hidden_pad;        // [kLmM][hidden] bf16: the call's rows are copied in, so no TMA
-                           // box of the hidden states is out of bounds (those are slow);
-                           // rows past the batch hold stale values the epilogue never reads
-  CUtensorMap map_h;       // over hidden_pad
-  CUtensorMap map_w;       // over the last weight pointer
+  CUtensorMap map_h;       // over the last hidden-state pointer and batch: boxes of the
+                           // batch's rows rounded up to 8 (the rest zero-filled by TMA)
+  const void *map_h_ptr;
+  int32_t map_h_rows;
+  uint32_t epoch;          // the last call's tag (never 0: the flags start zeroed)
+  CUtensorMap map_w;       // over the last weight pointer: boxes of 128 rows
+  CUtensorMap map_w16;     // the same, boxes of 16 rows (the narrow last tile of a range)
   const void *map_w_ptr;
   int32_t device;
   int32_t max_rows;
   int32_t vocab;
   int32_t hidden;
   int32_t grid;
-  int32_t tiles_per_cta;
-  int32_t ntiles;
+  int32_t units;
   float2 *stats;
   unsigned long long *cands;
-  uint32_t *error;  // [0] a bounded wait ran out, [1] some row needs the exact pass
-  uint32_t *flags;  // [max_rows] rows the exact pass recomputes
+  uint32_t *error;  // [0] = the epoch of a call whose bounded wait ran out, [1] = the
+                    // epoch of a call with a row for the exact pass
+  uint32_t *flags;  // [max_rows] = the epoch of a call whose exact pass recomputes the row
 };
 
 extern "C" {
@@ -639,17 +752,15 @@ int tabby_lmhead_create(int32_t device, int32_t max_rows, int32_t vocab, int32_t
   h->max_rows = max_rows;
   h->vocab = vocab;
   h->hidden = hidden;
-  h->ntiles = (vocab + kLmN - 1) / kLmN;
-  h->grid = std::min(h->ntiles, std::max(sms, 1));  // every SM, an even share of tiles each
-  h->tiles_per_cta = (h->ntiles + h->grid - 1) / h->grid;
-  const size_t nst = (size_t)max_rows * h->grid * 2;  // two parts a CTA
+  h->units = (vocab + kLmUnit - 1) / kLmUnit;
+  // Every SM, an even share of the 16-row units each (at least a full tile's worth).
+  h->grid = std::min((h->units + kLmN / kLmUnit - 1) / (kLmN / kLmUnit), std::max(sms, 1));
+  const size_t nst = (size_t)max_rows * h->grid;  // one part a CTA
   if ((err = cudaMalloc(&h->stats, nst * sizeof(float2))) != cudaSuccess ||
       (err = cudaMalloc(&h->cands, nst * kLmCands * 8)) != cudaSuccess ||
       (err = cudaMalloc(&h->error, 16)) != cudaSuccess ||
       (err = cudaMemset(h->error, 0, 16)) != cudaSuccess ||
       (err = cudaMalloc(&h->flags, (size_t)max_rows * 4)) != cudaSuccess ||
-      (err = cudaMalloc(&h->hidden_pad, (size_t)kLmM * hidden * 2)) != cudaSuccess ||
-      (err = cudaMemset(h->hidden_pad, 0, (size_t)kLmM * hidden * 2)) != cudaSuccess ||
       (err = cudaMemset(h->flags, 0, (size_t)max_rows * 4)) != cudaSuccess ||
       (err = cudaFuncSetAttribute(lmhead_kernel<kFastKeep>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -658,18 +769,12 @@ int tabby_lmhead_create(int32_t device, int32_t max_rows, int32_t vocab, int32_t
                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)lm_smem<kLmCands>())) != cudaSuccess) {
     if (h->flags) cudaFree(h->flags);
-    if (h->hidden_pad) cudaFree(h->hidden_pad);
     if (h->stats) cudaFree(h->stats);
     if (h->cands) cudaFree(h->cands);
     if (h->error) cudaFree(h->error);
     delete h;
     if (cur != device) cudaSetDevice(cur);
     return lfail(TABBY_ENOMEM, "LM-head set-up failed: %s", cudaGetErrorString(err));
-  }
-  if (!make_map(&h->map_h, h->hidden_pad, (uint64_t)hidden, (uint64_t)kLmM, (uint32_t)kLmM)) {
-    if (cur != device) cudaSetDevice(cur);
-    tabby_lmhead_destroy(h);
-    return lfail(TABBY_ECUDA, "cuTensorMapEncodeTiled failed");
   }
   if (cur != device) cudaSetDevice(cur);
   *out = h;
@@ -685,7 +790,6 @@ int tabby_lmhead_destroy(tabby_lmhead *h) {
   cudaFree(h->cands);
   cudaFree(h->error);
   cudaFree(h->flags);
-  cudaFree(h->hidden_pad);
   if (cur != h->device) cudaSetDevice(cur);
   delete h;
   return TABBY_OK;
@@ -712,38 +816,46 @@ int tabby_lmhead_sample_async(tabby_lmhead *h, const void *d_hidden, const void 
   if (err == cudaSuccess && cur != h->device) err = cudaSetDevice(h->device);
   if (err != cudaSuccess) return lfail(TABBY_ECUDA, "cudaSetDevice: %s", cudaGetErrorString(err));
   if (d_weight != h->map_w_ptr) {
-    if (!make_map(&h->map_w, d_weight, (uint64_t)h->hidden, (uint64_t)h->vocab, (uint32_t)kLmN)) {
+    if (!make_map(&h->map_w, d_weight, (uint64_t)h->hidden, (uint64_t)h->vocab, (uint32_t)kLmN) ||
+        !make_map(&h->map_w16, d_weight, (uint64_t)h->hidden, (uint64_t)h->vocab,
+                  (uint32_t)kLmUnit)) {
+      h->map_w_ptr = nullptr;
       if (cur != h->device) cudaSetDevice(cur);
       return lfail(TABBY_ECUDA, "cuTensorMapEncodeTiled failed");
     }
     h->map_w_ptr = d_weight;
   }
-  const CUtensorMap &mh = h->map_h, &mw = h->map_w;
-  cudaStream_t q = (cudaStream_t)stream;
-  err = cudaMemcpyAsync(h->hidden_pad, d_hidden, (size_t)rows * h->hidden * 2,
-                        cudaMemcpyDeviceToDevice, q);
-  if (err != cudaSuccess) {
-    if (cur != h->device) cudaSetDevice(cur);
-    return lfail(TABBY_ECUDA, "copy of the hidden states: %s", cudaGetErrorString(err));
+  const int mb = (rows + 7) / 8;  // hidden-state boxes of 8 * mb rows
+  if (d_hidden != h->map_h_ptr || rows != h->map_h_rows) {
+    if (!make_map(&h->map_h, d_hidden, (uint64_t)h->hidden, (uint64_t)rows, (uint32_t)(8 * mb))) {
+      h->map_h_ptr = nullptr;
+      if (cur != h->device) cudaSetDevice(cur);
+      return lfail(TABBY_ECUDA, "cuTensorMapEncodeTiled failed");
+    }
+    h->map_h_ptr = d_hidden;
+    h->map_h_rows = rows;
   }
+  if (++h->epoch == 0u) h->epoch = 1u;
+  const CUtensorMap &mh = h->map_h, &mw = h->map_w, &mw16 = h->map_w16;
+  cudaStream_t q = (cudaStream_t)stream;
   LmArgs a;
   a.rows = rows;
   a.vocab = h->vocab;
   a.hidden = h->hidden;
-  a.tiles_per_cta = h->tiles_per_cta;
-  a.ntiles = h->ntiles;
+  a.units = h->units;
+  a.a_bytes = (uint32_t)(8 * mb * kLmK * 2);
   a.stats = h->stats;
   a.cands = h->cands;
   a.logits_out = d_logits_out;
   a.error = h->error;
+  a.epoch = h->epoch;
   // The fast pass and its merge; then the exact pass and its merge, which return at once
   // unless the fast merge flagged a row (a part's 16th best above the row's k-th best).
   a.gate = nullptr;
-  if (err == cudaSuccess) err = cudaMemsetAsync(h->error, 0, 8, q);
   LmheadMergeLaunch l;
   l.stats = h->stats;
   l.cands = h->cands;
-  l.parts = 2 * h->grid;
+  l.parts = h->grid;
   l.rows = rows;
   l.vocab = h->vocab;
   l.params = d_params;
@@ -755,8 +867,9 @@ int tabby_lmhead_sample_async(tabby_lmhead *h, const void *d_hidden, const void 
   l.error = h->error;
   l.row_flag = h->flags;
   l.any_flag = h->error + 1;
+  l.epoch = h->epoch;
   if (err == cudaSuccess) {
-    lmhead_kernel<kFastKeep><<<h->grid, kLmThreads, lm_smem<kFastKeep>(), q>>>(mh, mw, a);
+    lmhead_kernel<kFastKeep><<<h->grid, kLmThreads, lm_smem<kFastKeep>(), q>>>(mh, mw, mw16, a);
     err = cudaGetLastError();
   }
   if (err == cudaSuccess) {
@@ -765,7 +878,7 @@ int tabby_lmhead_sample_async(tabby_lmhead *h, const void *d_hidden, const void 
   }
   if (err == cudaSuccess) {
     a.gate = h->error + 1;
-    lmhead_kernel<kLmCands><<<h->grid, kLmThreads, lm_smem<kLmCands>(), q>>>(mh, mw, a);
+    lmhead_kernel<kLmCands><<<h->grid, kLmThreads, lm_smem<kLmCands>(), q>>>(mh, mw, mw16, a);
     err = cudaGetLastError();
   }
   if (err == cudaSuccess) {

@@ -68,15 +68,16 @@ struct LmheadMergeLaunch {
   int32_t *topk_ids = nullptr;
   float *topk_values = nullptr;
   int32_t topk_ld = 0;
-  const uint32_t *error = nullptr;  // non-zero: a bounded wait of the fused kernel ran out
+  const uint32_t *error = nullptr;  // == epoch: a bounded wait of the fused kernel ran out
   // keep < kLmCands (the fast pass): each part kept only its best `keep`; the merge checks
   // that no part's last kept candidate lies above the row's k-th best and, where one does,
-  // sets row_flag[row] and *any_flag so the exact pass recomputes the row. keep ==
-  // kLmCands with row_flag set (the exact pass's merge): only flagged rows are finished,
-  // and their flags cleared.
+  // sets row_flag[row] and *any_flag to the epoch so the exact pass recomputes the row.
+  // keep == kLmCands with row_flag set (the exact pass's merge): only the rows flagged with
+  // this epoch are finished.
   int32_t keep = kLmCands;
   uint32_t *row_flag = nullptr;
   uint32_t *any_flag = nullptr;
+  uint32_t epoch = 0;  // the call's tag: error, row_flag and any_flag hold the epoch they refer to
 };
 cudaError_t launch_lmhead_merge(const LmheadMergeLaunch &l, cudaStream_t stream);
 

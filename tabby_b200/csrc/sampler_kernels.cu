@@ -2285,28 +2285,71 @@ cudaError_t launch_merge(const MergeLaunch &l, cudaStream_t stream) {
 // (k <= kLmCands, the reference's MAX_TOP_K) of the CTAs' best logits by (value desc,
 // index asc), then sampleFromTopK exactly as the row pass does.
 // ------------------------------------------------------------------------------------
+__host__ __device__ __forceinline__ int lm_merge_cap(int parts, int keep) {
+  return max(kFinishCap, parts * min(max(keep, 1), kLmCands));
+}
+
 __global__ void __launch_bounds__(kThreads) lmhead_merge_kernel(LmheadMergeLaunch a) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ Shared sh_s;
   Shared *sh = &sh_s;
+  // Room for every entry the parts wrote (at least kFinishCap), then the histogram.
+  const int cap = lm_merge_cap(a.parts, a.keep);
   uint64_t *cand = reinterpret_cast<uint64_t *>(smem_raw);
-  uint32_t *hist = reinterpret_cast<uint32_t *>(cand + kFinishCap);
+  uint32_t *hist = reinterpret_cast<uint32_t *>(cand + cap);
   const int row = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool exact_pass = a.keep >= kLmCands && a.row_flag != nullptr;
-  if (exact_pass && __ldcg(a.row_flag + row) == 0u) return;  // settled by the fast pass
+  if (exact_pass && __ldcg(a.row_flag + row) != a.epoch) return;  // settled by the fast pass
   const tabby_sampling_params prm = a.params[row];
   uint32_t pflags = (isnan(prm.temperature) || isnan(prm.top_p)) ? kFlagBadParams : 0u;
   const int k = min(pool_rule(prm.temperature, prm.top_k, kLmCands), a.vocab);
   double uni = (!a.rng_state && a.uniforms) ? a.uniforms[row] : 0.0;
-  // (max, sum-exp) of the CTAs, merged in CTA order.
+  // The parts' candidates: raw value bits << 32 | id, each part's list sorted best first;
+  // the first batch of loads is issued before anything waits on memory.
+  const int total = a.parts * kLmCands;
+  const unsigned long long *rc = a.cands + (int64_t)row * total;
+  const int keep = min(a.keep, kLmCands);
+  const int nent = a.parts * keep;  // the entries the parts wrote
+  constexpr int kBatch = 10;        // a thread's loads in flight at once
+  unsigned long long w[kBatch];
+  auto load_batch = [&](int base) {
+#pragma unroll
+    for (int u = 0; u < kBatch; u++) {
+      const int i = base + u * kThreads + tid;
+      w[u] = i < nent ? __ldcg(rc + (i / keep) * kLmCands + i % keep) : 0xffffffffull;
+    }
+  };
+  load_batch(0);
+  auto comp_of = [](unsigned long long e) -> uint64_t {
+    return (uint32_t)e == 0xffffffffu
+               ? 0ull
+               : composite(key_of(__uint_as_float((uint32_t)(e >> 32))), (uint32_t)e);
+  };
+  // Each part's best entry, and the (max, sum-exp) of the parts, merged in part order.
+  uint64_t *heads = reinterpret_cast<uint64_t *>(hist);  // [parts]: free until the top-k
   float2 st = make_float2(-3.40282347e38f, 0.f);
-  if (tid < a.parts) st = a.stats[(int64_t)row * a.parts + tid];
+  uint64_t hv = 0ull;
+  if (tid < a.parts) {
+    st = a.stats[(int64_t)row * a.parts + tid];
+    hv = comp_of(__ldcg(rc + (int64_t)tid * kLmCands));
+    heads[tid] = hv;
+  }
   float bm = st.x;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
   if (lane == 0) sh->red_f[warp] = bm;
-  if (tid == 0) sh->count = 0;
+  if (tid == 0) {
+    sh->count = 0;
+    sh->tau = 0ull;
+  }
   __syncthreads();
+  // A lower bound on the row's k-th best: the k-th best of the parts' heads (k parts hold a
+  // candidate at or above it), found by counting; nothing below it can be in the top k.
+  if (hv != 0ull && a.parts >= k && k > 0) {
+    int above = 0;
+    for (int q = 0; q < a.parts; q++) above += heads[q] > hv ? 1 : 0;
+    if (above == k - 1) sh->tau = hv;
+  }
   float M = lane < kWarps ? sh->red_f[lane] : -3.40282347e38f;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
@@ -2319,16 +2362,23 @@ __global__ void __launch_bounds__(kThreads) lmhead_merge_kernel(LmheadMergeLaunc
     sh->red_f2[warp] = contrib;
     sh->red_u[warp] = wbad ? 1u : 0u;
   }
-  // The CTAs' candidates as composites (order-preserving key, inverted index).
-  const int total = a.parts * kLmCands;
-  const unsigned long long *rc = a.cands + (int64_t)row * total;
-  const int keep = min(a.keep, kLmCands);
-  for (int i = tid; i < a.parts * keep; i += kThreads) {  // the entries each part used
-    const unsigned long long w = rc[(i / keep) * kLmCands + i % keep];
-    const uint32_t idx = (uint32_t)w;
-    if (idx != 0xffffffffu) {
-      const uint32_t slot = atomicAdd(&sh->count, 1u);
-      if (slot < (uint32_t)kFinishCap) cand[slot] = composite(key_of(__uint_as_float((uint32_t)(w >> 32))), idx);
+  __syncthreads();
+  // The candidates at or above the bound as composites (order-preserving key, inverted
+  // id); a warp appends its batch with one shared-memory atomic.
+  const uint64_t tau = sh->tau;
+  for (int base = 0; base < nent; base += kBatch * kThreads) {
+    if (base > 0) load_batch(base);
+#pragma unroll
+    for (int u = 0; u < kBatch; u++) {
+      const uint64_t c = comp_of(w[u]);
+      const bool valid = c != 0ull && c >= tau;
+      const uint32_t ball = __ballot_sync(0xffffffffu, valid);
+      if (ball == 0u) continue;
+      uint32_t first = 0;
+      if (lane == 0) first = atomicAdd(&sh->count, (uint32_t)__popc(ball));
+      first = __shfl_sync(0xffffffffu, first, 0);
+      const uint32_t slot = first + (uint32_t)__popc(ball & ((1u << lane) - 1u));
+      if (valid && slot < (uint32_t)cap) cand[slot] = c;
     }
   }
   __syncthreads();
@@ -2337,10 +2387,10 @@ __global__ void __launch_bounds__(kThreads) lmhead_merge_kernel(LmheadMergeLaunc
   for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
   const bool bad = __any_sync(0xffffffffu, lane < kWarps && sh->red_u[lane] != 0u) ||
                    !(S <= 3.40282347e38f) || !(M <= 3.40282347e38f);
-  const int n = min((int)sh->count, kFinishCap);
-  const bool timed_out = a.error && *a.error != 0u;
+  const int n = min((int)sh->count, cap);
+  const bool timed_out = a.error && *a.error == a.epoch;
   int kk = 0;
-  if (!timed_out && !bad && k > 0) kk = top_sorted(cand, n, k, kFinishCap, hist, sh);
+  if (!timed_out && !bad && k > 0) kk = top_sorted(cand, n, k, cap, hist, sh);
   else __syncthreads();
   if (a.keep < kLmCands && a.row_flag) {
     // The fast pass: a part whose last kept candidate lies above the k-th best may have
@@ -2355,13 +2405,12 @@ __global__ void __launch_bounds__(kThreads) lmhead_merge_kernel(LmheadMergeLaunc
     }
     if (__syncthreads_or(unsettled ? 1 : 0)) {
       if (tid == 0) {
-        a.row_flag[row] = 1u;
-        atomicOr(a.any_flag, 1u);
+        a.row_flag[row] = a.epoch;
+        *a.any_flag = a.epoch;
       }
       return;  // the exact pass writes this row
     }
   }
-  if (exact_pass && tid == 0) a.row_flag[row] = 0u;
   const uint32_t status = timed_out ? (uint32_t)TABBY_ETIMEOUT
                           : bad     ? (uint32_t)TABBY_EINPUT
                           : pflags  ? (uint32_t)TABBY_EINVAL
@@ -2376,12 +2425,14 @@ __global__ void __launch_bounds__(kThreads) lmhead_merge_kernel(LmheadMergeLaunc
     const uint64_t c = e ? c1 : c0;
     if (i < kk && (uint32_t)(c >> 32) == 0x80000000u) {
       const uint32_t want = ~(uint32_t)c;
-      for (int j = 0; j < total; j++)
-        if ((uint32_t)rc[j] == want) {
-          if (e) x1 = __uint_as_float((uint32_t)(rc[j] >> 32));
-          else x0 = __uint_as_float((uint32_t)(rc[j] >> 32));
+      for (int i2 = 0; i2 < a.parts * keep; i2++) {  // the entries the parts wrote
+        const unsigned long long w = rc[(i2 / keep) * kLmCands + i2 % keep];
+        if ((uint32_t)w == want) {
+          if (e) x1 = __uint_as_float((uint32_t)(w >> 32));
+          else x0 = __uint_as_float((uint32_t)(w >> 32));
           break;
         }
+      }
     }
   }
   const float max_logit = kk > 0 ? __shfl_sync(0xffffffffu, x0, 0) : M;
@@ -2406,18 +2457,23 @@ __global__ void __launch_bounds__(kThreads) lmhead_merge_kernel(LmheadMergeLaunc
 cudaError_t launch_lmhead_merge(const LmheadMergeLaunch &l, cudaStream_t stream) {
   if (l.rows == 0) return cudaSuccess;
   if (l.parts < 1 || l.parts > kThreads) return cudaErrorInvalidValue;
-  const size_t smem = (size_t)kFinishCap * 8 + (size_t)kBins * 4;
-  static std::once_flag once[64];
+  const size_t smem = (size_t)lm_merge_cap(l.parts, l.keep) * 8 + (size_t)kBins * 4;
+  // The attribute is raised per device to the largest size launched so far.
+  static std::mutex mu;
+  static size_t set_to[64];
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  cudaError_t set = cudaSuccess;
-  std::call_once(once[dev], [&]() {
-    set = cudaFuncSetAttribute(lmhead_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)smem);
-  });
-  if (set != cudaSuccess) return set;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    if (set_to[dev] < smem) {
+      err = cudaFuncSetAttribute(lmhead_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem);
+      if (err != cudaSuccess) return err;
+      set_to[dev] = smem;
+    }
+  }
   lmhead_merge_kernel<<<l.rows, kThreads, smem, stream>>>(l);
   return cudaGetLastError();
 }

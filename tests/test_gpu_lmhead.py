@@ -78,3 +78,37 @@ def test_lmhead_matches_fp32_gemm_and_oracle(oracle, rows, vocab, hidden):
     out2, ids2, _, _ = _run(torch, h, w, p, u, False)
     np.testing.assert_array_equal(out2["id"], out["id"])
     np.testing.assert_array_equal(ids2, ids)
+
+
+@pytest.mark.parametrize("rows,vocab,hidden", [(4, 151936, 896), (64, 151936, 896)])
+def test_lmhead_concentrated_top_runs_exact_pass(oracle, rows, vocab, hidden):
+    """Every row's best logits lie in one CTA's columns (so the fast pass's 16 a part cannot
+    settle the row and the exact pass recomputes it), with tied logits among them."""
+    if not gpu_available():
+        pytest.skip("no CUDA device")
+    import torch
+
+    g = torch.Generator().manual_seed(rows * 7 + 1)
+    h = torch.randn(rows, hidden, generator=g)
+    w = torch.randn(vocab, hidden, generator=g) * (3.0 / hidden ** 0.5)
+    for r in range(rows):
+        base = 5000 + 1024 * r
+        w[base:base + 100] = h[r] * (0.02 + 0.01 * torch.rand(100, 1, generator=g))
+        w[base + 100:base + 110] = w[base]  # ties with id base: the lower id ranks first
+    h = h.to(torch.bfloat16).cuda()
+    w = w.to(torch.bfloat16).cuda()
+    rng = np.random.default_rng(rows)
+    p = oracle.make_params(rng.uniform(0.3, 1.5, rows), rng.uniform(0.5, 1.0, rows),
+                           rng.choice([0, 40, 64], rows), rows)
+    u = rng.random(rows)
+    out, ids, vals, logits = _run(torch, h, w, p, u, True)
+    ref, rids, rvals = oracle.sample_rows(logits, p, u, CAP)
+    for r in range(rows):
+        o, e = out[r], ref[r]
+        assert o["status"] == 0, (r, o["status"])
+        k = int(e["pool_size"])
+        assert int(o["pool_size"]) == k
+        np.testing.assert_array_equal(ids[r, :k], rids[r, :k])
+        np.testing.assert_array_equal(vals[r, :k].view(np.uint32), rvals[r, :k].view(np.uint32))
+        assert int(o["id"]) == int(e["id"]), r
+        assert abs(o["probability"] - e["probability"]) <= REL * e["probability"]
