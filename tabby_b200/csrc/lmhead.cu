@@ -249,13 +249,13 @@ __global__ void __launch_bounds__(kLmThreads, 1)
   extern __shared__ unsigned char smem_dyn[];
   unsigned char *base = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~(uintptr_t)1023);
-  unsigned char *wring = base;                      // [kW] weight tiles
-  unsigned char *aring = base + kW * kWTileBytes;   // [kA] hidden-state tiles
+  constexpr int kRing = kW * kWTileBytes + kA * kTileBytes;  // both rings' bytes
+  constexpr int kWMax = kRing / kWTileBytes;
   unsigned long long *cand =
-      reinterpret_cast<unsigned long long *>(aring + kA * kTileBytes);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(aring + kA * kTileBytes + LmVariant<KL>::kTable);
-  uint64_t *wfull = bars, *wempty = bars + kW;
-  uint64_t *afull = bars + 2 * kW, *aempty = afull + kAMaxStages;
+      reinterpret_cast<unsigned long long *>(base + kRing);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(base + kRing + LmVariant<KL>::kTable);
+  uint64_t *wfull = bars, *wempty = bars + kWMax;
+  uint64_t *afull = bars + 2 * kWMax, *aempty = afull + kAMaxStages;
   uint64_t *tfull = aempty + kAMaxStages, *tempty = tfull + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
   volatile uint32_t *err = tmem_slot + 1;
@@ -269,13 +269,19 @@ __global__ void __launch_bounds__(kLmThreads, 1)
   auto tile_v0 = [&](int t) { return (u0 + t * kUpt) * kLmUnit; };
   auto tile_n = [&](int t) { return min(kUpt, nu - t * kUpt) * kLmUnit; };
   const int kb_n = a.hidden / kLmK;
-  // Hidden-state ring: as many boxes of the batch's rows as fit; resident when all K blocks do
-  // (loaded once, never released), otherwise refilled once the MMAs of a stage complete.
-  const int dA = min(kAMaxStages, (kA * kTileBytes) / (int)a.a_bytes);
-  const bool a_res = dA >= kb_n;
+  // The rings share kRing bytes. When every K block of the batch's hidden states fits
+  // beside kW weight stages, the states stay resident (loaded once, never released) and
+  // the weight ring takes the rest; otherwise the hidden-state ring holds as many boxes as
+  // kA full ones would, refilled once the MMAs of a stage complete.
+  const int a_all = kb_n * (int)a.a_bytes;
+  const bool a_res = a_all <= kRing - kW * kWTileBytes && kb_n <= kAMaxStages;
+  const int dA = a_res ? kb_n : min(kAMaxStages, (kA * kTileBytes) / (int)a.a_bytes);
+  const int dW = a_res ? (kRing - a_all) / kWTileBytes : kW;
+  unsigned char *wring = base;                      // [dW] weight tiles
+  unsigned char *aring = base + dW * kWTileBytes;   // [dA] hidden-state boxes
 
   if (tid == 0) {
-    for (int s = 0; s < kW; s++) {
+    for (int s = 0; s < kWMax; s++) {
       mb_init(&wfull[s], 1);
       mb_init(&wempty[s], 1);
     }
@@ -307,16 +313,16 @@ __global__ void __launch_bounds__(kLmThreads, 1)
     // not hold up the other): warp 0 the weight tiles, warp 10 the hidden-state tiles ----
     if (lane == 0) {
       const bool wt = warp == 0;
-      const int depth = wt ? kW : dA;
+      const int depth = wt ? dW : dA;
       uint64_t *full = wt ? wfull : afull, *empty = wt ? wempty : aempty;
       unsigned char *ring = wt ? wring : aring;
       const int slot = wt ? kWTileBytes : (int)a.a_bytes;
-      int it = 0;
+      int it = 0, s = 0;
+      uint32_t ph = 0;  // the ring's round parity; a fresh barrier passes a wait on parity 1
       for (int t = 0; t < ((!wt && a_res) ? min(nt, 1) : nt) && !*err; t++) {
         const int v0 = tile_v0(t), n = tile_n(t);
         for (int kb = 0; kb < kb_n; kb++, it++) {
-          const int s = it % depth;
-          if (it >= depth && !mb_wait(&empty[s], ((it / depth) - 1) & 1)) {
+          if (!mb_wait(&empty[s], ph ^ 1u)) {
             *err = 1u;
             break;
           }
@@ -332,15 +338,28 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             for (int j = 0; j < n; j += kLmUnit)
               tma_load_2d(dst + j * kLmK * 2, &map_w16, kb * kLmK, v0 + j, &full[s]);
           }
+          if (++s == depth) {
+            s = 0;
+            ph ^= 1u;
+          }
         }
       }
-      // Every issued load has landed before the CTA may exit (bounded).
-      for (int j = max(0, it - depth); j < it; j++) mb_wait(&full[j % depth], (j / depth) & 1);
+      // Every issued load has landed before the CTA may exit (bounded): the last
+      // min(it, depth) stages, newest first.
+      for (int j = 0; j < min(it, depth); j++) {
+        if (s == 0) {
+          s = depth;
+          ph ^= 1u;
+        }
+        s--;
+        mb_wait(&full[s], ph);
+      }
     }
   } else if (warp == 1) {
     // ---- MMA issuer ----
     if (lane == 0) {
-      int it = 0;
+      int sw = 0, sa = 0;
+      uint32_t pw = 0, pa = 0;  // round parities of the two rings
       for (int t = 0; t < nt && !*err; t++) {
         const int b = t & 1;
         if (t >= 2 && !mb_wait(&tempty[b], ((t >> 1) - 1) & 1)) {
@@ -350,10 +369,8 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(b * kLmN);
         const uint32_t idesc = idesc_n(tile_n(t));
-        for (int kb = 0; kb < kb_n; kb++, it++) {
-          const int sw = it % kW, sa = a_res ? kb : it % dA;
-          if (!mb_wait(&wfull[sw], (it / kW) & 1) ||
-              !mb_wait(&afull[sa], a_res ? 0u : (uint32_t)((it / dA) & 1))) {
+        for (int kb = 0; kb < kb_n; kb++) {
+          if (!mb_wait(&wfull[sw], pw) || !mb_wait(&afull[sa], pa)) {
             *err = 1u;
             break;
           }
@@ -366,6 +383,14 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                    (kb | kk) != 0 ? 1u : 0u);
           mma_commit(&wempty[sw]);  // the stages are free once these MMAs have read them
           if (!a_res) mma_commit(&aempty[sa]);
+          if (++sw == dW) {
+            sw = 0;
+            pw ^= 1u;
+          }
+          if (++sa == dA) {  // resident states: every tile reads the same stages, round 0
+            sa = 0;
+            if (!a_res) pa ^= 1u;
+          }
         }
         if (*err) break;
         mma_commit(&tfull[b]);  // the tile's accumulator is complete
