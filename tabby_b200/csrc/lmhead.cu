@@ -6,27 +6,32 @@
 // src/shaders/matmul_f16.wgsl / matvec_q4.wgsl into this.logits) followed by the sampling
 // dispatches (forward.ts:520-601) and sampleFromTopK (src/engine/sampler.ts:147-212).
 //
-//   lmhead_kernel   one CTA a SM, each a contiguous range of vocabulary tiles of 128 rows.
-//                   warps 0 and 10     TMA producers (one lane each): cp.async.bulk.tensor 2-D loads of the
-//                                      weight tiles (128 x 64 bf16, an 8-stage ring: they
-//                                      come from HBM) and of the hidden-state tiles (128 x
-//                                      64 bf16, a 4-stage ring: they stay in L2), 128-byte
-//                                      swizzle, mbarrier transaction counts. No multicast.
+//   lmhead_kernel   one CTA a SM, 320 threads. Vocabulary tiles of 128 rows (the last one
+//                   narrower, a multiple of 16) are taken from a global counter, so SMs
+//                   that stream faster take more of them.
+//                   warp 0 (one lane)  TMA producer: cp.async.bulk.tensor 2-D loads of the
+//                                      weight stages (128 rows x 64 bf16, 128-byte swizzle,
+//                                      from HBM) and of the hidden states (the batch's rows
+//                                      rounded up to 8; resident in shared memory when all
+//                                      K blocks fit, else a ring), mbarrier transaction
+//                                      counts. No multicast.
 //                   warp 1 (one lane)  tcgen05.mma.cta_group::1.kind::f16, M = 128 token rows
-//                                      (rows past the batch are zero-filled by TMA), N = 128
-//                                      vocabulary rows, K = 16 a step, fp32 accumulators in
-//                                      TMEM, double-buffered (2 x 128 columns); tcgen05.commit
+//                                      (rows past the batch are never read back), N = the
+//                                      tile's rows, K = 16 a step, fp32 accumulators in TMEM,
+//                                      double-buffered (2 x 128 columns); tcgen05.commit
 //                                      frees a stage and hands a finished tile over.
-//                   warps 2-5          epilogue: tcgen05.ld 32x32b of the accumulator, one
-//                                      thread a token row: online max and sum(exp(x - max));
-//                                      logits above the row's 64th best so far are appended
-//                                      to the row's pending list in shared memory, and the
-//                                      warp merges a row's pending list into its sorted best
-//                                      64 (bitonic networks) once 32 are pending; then the
-//                                      CTA's (max, sum-exp) and best 64 go to a partials
-//                                      buffer (optionally the logits themselves, for tests).
+//                   warps 2-9          epilogue, one thread a (token row, half of the tile's
+//                                      columns): tcgen05.ld 32x32b, online max and
+//                                      sum(exp(x - max)) with tree reductions, and the best
+//                                      16 logits in registers (a parallel insertion); at the
+//                                      end the two halves merge, and the CTA's (max,
+//                                      sum-exp) and best 16 go to a partials buffer
+//                                      (optionally the logits themselves, for tests).
 //   lmhead_merge_kernel (sampler_kernels.cu) finishes every row: merged statistics, the
-//                   global top-k of the candidates, sampleFromTopK in float64.
+//                   global top-k of the candidates, sampleFromTopK in float64, and flags
+//                   rows where a CTA's 16th best lies above the row's k-th best. For those
+//                   (rare) rows the exact variant (the best 64 a CTA, in a shared-memory
+//                   table) and its merge run; both launches return at once otherwise.
 // Every mbarrier wait is bounded; a wait that runs out sets an error word and the rows
 // report TABBY_ETIMEOUT.
 #include <cuda.h>
@@ -54,7 +59,7 @@ constexpr int kLmUnit = 16;        // CTAs own vocabulary ranges in units of 16 
 constexpr int kTileBytes = kLmM * kLmK * 2;   // 16 KB: a hidden-state tile
 constexpr int kWTileBytes = kLmN * kLmK * 2;  // 16 KB: a weight tile
 constexpr int kStageBytes2 = 2 * kTileBytes;
-constexpr int kLmThreads = 352;    // weight producer, MMA, 8 epilogue warps, hidden producer
+constexpr int kLmThreads = 320;    // TMA producer, MMA issuer, 8 epilogue warps
 constexpr int kEpiThreads = 256;   // two epilogue warps a TMEM lane quarter
 constexpr int kTmemCols = 2 * kLmN;
 constexpr unsigned long long kWaitNs = 500000000ull;  // a bounded wait gives up after 0.5 s
@@ -90,6 +95,8 @@ constexpr size_t lm_smem() {
 struct LmArgs {
   int32_t rows, vocab, hidden;
   int32_t units;                 // vocabulary rows in units of kLmUnit
+  int32_t ntiles;                // tiles of kLmN rows (the last one may be narrower)
+  uint32_t *tile_ctr;            // [0] next tile, [1] CTAs done: zero between launches
   uint32_t a_bytes;              // bytes of a hidden-state box: round_up(rows, 8) x 128
   float2 *stats;                 // [rows][gridDim.x]
   unsigned long long *cands;     // [rows][gridDim.x][kLmCands]
@@ -245,6 +252,9 @@ __global__ void __launch_bounds__(kLmThreads, 1)
     lmhead_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__ CUtensorMap map_w,
                   const __grid_constant__ CUtensorMap map_w16, const __grid_constant__ LmArgs a) {
   constexpr int kW = LmVariant<KL>::kWStages, kA = LmVariant<KL>::kAStages;
+  // Launched with programmatic stream serialization (its launch overlaps the previous
+  // kernel's tail): wait for the previous kernel in the stream to complete.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (a.gate && *a.gate != a.epoch) return;  // the exact pass, not needed this call
   extern __shared__ unsigned char smem_dyn[];
   unsigned char *base = reinterpret_cast<unsigned char *>(
@@ -259,15 +269,14 @@ __global__ void __launch_bounds__(kLmThreads, 1)
   uint64_t *tfull = aempty + kAMaxStages, *tempty = tfull + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
   volatile uint32_t *err = tmem_slot + 1;
+  // Which tile a weight stage belongs to (-1: no more tiles), and which tile each
+  // accumulator holds, handed from the producer to the MMA issuer to the epilogue.
+  volatile int32_t *stage_tile = reinterpret_cast<volatile int32_t *>(tmem_slot + 2);
+  volatile int32_t *acc_tile = stage_tile + kWMax;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // This CTA's vocabulary rows: an even share of the 16-row units, contiguous, cut into
-  // tiles of kLmN rows (the last one narrower when the share is not a multiple of kLmN).
-  const int u0 = (int)(((int64_t)blockIdx.x * a.units) / gridDim.x);
-  const int nu = (int)(((int64_t)(blockIdx.x + 1) * a.units) / gridDim.x) - u0;
-  constexpr int kUpt = kLmN / kLmUnit;  // units a full tile
-  const int nt = (nu + kUpt - 1) / kUpt;
-  auto tile_v0 = [&](int t) { return (u0 + t * kUpt) * kLmUnit; };
-  auto tile_n = [&](int t) { return min(kUpt, nu - t * kUpt) * kLmUnit; };
+  // Tiles are taken from a global counter, so SMs that stream faster take more of them;
+  // a CTA's tiles come in increasing order. Tile g: vocabulary rows [g kLmN, + width).
+  auto tile_width = [&](int g) { return min(kLmN, a.units * kLmUnit - g * kLmN); };
   const int kb_n = a.hidden / kLmK;
   // The rings share kRing bytes. When every K block of the batch's hidden states fits
   // beside kW weight stages, the states stay resident (loaded once, never released) and
@@ -290,7 +299,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
       mb_init(&aempty[s], 1);
     }
     for (int b = 0; b < 2; b++) {
-      mb_init(&tfull[b], 1);
+      mb_init(&tfull[b], 2);  // the MMAs' completion and the issuer's tile hand-over
       mb_init(&tempty[b], kEpiThreads / 32);  // one arrival an epilogue warp
     }
     *err = 0u;
@@ -308,69 +317,112 @@ __global__ void __launch_bounds__(kLmThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 || warp == 10) {
-    // ---- TMA producers, one lane of their own warp each (a lane blocked on one ring must
-    // not hold up the other): warp 0 the weight tiles, warp 10 the hidden-state tiles ----
+  if (warp == 0) {
+    // ---- TMA producer (one lane): takes a tile, then streams its weight stages and, per
+    // stage, the hidden-state box (resident states: only with the first tile) ----
     if (lane == 0) {
-      const bool wt = warp == 0;
-      const int depth = wt ? dW : dA;
-      uint64_t *full = wt ? wfull : afull, *empty = wt ? wempty : aempty;
-      unsigned char *ring = wt ? wring : aring;
-      const int slot = wt ? kWTileBytes : (int)a.a_bytes;
-      int it = 0, s = 0;
-      uint32_t ph = 0;  // the ring's round parity; a fresh barrier passes a wait on parity 1
-      for (int t = 0; t < ((!wt && a_res) ? min(nt, 1) : nt) && !*err; t++) {
-        const int v0 = tile_v0(t), n = tile_n(t);
-        for (int kb = 0; kb < kb_n; kb++, it++) {
-          if (!mb_wait(&empty[s], ph ^ 1u)) {
-            *err = 1u;
+      int sw = 0, sa = 0, nw = 0, na = 0;
+      uint32_t pw = 0, pa = 0;  // round parities; a fresh barrier passes a wait on parity 1
+      bool a_loaded = false, ok = true, ended = false;
+      while (ok) {
+        int g = (int)atomicAdd(a.tile_ctr, 1u);
+        if (g >= a.ntiles || *err) g = -1;
+        if (!mb_wait(&wempty[sw], pw ^ 1u)) break;
+        if (g < 0) {  // the end: a stage with no data carries the mark
+          stage_tile[sw] = -1;
+          mb_arrive(&wfull[sw]);
+          nw++;
+          if (++sw == dW) {
+            sw = 0;
+            pw ^= 1u;
+          }
+          ended = true;
+          break;
+        }
+        const int v0 = g * kLmN, n = tile_width(g);
+        for (int kb = 0; kb < kb_n; kb++) {
+          if (kb > 0 && !mb_wait(&wempty[sw], pw ^ 1u)) {
+            ok = false;
             break;
           }
-          unsigned char *dst = ring + s * slot;
-          if (!wt) {  // only the batch's rows (rounded up to 8) of the hidden states
-            mb_arrive_expect(&full[s], a.a_bytes);
-            tma_load_2d(dst, &map_h, kb * kLmK, 0, &full[s]);
-          } else if (n == kLmN) {
-            mb_arrive_expect(&full[s], (uint32_t)kWTileBytes);
-            tma_load_2d(dst, &map_w, kb * kLmK, v0, &full[s]);
+          if (!a_res || !a_loaded) {  // only the batch's rows (rounded up to 8)
+            if (!mb_wait(&aempty[sa], pa ^ 1u)) {
+              ok = false;
+              break;
+            }
+            mb_arrive_expect(&afull[sa], a.a_bytes);
+            tma_load_2d(aring + sa * (int)a.a_bytes, &map_h, kb * kLmK, 0, &afull[sa]);
+            na++;
+            if (++sa == dA) {
+              sa = 0;
+              pa ^= 1u;
+            }
+          }
+          stage_tile[sw] = g;
+          unsigned char *dst = wring + sw * kWTileBytes;
+          if (n == kLmN) {
+            mb_arrive_expect(&wfull[sw], (uint32_t)kWTileBytes);
+            tma_load_2d(dst, &map_w, kb * kLmK, v0, &wfull[sw]);
           } else {  // a narrow last tile: boxes of 16 rows, 2 KB apart (same swizzle phase)
-            mb_arrive_expect(&full[s], (uint32_t)(n * kLmK * 2));
+            mb_arrive_expect(&wfull[sw], (uint32_t)(n * kLmK * 2));
             for (int j = 0; j < n; j += kLmUnit)
-              tma_load_2d(dst + j * kLmK * 2, &map_w16, kb * kLmK, v0 + j, &full[s]);
+              tma_load_2d(dst + j * kLmK * 2, &map_w16, kb * kLmK, v0 + j, &wfull[sw]);
           }
-          if (++s == depth) {
-            s = 0;
-            ph ^= 1u;
+          nw++;
+          if (++sw == dW) {
+            sw = 0;
+            pw ^= 1u;
           }
         }
+        a_loaded = true;
       }
-      // Every issued load has landed before the CTA may exit (bounded): the last
-      // min(it, depth) stages, newest first.
-      for (int j = 0; j < min(it, depth); j++) {
-        if (s == 0) {
-          s = depth;
-          ph ^= 1u;
+      if (!ended) *err = 1u;  // a wait ran out
+      // Every issued load has landed before the CTA may exit (bounded): the last stages
+      // of each ring, newest first.
+      for (int j = 0; j < min(nw, dW); j++) {
+        if (sw == 0) {
+          sw = dW;
+          pw ^= 1u;
         }
-        s--;
-        mb_wait(&full[s], ph);
+        sw--;
+        mb_wait(&wfull[sw], pw);
+      }
+      for (int j = 0; j < min(na, dA); j++) {
+        if (sa == 0) {
+          sa = dA;
+          pa ^= 1u;
+        }
+        sa--;
+        mb_wait(&afull[sa], pa);
       }
     }
   } else if (warp == 1) {
-    // ---- MMA issuer ----
+    // ---- MMA issuer (one lane) ----
     if (lane == 0) {
       int sw = 0, sa = 0;
       uint32_t pw = 0, pa = 0;  // round parities of the two rings
-      for (int t = 0; t < nt && !*err; t++) {
+      for (int t = 0; !*err; t++) {
         const int b = t & 1;
         if (t >= 2 && !mb_wait(&tempty[b], ((t >> 1) - 1) & 1)) {
           *err = 1u;
           break;
         }
+        if (!mb_wait(&wfull[sw], pw)) {
+          *err = 1u;
+          break;
+        }
+        const int g = stage_tile[sw];
+        acc_tile[b] = g;
+        if (g < 0) {  // no more tiles: both arrivals, so the epilogue sees the mark
+          mb_arrive(&tfull[b]);
+          mb_arrive(&tfull[b]);
+          break;
+        }
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(b * kLmN);
-        const uint32_t idesc = idesc_n(tile_n(t));
+        const uint32_t idesc = idesc_n(tile_width(g));
         for (int kb = 0; kb < kb_n; kb++) {
-          if (!mb_wait(&wfull[sw], pw) || !mb_wait(&afull[sa], pa)) {
+          if ((kb > 0 && !mb_wait(&wfull[sw], pw)) || !mb_wait(&afull[sa], pa)) {
             *err = 1u;
             break;
           }
@@ -393,6 +445,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
           }
         }
         if (*err) break;
+        mb_arrive(&tfull[b]);   // the tile number in acc_tile[b] is published
         mma_commit(&tfull[b]);  // the tile's accumulator is complete
       }
     }
@@ -423,14 +476,16 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         bi[e] = 0xffffffffu;
       }
       float thr_val = -INFINITY;  // bv[kFastKeep - 1]: a logit must exceed it to enter
-      for (int t = 0; t < nt; t++) {
+      for (int t = 0;; t++) {
         const int b = t & 1;
         if (!mb_wait(&tfull[b], (t >> 1) & 1)) {
           *err = 1u;
           break;
         }
         tc_fence_after();
-        const int v0 = tile_v0(t), vend = min(a.vocab, v0 + tile_n(t));
+        const int g = acc_tile[b];
+        if (g < 0) break;  // no more tiles
+        const int v0 = g * kLmN, vend = min(a.vocab, v0 + tile_width(g));
 #pragma unroll 1
         for (int c = hf * (kLmN / 64); c < (hf + 1) * (kLmN / 64); c++) {
           const int vb = v0 + 32 * c;
@@ -601,14 +656,16 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         __syncwarp();
       }
     };
-    for (int t = 0; t < nt; t++) {
+    for (int t = 0;; t++) {
       const int b = t & 1;
       if (!mb_wait(&tfull[b], (t >> 1) & 1)) {
         *err = 1u;
         break;
       }
       tc_fence_after();
-      const int v0 = tile_v0(t), vend = min(a.vocab, v0 + tile_n(t));
+      const int g = acc_tile[b];
+      if (g < 0) break;  // no more tiles
+      const int v0 = g * kLmN, vend = min(a.vocab, v0 + tile_width(g));
 #pragma unroll 1
       for (int c = 0; c < (hf == 0 ? kLmN / 32 : 0); c++) {
         uint32_t r[32];
@@ -668,7 +725,15 @@ __global__ void __launch_bounds__(kLmThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (*err && tid == 0) *a.error = a.epoch;
+  if (tid == 0) {
+    if (*err) *a.error = a.epoch;
+    // The last CTA to finish zeroes the tile counter for the next launch (every CTA has
+    // taken its last tile by now).
+    if (atomicAdd(a.tile_ctr + 1, 1u) == gridDim.x - 1) {
+      a.tile_ctr[0] = 0u;
+      a.tile_ctr[1] = 0u;
+    }
+  }
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
@@ -712,6 +777,24 @@ bool make_map(CUtensorMap *m, const void *ptr, uint64_t inner, uint64_t outer, u
          CUDA_SUCCESS;
 }
 
+// A launch with programmatic stream serialization: the kernel may start before the previous
+// one in the stream completes and orders itself with griddepcontrol.wait.
+template <typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Args...), int grid, int block, size_t smem,
+                       cudaStream_t stream, const Args &...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 int lfail(int status, const char *fmt, ...) {
   char msg[256];
   va_list ap;
@@ -744,6 +827,8 @@ struct tabby_lmhead {
   uint32_t *error;  // [0] = the epoch of a call whose bounded wait ran out, [1] = the
                     // epoch of a call with a row for the exact pass
   uint32_t *flags;  // [max_rows] = the epoch of a call whose exact pass recomputes the row
+  uint32_t *tile_ctr;  // the kernels' tile counter (zeroed by the last CTA of each launch)
+  int32_t ntiles;
 };
 
 extern "C" {
@@ -778,6 +863,7 @@ int tabby_lmhead_create(int32_t device, int32_t max_rows, int32_t vocab, int32_t
   h->vocab = vocab;
   h->hidden = hidden;
   h->units = (vocab + kLmUnit - 1) / kLmUnit;
+  h->ntiles = (h->units + kLmN / kLmUnit - 1) / (kLmN / kLmUnit);
   // Every SM, an even share of the 16-row units each (at least a full tile's worth).
   h->grid = std::min((h->units + kLmN / kLmUnit - 1) / (kLmN / kLmUnit), std::max(sms, 1));
   const size_t nst = (size_t)max_rows * h->grid;  // one part a CTA
@@ -786,6 +872,8 @@ int tabby_lmhead_create(int32_t device, int32_t max_rows, int32_t vocab, int32_t
       (err = cudaMalloc(&h->error, 16)) != cudaSuccess ||
       (err = cudaMemset(h->error, 0, 16)) != cudaSuccess ||
       (err = cudaMalloc(&h->flags, (size_t)max_rows * 4)) != cudaSuccess ||
+      (err = cudaMalloc(&h->tile_ctr, 8)) != cudaSuccess ||
+      (err = cudaMemset(h->tile_ctr, 0, 8)) != cudaSuccess ||
       (err = cudaMemset(h->flags, 0, (size_t)max_rows * 4)) != cudaSuccess ||
       (err = cudaFuncSetAttribute(lmhead_kernel<kFastKeep>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -794,6 +882,7 @@ int tabby_lmhead_create(int32_t device, int32_t max_rows, int32_t vocab, int32_t
                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)lm_smem<kLmCands>())) != cudaSuccess) {
     if (h->flags) cudaFree(h->flags);
+    if (h->tile_ctr) cudaFree(h->tile_ctr);
     if (h->stats) cudaFree(h->stats);
     if (h->cands) cudaFree(h->cands);
     if (h->error) cudaFree(h->error);
@@ -815,6 +904,7 @@ int tabby_lmhead_destroy(tabby_lmhead *h) {
   cudaFree(h->cands);
   cudaFree(h->error);
   cudaFree(h->flags);
+  cudaFree(h->tile_ctr);
   if (cur != h->device) cudaSetDevice(cur);
   delete h;
   return TABBY_OK;
@@ -868,6 +958,8 @@ int tabby_lmhead_sample_async(tabby_lmhead *h, const void *d_hidden, const void 
   a.vocab = h->vocab;
   a.hidden = h->hidden;
   a.units = h->units;
+  a.ntiles = h->ntiles;
+  a.tile_ctr = h->tile_ctr;
   a.a_bytes = (uint32_t)(8 * mb * kLmK * 2);
   a.stats = h->stats;
   a.cands = h->cands;
@@ -893,18 +985,17 @@ int tabby_lmhead_sample_async(tabby_lmhead *h, const void *d_hidden, const void 
   l.row_flag = h->flags;
   l.any_flag = h->error + 1;
   l.epoch = h->epoch;
-  if (err == cudaSuccess) {
-    lmhead_kernel<kFastKeep><<<h->grid, kLmThreads, lm_smem<kFastKeep>(), q>>>(mh, mw, mw16, a);
-    err = cudaGetLastError();
-  }
+  if (err == cudaSuccess)
+    err = launch_pdl(lmhead_kernel<kFastKeep>, h->grid, kLmThreads, lm_smem<kFastKeep>(), q, mh,
+                     mw, mw16, a);
   if (err == cudaSuccess) {
     l.keep = kFastKeep;
     err = launch_lmhead_merge(l, q);
   }
   if (err == cudaSuccess) {
     a.gate = h->error + 1;
-    lmhead_kernel<kLmCands><<<h->grid, kLmThreads, lm_smem<kLmCands>(), q>>>(mh, mw, mw16, a);
-    err = cudaGetLastError();
+    err = launch_pdl(lmhead_kernel<kLmCands>, h->grid, kLmThreads, lm_smem<kLmCands>(), q, mh, mw,
+                     mw16, a);
   }
   if (err == cudaSuccess) {
     l.keep = kLmCands;

@@ -2299,6 +2299,9 @@ __global__ void __launch_bounds__(kThreads) lmhead_merge_kernel(LmheadMergeLaunc
   uint32_t *hist = reinterpret_cast<uint32_t *>(cand + cap);
   const int row = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool exact_pass = a.keep >= kLmCands && a.row_flag != nullptr;
+  // Launched with programmatic stream serialization (its launch overlaps the previous
+  // kernel's tail): wait for the previous kernel in the stream to complete.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (exact_pass && __ldcg(a.row_flag + row) != a.epoch) return;  // settled by the fast pass
   const tabby_sampling_params prm = a.params[row];
   uint32_t pflags = (isnan(prm.temperature) || isnan(prm.top_p)) ? kFlagBadParams : 0u;
@@ -2474,8 +2477,17 @@ cudaError_t launch_lmhead_merge(const LmheadMergeLaunch &l, cudaStream_t stream)
       set_to[dev] = smem;
     }
   }
-  lmhead_merge_kernel<<<l.rows, kThreads, smem, stream>>>(l);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)l.rows);
+  cfg.blockDim = dim3((unsigned)kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, lmhead_merge_kernel, l);
 }
 
 int host_sample_from_topk(const int32_t *ids, const float *logits, int32_t n, float max_logit,
