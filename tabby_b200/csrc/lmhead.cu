@@ -98,7 +98,8 @@ struct LmArgs {
   int32_t ntiles;                // tiles of kLmN rows (the last one may be narrower)
   uint32_t *tile_ctr;            // [0] next tile, [1] CTAs done: zero between launches
   uint32_t a_bytes;              // bytes of a hidden-state box: round_up(rows, 8) x 128
-  float2 *stats;                 // [rows][gridDim.x]
+  float2 *stats;                 // [ntiles][2][stats_ld]: (max, sum-exp) a tile and half
+  int32_t stats_ld;
   unsigned long long *cands;     // [rows][gridDim.x][kLmCands]
   float *logits_out;             // tests only: [rows][vocab] fp32, or NULL
   uint32_t *error;               // set to `epoch` when a bounded wait runs out
@@ -486,6 +487,10 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         const int g = acc_tile[b];
         if (g < 0) break;  // no more tiles
         const int v0 = g * kLmN, vend = min(a.vocab, v0 + tile_width(g));
+        // Statistics a tile and half, so that the merge combines them in a fixed order
+        // whichever CTA took the tile.
+        m = -3.40282347e38f;
+        s = 0.f;
 #pragma unroll 1
         for (int c = hf * (kLmN / 64); c < (hf + 1) * (kLmN / 64); c++) {
           const int vb = v0 + 32 * c;
@@ -563,19 +568,18 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             }
           }
         }
+        if (live) a.stats[((int64_t)g * 2 + hf) * a.stats_ld + row] = make_float2(m, s);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mb_arrive(&tempty[b]);  // the accumulator may be overwritten
       }
-      // The second half's threads hand their statistics and lists over through shared
+      // The second half's threads hand their lists over through shared
       // memory (the staging area, free now: a barrier of the 256 epilogue threads first);
       // the first half's merge them, the lists by (value desc, id asc).
-      float2 *xs = reinterpret_cast<float2 *>(stage_f);             // [kLmM]
-      float *xv = stage_f + 2 * kLmM;                                // [kFastKeep][kLmM]
+      float *xv = stage_f;                                           // [kFastKeep][kLmM]
       uint32_t *xi = reinterpret_cast<uint32_t *>(xv + kFastKeep * kLmM);
       asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
       if (hf == 1) {
-        xs[row] = make_float2(m, s);
 #pragma unroll
         for (int e = 0; e < kFastKeep; e++) {
           xv[e * kLmM + row] = bv[e];
@@ -584,10 +588,6 @@ __global__ void __launch_bounds__(kLmThreads, 1)
       }
       asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
       if (hf == 0 && live) {
-        const float2 o = xs[row];
-        const float mm = fmaxf(m, o.x);
-        s = s * ex2_fast((m - mm) * kLog2e) + o.y * ex2_fast((o.x - mm) * kLog2e);
-        m = mm;
         // Two-pointer merge: this thread's list pops from the front of its registers (a
         // shift), the other half's list is read from shared memory.
         float ov[kFastKeep];
@@ -619,7 +619,6 @@ __global__ void __launch_bounds__(kLmThreads, 1)
           bv[e] = ov[e];
           bi[e] = oi[e];
         }
-        a.stats[(int64_t)row * parts + pi] = make_float2(m, s);
         unsigned long long *dst = a.cands + ((int64_t)row * parts + pi) * kLmCands;
 #pragma unroll
         for (int e = 0; e < kFastKeep; e++)  // the merge reads the first kFastKeep entries
@@ -666,6 +665,8 @@ __global__ void __launch_bounds__(kLmThreads, 1)
       const int g = acc_tile[b];
       if (g < 0) break;  // no more tiles
       const int v0 = g * kLmN, vend = min(a.vocab, v0 + tile_width(g));
+      m = -3.40282347e38f;  // statistics a tile (the second half's slot stays empty)
+      s = 0.f;
 #pragma unroll 1
       for (int c = 0; c < (hf == 0 ? kLmN / 32 : 0); c++) {
         uint32_t r[32];
@@ -705,13 +706,13 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         }
         merge_rows(32);  // keeps every row's pending list below 64
       }
+      if (live) a.stats[((int64_t)g * 2 + hf) * a.stats_ld + row] = make_float2(m, s);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mb_arrive(&tempty[b]);  // the accumulator may be overwritten
     }
     if (hf == 0) merge_rows(1);  // the last pending composites of every row
     if (live && hf == 0) {
-      a.stats[(int64_t)row * parts + pi] = make_float2(m, s);
       unsigned long long *dst = a.cands + ((int64_t)row * parts + pi) * kLmCands;
       for (int e = 0; e < kLmCands; e++) {
         // composite: raw value bits from the key (+0 for a -0 logit, the one value the key folds)
@@ -866,8 +867,9 @@ int tabby_lmhead_create(int32_t device, int32_t max_rows, int32_t vocab, int32_t
   h->ntiles = (h->units + kLmN / kLmUnit - 1) / (kLmN / kLmUnit);
   // Every SM, an even share of the 16-row units each (at least a full tile's worth).
   h->grid = std::min((h->units + kLmN / kLmUnit - 1) / (kLmN / kLmUnit), std::max(sms, 1));
-  const size_t nst = (size_t)max_rows * h->grid;  // one part a CTA
-  if ((err = cudaMalloc(&h->stats, nst * sizeof(float2))) != cudaSuccess ||
+  const size_t nst = (size_t)max_rows * h->grid;  // one candidate part a CTA
+  if ((err = cudaMalloc(&h->stats, (size_t)max_rows * h->ntiles * 2 * sizeof(float2))) !=
+          cudaSuccess ||
       (err = cudaMalloc(&h->cands, nst * kLmCands * 8)) != cudaSuccess ||
       (err = cudaMalloc(&h->error, 16)) != cudaSuccess ||
       (err = cudaMemset(h->error, 0, 16)) != cudaSuccess ||
@@ -962,6 +964,7 @@ int tabby_lmhead_sample_async(tabby_lmhead *h, const void *d_hidden, const void 
   a.tile_ctr = h->tile_ctr;
   a.a_bytes = (uint32_t)(8 * mb * kLmK * 2);
   a.stats = h->stats;
+  a.stats_ld = h->max_rows;
   a.cands = h->cands;
   a.logits_out = d_logits_out;
   a.error = h->error;
@@ -973,6 +976,8 @@ int tabby_lmhead_sample_async(tabby_lmhead *h, const void *d_hidden, const void 
   l.stats = h->stats;
   l.cands = h->cands;
   l.parts = h->grid;
+  l.stat_n = 2 * h->ntiles;
+  l.stats_ld = h->max_rows;
   l.rows = rows;
   l.vocab = h->vocab;
   l.params = d_params;

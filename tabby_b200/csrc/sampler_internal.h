@@ -56,7 +56,9 @@ struct MergeLaunch {
 // row as (raw float bits << 32 | vocab index); unused slots hold index 0xffffffff.
 constexpr int32_t kLmCands = 64;
 struct LmheadMergeLaunch {
-  const float2 *stats = nullptr;               // [rows][parts]
+  const float2 *stats = nullptr;               // [stat_n][stats_ld]: (max, sum-exp) entries
+  int32_t stat_n = 0;
+  int32_t stats_ld = 0;
   const unsigned long long *cands = nullptr;   // [rows][parts][kLmCands]
   int32_t parts = 0;
   int32_t rows = 0;

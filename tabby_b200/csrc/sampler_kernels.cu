@@ -2328,14 +2328,35 @@ __global__ void __launch_bounds__(kThreads) lmhead_merge_kernel(LmheadMergeLaunc
                ? 0ull
                : composite(key_of(__uint_as_float((uint32_t)(e >> 32))), (uint32_t)e);
   };
-  // Each part's best entry, and the (max, sum-exp) of the parts, merged in part order.
+  // Each part's best entry; the (max, sum-exp) entries combined in a fixed order (entry
+  // i by thread i mod kThreads, in increasing i, then the block's trees), so the sum does
+  // not depend on which CTA produced which entry.
   uint64_t *heads = reinterpret_cast<uint64_t *>(hist);  // [parts]: free until the top-k
-  float2 st = make_float2(-3.40282347e38f, 0.f);
   uint64_t hv = 0ull;
   if (tid < a.parts) {
-    st = a.stats[(int64_t)row * a.parts + tid];
     hv = comp_of(__ldcg(rc + (int64_t)tid * kLmCands));
     heads[tid] = hv;
+  }
+  float2 st = make_float2(-3.40282347e38f, 0.f);
+  bool bad_part = false;
+  constexpr int kStatBatch = 8;
+  for (int base = 0; base < a.stat_n; base += kStatBatch * kThreads) {
+    float2 e[kStatBatch];
+#pragma unroll
+    for (int u = 0; u < kStatBatch; u++) {
+      const int i = base + u * kThreads + tid;
+      e[u] = i < a.stat_n ? __ldcg(a.stats + (int64_t)i * a.stats_ld + row)
+                          : make_float2(-3.40282347e38f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < kStatBatch; u++) {
+      bad_part = bad_part || e[u].y != e[u].y || !(e[u].x <= 3.40282347e38f);
+      if (e[u].y > 0.f) {
+        const float mm = fmaxf(st.x, e[u].x);
+        st.y = st.y * __expf(st.x - mm) + e[u].y * __expf(e[u].x - mm);
+        st.x = mm;
+      }
+    }
   }
   float bm = st.x;
 #pragma unroll
@@ -2356,8 +2377,7 @@ __global__ void __launch_bounds__(kThreads) lmhead_merge_kernel(LmheadMergeLaunc
   float M = lane < kWarps ? sh->red_f[lane] : -3.40282347e38f;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  float contrib = (tid < a.parts && st.y > 0.f) ? st.y * __expf(st.x - M) : 0.f;
-  const bool bad_part = tid < a.parts && (st.y != st.y || !(st.x <= 3.40282347e38f));
+  float contrib = st.y > 0.f ? st.y * __expf(st.x - M) : 0.f;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) contrib += __shfl_xor_sync(0xffffffffu, contrib, o);
   const bool wbad = __any_sync(0xffffffffu, bad_part);

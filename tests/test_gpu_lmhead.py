@@ -74,9 +74,10 @@ def test_lmhead_matches_fp32_gemm_and_oracle(oracle, rows, vocab, hidden):
         assert int(o["considered_count"]) == int(e["considered_count"])
         assert abs(float(o["sum_exp"]) - float(e["sum_exp"])) <= REL * float(e["sum_exp"])
         assert abs(o["probability"] - e["probability"]) <= REL * e["probability"]
-    # The production call (no logits written) gives the same outcomes.
+    # The production call (no logits written) gives the same outcomes, bit for bit: the
+    # statistics are combined in a fixed order whichever CTA took which tile.
     out2, ids2, _, _ = _run(torch, h, w, p, u, False)
-    np.testing.assert_array_equal(out2["id"], out["id"])
+    np.testing.assert_array_equal(out2.view(np.uint8), out.view(np.uint8))
     np.testing.assert_array_equal(ids2, ids)
 
 
