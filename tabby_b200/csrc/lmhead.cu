@@ -155,6 +155,21 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
       : "memory");
 }
+// The same with an L2 cache policy: the weights are read once a call, so their lines go
+// first when L2 needs room and the small buffers and code the other kernels use stay.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void tma_load_2d_hint(void *dst, const CUtensorMap *map, int x, int y,
+                                                 uint64_t *bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "l"(pol)
+      : "memory");
+}
 // Shared-memory matrix descriptor of a K-major tile written by TMA with 128-byte swizzle:
 // rows of 128 bytes, 8-row groups 1024 bytes apart (stride byte offset), descriptor
 // version 1 (sm_100), layout type 2 (SWIZZLE_128B). The tile base is 1024-byte aligned.
@@ -325,6 +340,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
       int sw = 0, sa = 0, nw = 0, na = 0;
       uint32_t pw = 0, pa = 0;  // round parities; a fresh barrier passes a wait on parity 1
       bool a_loaded = false, ok = true, ended = false;
+      const uint64_t pol = l2_evict_first();
       while (ok) {
         int g = (int)atomicAdd(a.tile_ctr, 1u);
         if (g >= a.ntiles || *err) g = -1;
@@ -363,11 +379,11 @@ __global__ void __launch_bounds__(kLmThreads, 1)
           unsigned char *dst = wring + sw * kWTileBytes;
           if (n == kLmN) {
             mb_arrive_expect(&wfull[sw], (uint32_t)kWTileBytes);
-            tma_load_2d(dst, &map_w, kb * kLmK, v0, &wfull[sw]);
+            tma_load_2d_hint(dst, &map_w, kb * kLmK, v0, &wfull[sw], pol);
           } else {  // a narrow last tile: boxes of 16 rows, 2 KB apart (same swizzle phase)
             mb_arrive_expect(&wfull[sw], (uint32_t)(n * kLmK * 2));
             for (int j = 0; j < n; j += kLmUnit)
-              tma_load_2d(dst + j * kLmK * 2, &map_w16, kb * kLmK, v0 + j, &wfull[sw]);
+              tma_load_2d_hint(dst + j * kLmK * 2, &map_w16, kb * kLmK, v0 + j, &wfull[sw], pol);
           }
           nw++;
           if (++sw == dW) {
