@@ -132,8 +132,17 @@ __device__ __forceinline__ void cp_async_commit() {
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
-__device__ __forceinline__ void cp_async16_u32(uint32_t dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+// An L2 policy for data read once: its lines go first when L2 needs room, so the code and
+// the small buffers the finish uses stay in L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void cp_async16_u32(uint32_t dst, const void *src, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst),
+               "l"(src), "l"(pol)
+               : "memory");
 }
 __device__ __forceinline__ void st_shared_f4(uint32_t dst, float4 v) {
   asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "f"(v.x), "f"(v.y),
@@ -1853,6 +1862,7 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
     // -FLT_MAX instead. They come back into registers once the group has landed.
     const uint32_t sslot = smem_u32(stage + tid);  // slot (s, q) at + (s * kVec + q) * 8 KB
     const float4 *gsrc = wp + lane;                // this thread's group of the next issue
+    const uint64_t pol = l2_evict_first_policy();  // the logits are read once
     int inext = 0;                                 // iteration of the next issue
     // Issues iteration inext into stage S (compile-time) and advances. Slots of groups
     // past the segment get -FLT_MAX.
@@ -1861,14 +1871,14 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
       if (inext + 1 < wit) {
 #pragma unroll
         for (int q = 0; q < kVec; q++)
-          cp_async16_u32(sslot + (uint32_t)((S * kVec + q) * kThreads * 16), gsrc + q * 32);
+          cp_async16_u32(sslot + (uint32_t)((S * kVec + q) * kThreads * 16), gsrc + q * 32, pol);
       } else if (inext < wit) {
         const int rem = wn - inext * kWarpIter - lane;
 #pragma unroll
         for (int q = 0; q < kVec; q++) {
           const uint32_t dst = sslot + (uint32_t)((S * kVec + q) * kThreads * 16);
           if (q * 32 < rem)
-            cp_async16_u32(dst, gsrc + q * 32);
+            cp_async16_u32(dst, gsrc + q * 32, pol);
           else
             st_shared_f4(dst, kPast);
         }
