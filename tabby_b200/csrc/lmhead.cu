@@ -341,9 +341,13 @@ __global__ void __launch_bounds__(kLmThreads, 1)
       uint32_t pw = 0, pa = 0;  // round parities; a fresh barrier passes a wait on parity 1
       bool a_loaded = false, ok = true, ended = false;
       const uint64_t pol = l2_evict_first();
+      // The next tile is asked for one tile ahead, so the counter's round trip overlaps
+      // the current tile's loads.
+      int g_next = (int)atomicAdd(a.tile_ctr, 1u);
       while (ok) {
-        int g = (int)atomicAdd(a.tile_ctr, 1u);
+        int g = g_next;
         if (g >= a.ntiles || *err) g = -1;
+        else g_next = (int)atomicAdd(a.tile_ctr, 1u);
         if (!mb_wait(&wempty[sw], pw ^ 1u)) break;
         if (g < 0) {  // the end: a stage with no data carries the mark
           stage_tile[sw] = -1;
