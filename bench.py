@@ -314,8 +314,10 @@ def run_ours(args, rank, local_rank, world):
     if not args.profile:
         sharded = run_sharded(args, rank, local_rank, world, dev, pg)
     sweep = None
+    lmhead = None
     if world == 1 and not args.profile:
         sweep = sweep_points(sampler, x, p, u, dev, steps=200)
+        lmhead, _, _ = lmhead_points((1, 128), 100)
 
     result = None
     if rank == 0:
@@ -345,6 +347,8 @@ def run_ours(args, rank, local_rank, world):
         }
         if sharded is not None:
             result["sharded"] = sharded
+        if lmhead is not None:
+            result["lmhead"] = {"what": LMHEAD_WHAT, "points": lmhead}
         if sweep is not None:
             result["sweep"] = {"what": "c4 rows, V=151936, pool cap 1024, outcomes only; "
                                        "each call on a different window of a 255 MB pool",
@@ -568,6 +572,19 @@ LMHEAD_ROWS = (1, 8, 32, 64, 128)
 
 
 def run_lmhead(args):
+    rows = [int(x) for x in args.rows.split(",")] if args.rows else LMHEAD_ROWS
+    points, peak, peak_kind = lmhead_points(rows, args.steps)
+    print(json.dumps({"lmhead": LMHEAD_WHAT, "peak_gbs": peak, "peak_kind": peak_kind,
+                      "points": points}), flush=True)
+    return 0
+
+
+LMHEAD_WHAT = ("fused LM head + sampling, V=151936 x hidden 896 bf16 (272 MB of weights a "
+               "call), pool cap 64; unfused = torch.matmul (cuBLAS, bf16 logits) + fp32 "
+               "conversion + tabby_sample_rows_async")
+
+
+def lmhead_points(rows, steps):
     """Fused LM head + sampling (tabby_lmhead_sample_async) at V=151936, hidden 896
     (Qwen2.5-0.5B's lm_head, bf16 weights, 272 MB: every call reads them from HBM), against
     the unfused path of the same library: torch.matmul (cuBLAS bf16 -> fp32 logits) then
@@ -590,7 +607,7 @@ def run_lmhead(args):
     sampler = Sampler(0, max_top_k=64, max_rows=128, max_vocab=V)
     sptr = torch.cuda.current_stream(dev).cuda_stream
     points = []
-    for b in LMHEAD_ROWS:
+    for b in rows:
         h = torch.randn(b, H, device=dev, generator=g).to(torch.bfloat16)
         p = np.zeros(b, [("temperature", "<f8"), ("top_p", "<f8"), ("top_k", "<i4"),
                          ("reserved", "<i4")])
@@ -617,7 +634,7 @@ def run_lmhead(args):
             for _ in range(5):
                 fn()
             torch.cuda.synchronize(dev)
-            n = max(20, min(args.steps, 200))
+            n = max(20, min(steps, 200))
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
@@ -636,10 +653,7 @@ def run_lmhead(args):
                        "weight_gbs": round(gbs, 1), "hbm_frac": round(gbs / peak, 3),
                        "tensor_tflops": round(tflops, 1)})
     sampler.close()
-    print(json.dumps({"lmhead": "fused LM head + sampling, V=151936 x hidden 896 bf16 "
-                                "(272 MB of weights a call), pool cap 64",
-                      "peak_gbs": peak, "peak_kind": peak_kind, "points": points}), flush=True)
-    return 0
+    return points, peak, peak_kind
 
 
 def main():
@@ -653,6 +667,7 @@ def main():
     ap.add_argument("--sweep", action="store_true", help="batch sweep B=1..256 on one GPU")
     ap.add_argument("--softmax", action="store_true", help="softmax_rows shapes on one GPU")
     ap.add_argument("--lmhead", action="store_true", help="fused LM head + sampling on one GPU")
+    ap.add_argument("--rows", default="", help="--lmhead: comma-separated batch sizes")
     ap.add_argument("--profile", action="store_true",
                     help="only warm-up + timed steps (for ncu): no heat loop, e2e or CPU leg")
     args = ap.parse_args()
