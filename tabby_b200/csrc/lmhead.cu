@@ -14,7 +14,7 @@
 //                                      from HBM) and of the hidden states (the batch's rows
 //                                      rounded up to 8; resident in shared memory when all
 //                                      K blocks fit, else a ring), mbarrier transaction
-//                                      counts. No multicast.
+//                                      counts; every CTA loads only its own tiles.
 //                   warp 1 (one lane)  tcgen05.mma.cta_group::1.kind::f16, M = 128 token rows
 //                                      (rows past the batch are never read back), N = the
 //                                      tile's rows, K = 16 a step, fp32 accumulators in TMEM,
