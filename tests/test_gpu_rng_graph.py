@@ -140,3 +140,35 @@ def test_captured_step_replays(torch_cuda, rows):
         np.testing.assert_array_equal(state.cpu().numpy(), ref_state.cpu().numpy())
     del graph
     s.close()
+
+
+def test_drop_in_sample_batch_agrees_with_device_states(torch_cuda):
+    """The host drop-in (Sampler.sample_batch with one SeededRandom a row, greedy steps
+    included) and the device-RNG path agree draw for draw: same ids every step and the
+    same generator states at the end (greedy steps leave both untouched)."""
+    torch = torch_cuda
+    from tabby_b200 import Sampler
+    from tabby_b200._lib import OUTCOME_DTYPE
+    from tabby_b200.sampler import SamplingParams, SeededRandom
+
+    rows = 6
+    dev = torch.device("cuda", 0)
+    s = Sampler(0, max_top_k=1024, max_rows=rows, max_vocab=VOCAB)
+    seeds = [11 + 977 * r for r in range(rows)]
+    gens = [SeededRandom(sd) for sd in seeds]
+    state_dev = torch.from_numpy(np.array(seeds, np.uint32).view(np.int32)).to(dev)
+    out = torch.empty(rows * OUTCOME_DTYPE.itemsize, dtype=torch.uint8, device=dev)
+    for step in range(5):
+        x, p = make_batch(rows, step, seed=3)
+        p["temperature"][(np.arange(rows) + step) % 3 == 0] = 0.0  # greedy rows move around
+        xd = torch.from_numpy(x).to(dev)
+        s.sample_rows_rng_async(xd, torch.from_numpy(p.view(np.uint8)).to(dev), state_dev, out)
+        got = out.cpu().numpy().view(OUTCOME_DTYPE).copy()
+        for r in range(rows):
+            prm = SamplingParams(temperature=float(p["temperature"][r]),
+                                 topK=int(p["top_k"][r]), topP=float(p["top_p"][r]))
+            host = s.sample_batch(xd[r:r + 1], prm, gens[r])
+            assert int(host.ids[0]) == int(got["id"][r]), (step, r)
+    np.testing.assert_array_equal(state_dev.cpu().numpy().view(np.uint32),
+                                  np.array([g._state for g in gens], np.uint32))
+    s.close()
