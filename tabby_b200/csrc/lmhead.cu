@@ -52,12 +52,13 @@ namespace tabby {
 namespace {
 
 constexpr int kLmM = 128;          // token rows of a tile (the MMA's M)
-constexpr int kLmN = 128;          // vocabulary rows of a tile (the MMA's N)
+constexpr int kLmN = 256;          // vocabulary rows of a full tile (the MMA's N, its largest)
+constexpr int kLmSmallUnits = 4;   // the schedule's tail: tiles of 4 units (64 rows)
 constexpr int kLmK = 64;           // hidden elements a stage (128 bytes of bf16: one swizzle row)
 constexpr int kLmUnit = 16;        // CTAs own vocabulary ranges in units of 16 rows (the MMA's
                                    // smallest N), so the last tile of a range may be narrower
 constexpr int kTileBytes = kLmM * kLmK * 2;   // 16 KB: a hidden-state tile
-constexpr int kWTileBytes = kLmN * kLmK * 2;  // 16 KB: a weight tile
+constexpr int kWTileBytes = kLmN * kLmK * 2;  // 32 KB: a weight stage
 constexpr int kStageBytes2 = 2 * kTileBytes;
 constexpr int kLmThreads = 320;    // TMA producer, MMA issuer, 8 epilogue warps
 constexpr int kEpiThreads = 256;   // two epilogue warps a TMEM lane quarter
@@ -76,12 +77,12 @@ constexpr int kAMaxStages = 64;
 template <int KL> struct LmVariant;
 // The weight tiles (from HBM) get a deeper ring than the hidden-state tiles (from L2).
 template <> struct LmVariant<kFastKeep> {
-  static constexpr int kWStages = 8;
+  static constexpr int kWStages = 4;
   static constexpr int kAStages = 4;
   static constexpr size_t kTable = (size_t)32 * kEpiThreads * 4;  // staged logits [32][256]
 };
 template <> struct LmVariant<kLmCands> {
-  static constexpr int kWStages = 4;
+  static constexpr int kWStages = 2;
   static constexpr int kAStages = 2;
   static constexpr size_t kTable = (size_t)kLmBuf * kLmM * 8;  // [kLmBuf][kLmM]
 };
@@ -95,7 +96,8 @@ constexpr size_t lm_smem() {
 struct LmArgs {
   int32_t rows, vocab, hidden;
   int32_t units;                 // vocabulary rows in units of kLmUnit
-  int32_t ntiles;                // tiles of kLmN rows (the last one may be narrower)
+  int32_t ntiles;                // tiles: big_tiles of kLmN rows, then tiles of 64 rows
+  int32_t big_tiles;
   uint32_t *tile_ctr;            // [0] next tile, [1] CTAs done: zero between launches
   uint32_t a_bytes;              // bytes of a hidden-state box: round_up(rows, 8) x 128
   float2 *stats;                 // [ntiles][2][stats_ld]: (max, sum-exp) a tile and half
@@ -291,8 +293,17 @@ __global__ void __launch_bounds__(kLmThreads, 1)
   volatile int32_t *acc_tile = stage_tile + kWMax;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // Tiles are taken from a global counter, so SMs that stream faster take more of them;
-  // a CTA's tiles come in increasing order. Tile g: vocabulary rows [g kLmN, + width).
-  auto tile_width = [&](int g) { return min(kLmN, a.units * kLmUnit - g * kLmN); };
+  // a CTA's tiles come in increasing order. The schedule: big_tiles tiles of kLmN rows,
+  // then tiles of 64 rows for the last two rounds (so CTAs end within a small tile of one
+  // another); the vocabulary's last tile may be narrower (a multiple of 16 rows).
+  auto tile_v0 = [&](int g) {
+    return g < a.big_tiles ? g * kLmN
+                           : (a.big_tiles * (kLmN / kLmUnit) + (g - a.big_tiles) * kLmSmallUnits) *
+                                 kLmUnit;
+  };
+  auto tile_width = [&](int g) {
+    return min(g < a.big_tiles ? kLmN : kLmSmallUnits * kLmUnit, a.units * kLmUnit - tile_v0(g));
+  };
   const int kb_n = a.hidden / kLmK;
   // The rings share kRing bytes. When every K block of the batch's hidden states fits
   // beside kW weight stages, the states stay resident (loaded once, never released) and
@@ -360,7 +371,7 @@ __global__ void __launch_bounds__(kLmThreads, 1)
           ended = true;
           break;
         }
-        const int v0 = g * kLmN, n = tile_width(g);
+        const int v0 = tile_v0(g), n = tile_width(g);
         for (int kb = 0; kb < kb_n; kb++) {
           if (kb > 0 && !mb_wait(&wempty[sw], pw ^ 1u)) {
             ok = false;
@@ -506,13 +517,15 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         tc_fence_after();
         const int g = acc_tile[b];
         if (g < 0) break;  // no more tiles
-        const int v0 = g * kLmN, vend = min(a.vocab, v0 + tile_width(g));
+        const int v0 = tile_v0(g), vend = min(a.vocab, v0 + tile_width(g));
         // Statistics a tile and half, so that the merge combines them in a fixed order
         // whichever CTA took the tile.
         m = -3.40282347e38f;
         s = 0.f;
+        // The halves take alternate 32-column chunks (so narrow tiles split evenly too);
+        // each thread still visits its vocabulary ids in increasing order.
 #pragma unroll 1
-        for (int c = hf * (kLmN / 64); c < (hf + 1) * (kLmN / 64); c++) {
+        for (int c = hf; c < kLmN / 32; c += 2) {
           const int vb = v0 + 32 * c;
           if (vb >= vend) break;  // past a narrow tile's columns (warp-uniform)
           uint32_t r[32];
@@ -684,11 +697,11 @@ __global__ void __launch_bounds__(kLmThreads, 1)
       tc_fence_after();
       const int g = acc_tile[b];
       if (g < 0) break;  // no more tiles
-      const int v0 = g * kLmN, vend = min(a.vocab, v0 + tile_width(g));
+      const int v0 = tile_v0(g), vend = min(a.vocab, v0 + tile_width(g));
       m = -3.40282347e38f;  // statistics a tile (the second half's slot stays empty)
       s = 0.f;
 #pragma unroll 1
-      for (int c = 0; c < (hf == 0 ? kLmN / 32 : 0); c++) {
+      for (int c = 0; c < (hf == 0 ? (vend - v0 + 31) / 32 : 0); c++) {
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kLmN + 32 * c), r);
         const int vb = v0 + 32 * c;
@@ -850,6 +863,7 @@ struct tabby_lmhead {
   uint32_t *flags;  // [max_rows] = the epoch of a call whose exact pass recomputes the row
   uint32_t *tile_ctr;  // the kernels' tile counter (zeroed by the last CTA of each launch)
   int32_t ntiles;
+  int32_t big_tiles;
 };
 
 extern "C" {
@@ -884,9 +898,16 @@ int tabby_lmhead_create(int32_t device, int32_t max_rows, int32_t vocab, int32_t
   h->vocab = vocab;
   h->hidden = hidden;
   h->units = (vocab + kLmUnit - 1) / kLmUnit;
-  h->ntiles = (h->units + kLmN / kLmUnit - 1) / (kLmN / kLmUnit);
+  // Tiles of 64 rows cover the last two rounds (8 units a CTA); big tiles the rest.
+  {
+    const int grid_guess = std::max(std::min(sms, (h->units + kLmSmallUnits - 1) / kLmSmallUnits), 1);
+    const int tail_units = std::min(h->units, 2 * kLmSmallUnits * grid_guess);
+    h->big_tiles = (h->units - tail_units) / (kLmN / kLmUnit);
+    const int rest = h->units - h->big_tiles * (kLmN / kLmUnit);
+    h->ntiles = h->big_tiles + (rest + kLmSmallUnits - 1) / kLmSmallUnits;
+  }
   // Every SM, an even share of the 16-row units each (at least a full tile's worth).
-  h->grid = std::min((h->units + kLmN / kLmUnit - 1) / (kLmN / kLmUnit), std::max(sms, 1));
+  h->grid = std::min(h->ntiles, std::max(sms, 1));
   const size_t nst = (size_t)max_rows * h->grid;  // one candidate part a CTA
   if ((err = cudaMalloc(&h->stats, (size_t)max_rows * h->ntiles * 2 * sizeof(float2))) !=
           cudaSuccess ||
@@ -981,6 +1002,7 @@ int tabby_lmhead_sample_async(tabby_lmhead *h, const void *d_hidden, const void 
   a.hidden = h->hidden;
   a.units = h->units;
   a.ntiles = h->ntiles;
+  a.big_tiles = h->big_tiles;
   a.tile_ctr = h->tile_ctr;
   a.a_bytes = (uint32_t)(8 * mb * kLmK * 2);
   a.stats = h->stats;
