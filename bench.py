@@ -310,9 +310,10 @@ def run_ours(args, rank, local_rank, world):
             e2e_s = float(t.item())
         e2e_value = world * ROWS * e2e_steps / e2e_s
 
-    sharded = None
+    sharded = sharded_peer = None
     if not args.profile:
         sharded = run_sharded(args, rank, local_rank, world, dev, pg)
+        sharded_peer = run_sharded(args, rank, local_rank, world, dev, pg, "peer")
     sweep = None
     lmhead = None
     if world == 1 and not args.profile:
@@ -347,6 +348,8 @@ def run_ours(args, rank, local_rank, world):
         }
         if sharded is not None:
             result["sharded"] = sharded
+        if sharded_peer is not None:
+            result["sharded_peer"] = sharded_peer
         if lmhead is not None:
             result["lmhead"] = {"what": LMHEAD_WHAT, "points": lmhead}
         if sweep is not None:
@@ -376,12 +379,15 @@ def run_ours(args, rank, local_rank, world):
 SHARD_ROWS = 512  # the c5 configuration: B=512 x V=151936 split over the GPUs
 
 
-def run_sharded(args, rank, local_rank, world, dev, pg):
+def run_sharded(args, rank, local_rank, world, dev, pg, exchange="gather"):
     """Vocab-sharded sampling (c5): every rank holds columns [r*V/N, (r+1)*V/N) of 512
-    rows; a step is the local top-64 blocks (row_kernel), one NCCL all-gather of the
-    blocks (none at N=1) and the merge (merge_kernel); every rank ends with the same
-    tokens. Strong scaling: the job is 512 rows of the full vocabulary whatever N is.
-    Device-timed with CUDA events on the launch stream, max over ranks, also per phase."""
+    rows; a step is the local top-64 blocks (row_kernel), then either one NCCL all-gather
+    of the blocks (none at N=1) and the merge of every row on every rank (merge_kernel),
+    or (exchange="peer") one xmerge_kernel that reads the peers' blocks over NVLink,
+    merges this rank's rows and stores their outcomes into every rank's buffer. Every
+    rank ends with the same tokens. Strong scaling: the job is 512 rows of the full
+    vocabulary whatever N is. Device-timed with CUDA events on the launch stream, max
+    over ranks, also per phase."""
     import torch
 
     from tabby_b200 import synth
@@ -389,7 +395,8 @@ def run_sharded(args, rank, local_rank, world, dev, pg):
     from tabby_b200.sharded import SHARD_TOP_K, ShardedSampler, gather_blocks
 
     x, p, u = synth.config("c5", seed=0, rows=SHARD_ROWS)
-    s = ShardedSampler(VOCAB, device=local_rank, max_rows=SHARD_ROWS)
+    s = ShardedSampler(VOCAB, device=local_rank, max_rows=SHARD_ROWS, exchange=exchange)
+    peer = exchange == "peer"
     local = torch.from_numpy(np.ascontiguousarray(x[:, s.lo:s.hi])).to(dev)
     p_dev = torch.from_numpy(p.view(np.uint8).copy()).to(dev)
     u_dev = torch.from_numpy(u).to(dev)
@@ -400,6 +407,15 @@ def run_sharded(args, rank, local_rank, world, dev, pg):
     def step(ev=None):
         if ev:
             ev[0].record(stream)
+        if peer:
+            s.local_into_exchange(local)
+            if ev:
+                ev[1].record(stream)
+                ev[2].record(stream)
+            s.exchange_merge_async(SHARD_ROWS, p_dev, u_dev, out)
+            if ev:
+                ev[3].record(stream)
+            return
         block = s.local_blocks(local)
         if ev:
             ev[1].record(stream)
@@ -434,7 +450,20 @@ def run_sharded(args, rank, local_rank, world, dev, pg):
     if pg is not None:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
     total, *phase = [float(v) for v in t.tolist()]
+    if pg is not None:
+        pg.barrier()  # every rank's last merge has returned before the buffers are freed
     s.close()
+    if peer:
+        return {"metric": "sampled rows/s, vocab-sharded (c5: B=512 x V=151936 split over "
+                          f"{world} GPU(s), local top-64, merge with the exchange over "
+                          "NVLink peer memory)",
+                "value": SHARD_ROWS / (total / 1e3), "unit": "rows/s", "ms_per_step": total,
+                "steps": steps, "scaling": "strong", "n_gpus": world,
+                "phases_us": {"local_row_kernel": 1e3 * phase[0],
+                              "xmerge_kernel (exchange + merge of this rank's rows)":
+                                  1e3 * phase[2]},
+                "local_columns": s.hi - s.lo,
+                "launches_per_step": "row_kernel + xmerge_kernel (no collective library call)"}
     return {"metric": "sampled rows/s, vocab-sharded (c5: B=512 x V=151936 split over "
                       f"{world} GPU(s), local top-64, NCCL all-gather, merge)",
             "value": SHARD_ROWS / (total / 1e3), "unit": "rows/s", "ms_per_step": total,

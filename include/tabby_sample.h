@@ -184,6 +184,40 @@ TABBY_API int tabby_shard_merge_async(tabby_sampler *sampler, const float *d_gat
                             void *stream);
 
 /*
+ * Vocab-sharded sampling with the exchange done by the merge kernel itself over NVLink
+ * peer memory, in place of the all-gather between tabby_shard_local_async and
+ * tabby_shard_merge_async (new in this build; the reference has no multi-GPU path). One
+ * exchange object per rank of a job of `world` ranks (one process per GPU):
+ *   1. tabby_exchange_create; tabby_exchange_ipc_handle gives this rank's
+ *      TABBY_EXCHANGE_HANDLE_BYTES-byte CUDA IPC handle; the caller moves the handles
+ *      between processes (rank-major) and passes all of them to tabby_exchange_open;
+ *   2. every call: tabby_shard_local_async writes this rank's blocks into the buffer
+ *      tabby_exchange_blocks returns; then tabby_exchange_merge_async on the same stream.
+ *      It publishes this rank's blocks, waits for every rank's, merges the rows this rank
+ *      owns (rows [r * rows / world, (r + 1) * rows / world)) into its own buffer, waits
+ *      for every rank's rows and reads them from their owners' buffers, and writes all
+ *      `rows` outcomes to d_out, the same on every rank. Every rank must make the same
+ *      calls in the same order with the same `rows`, params and uniforms. A wait that
+ *      runs out (0.5 s) gives the affected rows status TABBY_ETIMEOUT; the kernel always
+ *      returns.
+ *   3. tabby_exchange_destroy only after every rank's last merge has completed (e.g. after
+ *      a device synchronize and a barrier between the processes).
+ * 1 <= world <= TABBY_EXCHANGE_MAX_WORLD; pool sizes above TABBY_SHARD_TOP_K are clipped.
+ */
+#define TABBY_EXCHANGE_MAX_WORLD 16
+#define TABBY_EXCHANGE_HANDLE_BYTES 64
+typedef struct tabby_exchange tabby_exchange;
+TABBY_API int tabby_exchange_create(int32_t device, int32_t world, int32_t rank, int32_t max_rows,
+                          tabby_exchange **out);
+TABBY_API int tabby_exchange_ipc_handle(tabby_exchange *exchange, void *handle);
+TABBY_API int tabby_exchange_open(tabby_exchange *exchange, const void *handles);
+TABBY_API int tabby_exchange_blocks(tabby_exchange *exchange, float **d_blocks, int32_t *block_ld);
+TABBY_API int tabby_exchange_merge_async(tabby_exchange *exchange, int32_t rows,
+                               const tabby_sampling_params *d_params, const double *d_uniforms,
+                               tabby_sample_outcome *d_out, void *stream);
+TABBY_API int tabby_exchange_destroy(tabby_exchange *exchange);
+
+/*
  * Host-side sampleFromTopK on a TopKResult (sampler.ts:147-212) with the same float64
  * arithmetic the device finalize uses; no GPU involved. For callers that already hold
  * a TopKResult (e.g. from tabby_topk_rows_async).

@@ -24,6 +24,8 @@ TABBY_MAX_TOP_K_LIMIT = 1024
 TABBY_DEFAULT_MAX_TOP_K = 64
 TABBY_SHARD_TOP_K = 64
 TABBY_NOALLOC_MAX_TOP_K = 256
+TABBY_EXCHANGE_MAX_WORLD = 16
+TABBY_EXCHANGE_HANDLE_BYTES = 64
 SHARD_BLOCK_WORDS = 2 + 2 * TABBY_SHARD_TOP_K
 
 # tabby_sampling_params (24 bytes) and tabby_sample_outcome (48 bytes).
@@ -84,6 +86,12 @@ SIGNATURES = {
     "tabby_shard_local_async": ([_P, _P, _I64, _I32, _I32, _I64, _P, _I32, _P], ctypes.c_int),
     "tabby_shard_merge_async": (
         [_P, _P, _I32, _I32, _I32, _P, _P, _P, _P, _P, _I32, _P], ctypes.c_int),
+    "tabby_exchange_create": ([_I32, _I32, _I32, _I32, ctypes.POINTER(_P)], ctypes.c_int),
+    "tabby_exchange_ipc_handle": ([_P, _P], ctypes.c_int),
+    "tabby_exchange_open": ([_P, _P], ctypes.c_int),
+    "tabby_exchange_blocks": ([_P, ctypes.POINTER(_P), ctypes.POINTER(_I32)], ctypes.c_int),
+    "tabby_exchange_merge_async": ([_P, _I32, _P, _P, _P, _P], ctypes.c_int),
+    "tabby_exchange_destroy": ([_P], ctypes.c_int),
     "tabby_sample_from_topk": ([_P, _P, _I32, _F32, _F32, _P, _F64, _P], ctypes.c_int),
     "tabby_sample_rows_noalloc": (
         [_P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _P, _I32, _P], ctypes.c_int),

@@ -17,7 +17,8 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIBDIR = os.path.join(PKG, "lib")
 LIB = os.path.join(LIBDIR, "libtabbysample.so")
-SOURCES = ["sampler_kernels.cu", "capi.cu", "noalloc.cu", "softmax_rows.cu", "lmhead.cu"]
+SOURCES = ["sampler_kernels.cu", "capi.cu", "noalloc.cu", "softmax_rows.cu", "lmhead.cu",
+           "exchange.cu"]
 HEADERS = ["finalize.cuh", "js_math.cuh", "sampler_internal.h", "warp_sort.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

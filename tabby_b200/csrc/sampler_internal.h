@@ -51,6 +51,26 @@ struct MergeLaunch {
   int32_t topk_ld = 0;
 };
 
+// The vocab-sharded merge with its exchange over peer memory (xmerge_kernel). Each rank's
+// exchange buffer holds its blocks [max_rows][block_ld], the outcomes of all rows
+// [max_rows] (each written by the rank that owns the row) and 2 * world flag words
+// (arrive, done: slot q written by rank q with the call's epoch).
+struct XMergeLaunch {
+  MergeLaunch m;                             // rows = all rows; gathered unused; out = caller's
+  // Every rank's buffers, by rank (kernel parameters: no dependent load to find them).
+  const float *peer_blocks[TABBY_EXCHANGE_MAX_WORLD] = {};
+  tabby_sample_outcome *peer_outs[TABBY_EXCHANGE_MAX_WORLD] = {};
+  uint32_t *peer_flags[TABBY_EXCHANGE_MAX_WORLD] = {};
+  uint32_t *flags = nullptr;                 // this rank's flag words
+  uint32_t *counter = nullptr;               // CTAs done (the last one resets it)
+  tabby_sample_outcome *outs = nullptr;      // this rank's outcome buffer
+  int32_t rank = 0;
+  int32_t world = 1;
+  uint32_t epoch = 0;
+  uint64_t timeout_ns = 0;
+};
+cudaError_t launch_xmerge(const XMergeLaunch &l, cudaStream_t stream);
+
 // Partial results of the fused LM-head kernel (lmhead.cu), per (row, CTA): the CTA's
 // (max, sum-exp) of the row over its vocabulary range and its kLmCands best logits of the
 // row as (raw float bits << 32 | vocab index); unused slots hold index 0xffffffff.

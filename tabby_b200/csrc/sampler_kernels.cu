@@ -59,6 +59,7 @@ constexpr int kBins = 2048;               // radix digit: 11 bits
 constexpr int kMaxChunks = 32;            // chunks of one row (warp stats: chunks x 16 <= 512)
 constexpr int kMinChunk = 8192;           // logits: below this a row is not split further
 constexpr int kMergeThreads = 512;
+constexpr int kMaxShards = 16;           // shards the merge takes (candidates <= 2 x kMergeThreads)
 static_assert(kRowGroups == kScratchGroups && kFinishCap >= 8192 &&
                   kRowGroups / (kMaxChunks * kWarps) >= 16 && kMaxChunks == kScratchChunks &&
                   kWarps == kScratchWarps && kMaxChunks * kWarps <= kThreads,
@@ -613,11 +614,13 @@ __device__ __noinline__ uint64_t shrink_to(uint64_t *cand, int n, int k, int lim
 // exp(l - max) / sumExp of the chosen candidate, computed exactly (js_exp); poolMass is
 // the parallel sum (within 1e-12 relative of the reference's) unless the replay ran.
 // ------------------------------------------------------------------------------------
-__device__ __noinline__ void finalize_sample(const int32_t *ids, const float *vals, int n,
+template <bool kSecondOut>
+__device__ __noinline__ void finalize_sample_t(const int32_t *ids, const float *vals, int n,
                                              float max_logit, float sum_exp,
                                              tabby_sampling_params p, double u, double *cum,
                                              double *work, Shared *sh,
-                                             tabby_sample_outcome *out, uint32_t status) {
+                                             tabby_sample_outcome *out, uint32_t status,
+                                             tabby_sample_outcome *out2) {
   const int tid = threadIdx.x;
   if (status != TABBY_OK || n == 0) {
     if (tid == 0) {
@@ -633,6 +636,7 @@ __device__ __noinline__ void finalize_sample(const int32_t *ids, const float *va
       o.status = status != TABBY_OK ? (int32_t)status : (int32_t)TABBY_EEMPTY;
       o.reserved = 0;
       *out = o;
+      if (kSecondOut) *out2 = o;
     }
     return;
   }
@@ -732,9 +736,26 @@ __device__ __noinline__ void finalize_sample(const int32_t *ids, const float *va
     o.status = TABBY_OK;
     o.reserved = fallback ? 1 : 0;  // 1 when the sequential replay decided
     *out = o;
+    if (kSecondOut) *out2 = o;
   }
 }
 
+
+// sampleFromTopK writing one outcome (the row pass), or two (the exchange merge: the
+// peers' copy and the caller's).
+__device__ __forceinline__ void finalize_sample(const int32_t *ids, const float *vals, int n,
+                                                float max_logit, float sum_exp,
+                                                tabby_sampling_params p, double u, double *cum,
+                                                double *work, Shared *sh,
+                                                tabby_sample_outcome *out, uint32_t status,
+                                                tabby_sample_outcome *out2 = nullptr) {
+  if (out2)
+    finalize_sample_t<true>(ids, vals, n, max_logit, sum_exp, p, u, cum, work, sh, out, status,
+                            out2);
+  else
+    finalize_sample_t<false>(ids, vals, n, max_logit, sum_exp, p, u, cum, work, sh, out, status,
+                             nullptr);
+}
 
 // The min(64, n) largest of cand[0, n), sorted descending, into cand[0, 64) (zeros past
 // n). Block-uniform call. Every warp keeps a running top 64 of its share in registers
@@ -2075,11 +2096,14 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
 // ------------------------------------------------------------------------------------
 // Vocab-sharded finish: one CTA per row over the all-gathered shard blocks.
 // ------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch a) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  __shared__ Shared sh_s;
-  Shared *sh = &sh_s;
-  const int row = blockIdx.x;
+// One row of the vocab-sharded merge (block-uniform call): block s of the row is at
+// bases[s] + src_row * a.block_ld. Writes the outcome to *out (and *out2 unless NULL);
+// `status_in` (TABBY_OK or an
+// error found by the caller) overrides the outcome's status.
+__device__ __noinline__ void merge_row(const MergeLaunch &a, int row, int src_row,
+                                       const float *const *bases, uint32_t status_in,
+                                       tabby_sample_outcome *out, tabby_sample_outcome *out2,
+                                       unsigned char *smem_raw, Shared *sh) {
   const int tid = threadIdx.x;
   const int total = a.shards * TABBY_SHARD_TOP_K;
   uint64_t *cand = reinterpret_cast<uint64_t *>(smem_raw);
@@ -2089,19 +2113,20 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch a) {
   int32_t *ids = reinterpret_cast<int32_t *>(cum + TABBY_SHARD_TOP_K);
   float *vals = reinterpret_cast<float *>(ids + TABBY_SHARD_TOP_K);
   const tabby_sampling_params p = a.params[row];
+  auto blk = [&](int s) { return bases[s] + (int64_t)src_row * a.block_ld; };
 
   if (tid == 0) {
     // M = max m_s; S = sum s_s * exp(m_s - M), shards in rank order.
     float mx = -3.40282347e38f;
     uint32_t bad = 0;
     for (int s = 0; s < a.shards; s++) {
-      const float ms = a.gathered[((int64_t)s * a.rows + row) * a.block_ld];
+      const float ms = blk(s)[0];
       if (ms != ms) bad = kFlagBadInput;
       mx = fmaxf(mx, ms);
     }
     double S = 0.0;
     for (int s = 0; s < a.shards; s++) {
-      const float *b = a.gathered + ((int64_t)s * a.rows + row) * a.block_ld;
+      const float *b = blk(s);
       if (b[1] > 0.f)
         S = JS_ADD(S, JS_MUL((double)b[1], js_exp(JS_SUB((double)b[0], (double)mx))));
     }
@@ -2114,7 +2139,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch a) {
   __syncthreads();
   for (int i = tid; i < total; i += kMergeThreads) {
     const int s = i / TABBY_SHARD_TOP_K, j = i % TABBY_SHARD_TOP_K;
-    const float *b = a.gathered + ((int64_t)s * a.rows + row) * a.block_ld;
+    const float *b = blk(s);
     const uint32_t gi = __float_as_uint(b[3 + 2 * j]);
     if (gi != 0xffffffffu) cand[atomicAdd(&sh->count, 1u)] = composite(key_of(b[2 + 2 * j]), gi);
   }
@@ -2131,7 +2156,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch a) {
     if (key == 0x80000000u) {
       // Recover the sign of a zero from the shard block that holds it.
       for (int s = 0; s < a.shards; s++) {
-        const float *b = a.gathered + ((int64_t)s * a.rows + row) * a.block_ld;
+        const float *b = blk(s);
         for (int j = 0; j < TABBY_SHARD_TOP_K; j++)
           if (__float_as_uint(b[3 + 2 * j]) == gi) v = b[2 + 2 * j];
       }
@@ -2142,7 +2167,8 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch a) {
   __syncthreads();
   const float max_logit = kk > 0 ? vals[0] : sh->merge_max;
   const uint32_t flags = sh->flags;
-  const uint32_t status = (flags & kFlagBadInput)    ? (uint32_t)TABBY_EINPUT
+  const uint32_t status = status_in != TABBY_OK          ? status_in
+                          : (flags & kFlagBadInput)    ? (uint32_t)TABBY_EINPUT
                           : (flags & kFlagBadParams) ? (uint32_t)TABBY_EINVAL
                                                      : (uint32_t)TABBY_OK;
   if (a.topk_ids)
@@ -2151,7 +2177,139 @@ __global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch a) {
     for (int i = tid; i < kk; i += kMergeThreads)
       a.topk_values[(int64_t)row * a.topk_ld + i] = vals[i];
   finalize_sample(ids, vals, kk, max_logit, sh->merge_sum, p, a.uniforms[row], cum, scaled,
-                  sh, &a.out[row], status);
+                  sh, out, status, out2);
+}
+
+__global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch a) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ Shared sh_s;
+  __shared__ const float *bases[kMaxShards];
+  if (threadIdx.x < a.shards)
+    bases[threadIdx.x] = a.gathered + (int64_t)threadIdx.x * a.rows * a.block_ld;
+  __syncthreads();
+  const int row = blockIdx.x;
+  merge_row(a, row, row, bases, TABBY_OK, &a.out[row], nullptr, smem_raw, &sh_s);
+}
+
+// ------------------------------------------------------------------------------------
+// Vocab-sharded merge with the exchange over NVLink peer memory (one launch a rank).
+//
+// Every rank's local pass has written its blocks into its own exchange buffer. This
+// kernel (1) tells every rank that this rank's blocks of this call are ready (a release
+// store of the call's epoch into each rank's arrive slot for this rank), (2) waits until
+// every rank's arrive slot here holds the epoch, (3) merges the rows this rank owns
+// (rows [row0, row0 + nloc)), reading the blocks straight from the peers' buffers and
+// writing the outcomes into its own buffer, and (4) in the CTA that ends last, tells
+// every rank that this rank's outcomes are written, waits for every rank's word and
+// reads each row's outcome from the buffer of the rank that owns it into the caller's
+// buffer. A rank overwrites its blocks and outcomes only in its next call, after every
+// rank has said it is done with this one. Every wait polls at most `timeout_ns` of
+// %globaltimer; rows whose blocks or outcomes did not arrive in time report
+// TABBY_ETIMEOUT.
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ void st_release_sys_u32(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits until flags[i] == epoch for i in [0, n), i != skip (one thread). Returns the mask
+// of the slots that did not reach it in time.
+__device__ uint32_t wait_flags(const uint32_t *flags, int n, int skip, uint32_t epoch,
+                               uint64_t timeout_ns) {
+  const uint64_t t0 = global_ns();
+  uint32_t missing = (n >= 32 ? 0xffffffffu : ((1u << n) - 1u)) & ~(1u << skip);
+  if (!missing) return 0u;
+  for (;;) {
+    for (int i = 0; i < n; i++)
+      if (((missing >> i) & 1u) && ld_acquire_sys_u32(&flags[i]) == epoch) missing &= ~(1u << i);
+    if (!missing || global_ns() - t0 > timeout_ns) return missing;
+    __nanosleep(64);
+  }
+}
+
+__host__ __device__ __forceinline__ int32_t xrow0(int32_t rows, int32_t world, int32_t r) {
+  return (int32_t)(((int64_t)r * rows) / world);
+}
+
+// Element q of a per-rank pointer array held in the kernel parameters, selected with
+// constant indices (a dynamic index into the parameters would copy them to local memory).
+template <typename T>
+__device__ __forceinline__ T pick(const T (&arr)[TABBY_EXCHANGE_MAX_WORLD], int q) {
+  T v = arr[0];
+#pragma unroll
+  for (int i = 1; i < TABBY_EXCHANGE_MAX_WORLD; i++)
+    if (q == i) v = arr[i];
+  return v;
+}
+
+__global__ void __launch_bounds__(kMergeThreads) xmerge_kernel(const __grid_constant__ XMergeLaunch x) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ Shared sh_s;
+  __shared__ const float *bases[kMaxShards];
+  __shared__ uint32_t missing;
+  const MergeLaunch &a = x.m;
+  const int tid = threadIdx.x;
+  if (tid < x.world) bases[tid] = pick(x.peer_blocks, tid);
+  if (blockIdx.x == 0 && tid < x.world && tid != x.rank) {
+    // The local pass (the previous launch on this stream) has written the blocks.
+    __threadfence_system();
+    st_release_sys_u32(pick(x.peer_flags, tid) + x.rank, x.epoch);
+  }
+  // This rank's own blocks are ready by stream order; only the peers' are waited for.
+  if (tid == 0) missing = wait_flags(x.flags, x.world, x.rank, x.epoch, x.timeout_ns);
+  __syncthreads();
+  const int nloc = xrow0(a.rows, x.world, x.rank + 1) - xrow0(a.rows, x.world, x.rank);
+  if ((int)blockIdx.x < nloc) {
+    const int row = xrow0(a.rows, x.world, x.rank) + blockIdx.x;
+    // The outcome to this rank's buffer (for the peers) and to the caller's.
+    merge_row(a, row, row, bases, missing ? (uint32_t)TABBY_ETIMEOUT : (uint32_t)TABBY_OK,
+              &x.outs[row], &a.out[row], smem_raw, &sh_s);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();  // this CTA's outcome is written before it is counted
+    sh_s.last = atomicAdd(x.counter, 1u) == gridDim.x - 1 ? 1u : 0u;
+  }
+  __syncthreads();
+  if (!sh_s.last) return;
+  // The last CTA: every outcome of this rank is written; say so to every rank, wait for
+  // every rank's word, then read each row's outcome from the rank that owns it.
+  if (tid == 0) *x.counter = 0u;
+  if (x.world == 1) return;
+  if (tid < x.world && tid != x.rank) {
+    __threadfence_system();
+    st_release_sys_u32(pick(x.peer_flags, tid) + x.world + x.rank, x.epoch);
+  }
+  if (tid == 0) missing = wait_flags(x.flags + x.world, x.world, x.rank, x.epoch, x.timeout_ns);
+  __syncthreads();
+  const uint32_t late = missing;
+  const int mine0 = xrow0(a.rows, x.world, x.rank), mine1 = xrow0(a.rows, x.world, x.rank + 1);
+  for (int i = tid; i < a.rows; i += kMergeThreads) {
+    if (i >= mine0 && i < mine1) continue;  // written by this rank's CTAs
+    int owner = 0;
+    while (owner + 1 < x.world && xrow0(a.rows, x.world, owner + 1) <= i) owner++;
+    tabby_sample_outcome o;
+    const unsigned long long *src =
+        reinterpret_cast<const unsigned long long *>(pick(x.peer_outs, owner) + i);
+    unsigned long long *dst = reinterpret_cast<unsigned long long *>(&o);
+#pragma unroll
+    for (int w = 0; w < 6; w++) dst[w] = __ldcv(src + w);
+    if ((late >> owner) & 1u) {
+      o.id = -1;
+      o.considered_count = 0;
+      o.status = TABBY_ETIMEOUT;
+    }
+    a.out[i] = o;
+  }
 }
 
 // ------------------------------------------------------------------------------------
@@ -2278,6 +2436,14 @@ cudaError_t launch_rows(const RowLaunch &l, const RowGeometry &geo, const Scratc
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, row_kernel, a);
+}
+
+cudaError_t launch_xmerge(const XMergeLaunch &l, cudaStream_t stream) {
+  const size_t smem =
+      (size_t)2 * kMergeThreads * 8 + (size_t)TABBY_SHARD_TOP_K * (3 * 8 + 4 + 4);
+  const int nloc = xrow0(l.m.rows, l.world, l.rank + 1) - xrow0(l.m.rows, l.world, l.rank);
+  xmerge_kernel<<<std::max(nloc, 1), kMergeThreads, smem, stream>>>(l);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_merge(const MergeLaunch &l, cudaStream_t stream) {

@@ -16,6 +16,13 @@ is needed; every rank computes the same merge and ends with the same token ids (
 merge is deterministic), so no broadcast is needed either. Pool sizes are capped at
 64 (TABBY_SHARD_TOP_K), the reference's MAX_TOP_K (kernels.ts:448).
 
+With ``exchange="peer"`` steps 2 and 3 are one kernel instead: each rank's blocks stay in
+its own CUDA-IPC-shared buffer, and tabby_exchange_merge_async reads the peers' blocks
+over NVLink, merges only the rows this rank owns into its own buffer and then reads the
+other rows' outcomes from the ranks that own them (release/acquire flag words order the
+exchange), so the merge work is split across the ranks and no collective library call
+is on the path.
+
 Row-split data parallelism (independent rows per GPU) needs nothing from this module:
 each rank runs Sampler.sample_batch on its own rows with no collective.
 """
@@ -61,11 +68,56 @@ def gather_blocks(block, group=None):
     return torch.cat(parts, 0)
 
 
+class PeerExchange:
+    """This rank's tabby_exchange: a CUDA-IPC-shared buffer that every rank of `group`
+    maps, for tabby_exchange_merge_async. Collective to construct (every rank at once)."""
+
+    def __init__(self, device: int, max_rows: int, group=None):
+        import ctypes
+
+        import torch.distributed as dist
+
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.group = group
+        h = ctypes.c_void_p()
+        check(lib().tabby_exchange_create(int(device), self.world, self.rank, int(max_rows),
+                                          ctypes.byref(h)))
+        self.handle = h
+        self.max_rows = int(max_rows)
+        try:
+            mine = ctypes.create_string_buffer(_lib.TABBY_EXCHANGE_HANDLE_BYTES)
+            check(lib().tabby_exchange_ipc_handle(h, mine))
+            if self.world > 1:
+                allh = [None] * self.world
+                dist.all_gather_object(allh, mine.raw, group=group)
+            else:
+                allh = [mine.raw]
+            blob = ctypes.create_string_buffer(b"".join(allh), len(allh) * len(mine.raw))
+            check(lib().tabby_exchange_open(h, blob))
+            ptr, ld = ctypes.c_void_p(), ctypes.c_int32()
+            check(lib().tabby_exchange_blocks(h, ctypes.byref(ptr), ctypes.byref(ld)))
+            self.blocks_ptr, self.block_ld = ptr.value, ld.value
+        except Exception:
+            lib().tabby_exchange_destroy(h)
+            raise
+
+    def close(self) -> None:
+        """Frees the buffer; call on every rank after a barrier that follows the last merge."""
+        if self.handle:
+            lib().tabby_exchange_destroy(self.handle)
+            self.handle = None
+
+
 class ShardedSampler:
-    """Sampling of vocab-sharded rows on this rank's GPU; one instance per rank."""
+    """Sampling of vocab-sharded rows on this rank's GPU; one instance per rank.
+
+    exchange: "gather" (NCCL all-gather of the blocks, then every rank merges every row)
+    or "peer" (PeerExchange: the merge kernel exchanges over peer memory itself; every
+    rank merges its share of the rows and reads the rest from their owners)."""
 
     def __init__(self, vocab: int, device: Optional[int] = None, group=None,
-                 max_rows: int = 512):
+                 max_rows: int = 512, exchange: str = "gather"):
         import torch
         import torch.distributed as dist
 
@@ -77,9 +129,33 @@ class ShardedSampler:
         self.device = torch.cuda.current_device() if device is None else int(device)
         self.sampler = Sampler(self.device, max_top_k=SHARD_TOP_K, max_rows=max_rows,
                                max_vocab=self.hi - self.lo)
+        if exchange not in ("gather", "peer"):
+            raise ValueError(f"exchange must be 'gather' or 'peer', got {exchange!r}")
+        self.exchange = PeerExchange(self.device, max_rows, group) if exchange == "peer" else None
 
     def close(self) -> None:
+        if self.exchange is not None:
+            self.exchange.close()
         self.sampler.close()
+
+    def local_into_exchange(self, local_logits) -> int:
+        """Step 1 into the peer exchange buffer; returns the row count."""
+        x = self.sampler._check_logits(local_logits)
+        rows, sv = x.shape
+        if sv != self.hi - self.lo:
+            raise ValueError(f"rank {self.rank} holds {self.hi - self.lo} columns, got {sv}")
+        if rows > self.exchange.max_rows:
+            raise ValueError(f"{rows} rows exceed the exchange's {self.exchange.max_rows}")
+        check(lib().tabby_shard_local_async(self.sampler.handle, x.data_ptr(), x.stride(0), rows,
+                                            sv, self.lo, self.exchange.blocks_ptr,
+                                            self.exchange.block_ld, self.sampler._stream()))
+        return rows
+
+    def exchange_merge_async(self, rows: int, params_dev, uniforms_dev, out_dev) -> None:
+        """Steps 2-3 in one kernel over peer memory (device tensors, no sync)."""
+        check(lib().tabby_exchange_merge_async(self.exchange.handle, rows, params_dev.data_ptr(),
+                                               uniforms_dev.data_ptr(), out_dev.data_ptr(),
+                                               self.sampler._stream()))
 
     def local_blocks(self, local_logits):
         """Step 1: [rows, 130] float32 blocks of this rank's slice (device tensor)."""
@@ -114,10 +190,16 @@ class ShardedSampler:
         """One token per row from this rank's slice; identical result on every rank."""
         import torch
 
-        block = self.local_blocks(local_logits)
-        rows = block.shape[0]
-        gathered = gather_blocks(block, self.group)
-        dev = block.device
+        if self.exchange is not None:
+            if return_topk:
+                raise ValueError("return_topk needs exchange='gather'")
+            rows = self.local_into_exchange(local_logits)
+            dev = torch.device("cuda", self.device)
+        else:
+            block = self.local_blocks(local_logits)
+            rows = block.shape[0]
+            gathered = gather_blocks(block, self.group)
+            dev = block.device
         p = params_array(params, rows)
         u = np.ascontiguousarray(uniforms, dtype=np.float64).reshape(-1)
         if u.size != rows:
@@ -125,6 +207,11 @@ class ShardedSampler:
         p_dev = torch.from_numpy(p.view(np.uint8)).to(dev)
         u_dev = torch.from_numpy(u).to(dev)
         out_dev = torch.empty(rows * OUTCOME_DTYPE.itemsize, dtype=torch.uint8, device=dev)
+        if self.exchange is not None:
+            self.exchange_merge_async(rows, p_dev, u_dev, out_dev)
+            out = out_dev.cpu().numpy().view(OUTCOME_DTYPE)
+            _raise_row_errors(out)
+            return SampleBatch(out["id"].copy(), out, None, None)
         ids_dev = vals_dev = None
         if return_topk:
             ids_dev = torch.full((rows, SHARD_TOP_K), -1, dtype=torch.int32, device=dev)
@@ -137,5 +224,6 @@ class ShardedSampler:
                            vals_dev.cpu().numpy() if return_topk else None)
 
 
-__all__ = ["SHARD_TOP_K", "BLOCK_WORDS", "shard_bounds", "gather_blocks", "ShardedSampler"]
+__all__ = ["SHARD_TOP_K", "BLOCK_WORDS", "shard_bounds", "gather_blocks", "PeerExchange",
+           "ShardedSampler"]
 _ = _lib  # status constants live there

@@ -20,11 +20,12 @@ def declared_symbols():
 
 def test_header_declares_the_entry_points():
     names = declared_symbols()
-    assert len(names) == 18, names
+    assert len(names) == 24, names
     for n in ("tabby_sampler_create", "tabby_sample_rows_async", "tabby_topk_rows_async",
               "tabby_sample_rows_rng_async", "tabby_softmax_rows_async",
               "tabby_shard_local_async", "tabby_shard_merge_async", "tabby_sample_from_topk",
-              "tabby_sample_rows_noalloc", "tabby_last_error", "tabby_sample_rows_debug_async"):
+              "tabby_sample_rows_noalloc", "tabby_last_error", "tabby_sample_rows_debug_async",
+              "tabby_exchange_create", "tabby_exchange_merge_async"):
         assert n in names
 
 

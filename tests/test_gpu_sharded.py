@@ -1,9 +1,13 @@
-"""GPU: vocab-sharded sampling through tabby_b200.sharded.ShardedSampler (the C-ABI
-shard kernels plus an NCCL all-gather) against the oracle's whole-row result at pool
-cap 64: token ids, top-k sets and order bit-exact, probabilities within 1e-5.
+"""GPU: vocab-sharded sampling through tabby_b200.sharded.ShardedSampler against the
+oracle's whole-row result at pool cap 64: token ids, top-k sets and order bit-exact,
+probabilities within 1e-5. Both exchanges are covered: the NCCL all-gather followed by
+tabby_shard_merge_async ("gather"), and tabby_exchange_merge_async, whose kernel reads
+the peers' blocks and writes the outcomes over peer memory ("peer").
 
-World size 1 runs in this process; world sizes 2 and 4 run as one process per GPU
-when the box has that many GPUs (skipped otherwise)."""
+Every world size runs as one process per GPU (spawned children, NVLS off) when the box
+has that many GPUs (skipped otherwise). The peer exchange's bounded wait is also made to
+run out: one rank never calls the merge, and the other's kernel must return with every
+row reporting TABBY_ETIMEOUT."""
 import os
 import socket
 
@@ -39,11 +43,11 @@ def _compare(out, ids, x, p, u):
     np.testing.assert_allclose(out["pool_mass"], whole["pool_mass"], rtol=REL)
 
 
-def _rank_main(rank, world, port, rows, result_path):
+def _rank_main(rank, world, port, rows, result_path, exchange="gather", calls=1):
     import torch
     import torch.distributed as dist
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
                             device_id=torch.device("cuda", rank))
@@ -52,21 +56,28 @@ def _rank_main(rank, world, port, rows, result_path):
         from tabby_b200.sharded import ShardedSampler
 
         x, p, u = synth.config("c5", seed=11, rows=rows)
-        s = ShardedSampler(x.shape[1], device=rank, max_rows=rows)
+        s = ShardedSampler(x.shape[1], device=rank, max_rows=rows, exchange=exchange)
         local = torch.from_numpy(np.ascontiguousarray(x[:, s.lo:s.hi])).cuda(rank)
         from tabby_b200.sampler import SamplingParams
 
         params = [SamplingParams(float(q["temperature"]), int(q["top_k"]), float(q["top_p"]))
                   for q in p]
-        batch = s.sample_batch(local, params, u, return_topk=True)
-        np.savez(f"{result_path}.{rank}.npz", out=batch.outcomes.view(np.uint8),
-                 ids=batch.topk_ids)
+        outs = []
+        for _ in range(calls):  # repeated calls reuse the buffers and flag words
+            batch = s.sample_batch(local, params, u, return_topk=exchange == "gather")
+            outs.append(batch.outcomes.view(np.uint8).copy())
+        for o in outs[1:]:
+            np.testing.assert_array_equal(o, outs[0])
+        ids = batch.topk_ids if exchange == "gather" else np.zeros((0,), np.int32)
+        np.savez(f"{result_path}.{rank}.npz", out=outs[0], ids=ids)
+        torch.cuda.synchronize()
+        dist.barrier()
         s.close()
     finally:
         dist.destroy_process_group()
 
 
-def _run_world(tmp_path, world, rows):
+def _run_world(tmp_path, world, rows, exchange="gather", calls=1):
     import torch
 
     if not gpu_available() or torch.cuda.device_count() < world:
@@ -77,13 +88,18 @@ def _run_world(tmp_path, world, rows):
     from tabby_b200 import synth
 
     path = str(tmp_path / "res")
-    mp.start_processes(_rank_main, args=(world, _free_port(), rows, path), nprocs=world,
-                       join=True, start_method="spawn")
+    mp.start_processes(_rank_main, args=(world, _free_port(), rows, path, exchange, calls),
+                       nprocs=world, join=True, start_method="spawn")
     res = [np.load(f"{path}.{r}.npz") for r in range(world)]
     for r in range(1, world):
         np.testing.assert_array_equal(res[r]["out"], res[0]["out"])
     x, p, u = synth.config("c5", seed=11, rows=rows)
-    _compare(res[0]["out"].view(oracle.OUTCOME_DTYPE), res[0]["ids"], x, p, u)
+    out = res[0]["out"].view(oracle.OUTCOME_DTYPE)
+    if exchange == "gather":
+        _compare(out, res[0]["ids"], x, p, u)
+    else:
+        whole, wids, _ = oracle.sample_rows(x, p, u, 64)
+        _compare(out, wids, x, p, u)
 
 
 def test_sharded_world1(tmp_path):
@@ -96,6 +112,72 @@ def test_sharded_world2(tmp_path):
 
 def test_sharded_world4(tmp_path):
     _run_world(tmp_path, 4, 8)
+
+
+def test_sharded_peer_world1(tmp_path):
+    _run_world(tmp_path, 1, 16, "peer", calls=3)
+
+
+def test_sharded_peer_world2(tmp_path):
+    _run_world(tmp_path, 2, 37, "peer", calls=3)
+
+
+def test_sharded_peer_world4(tmp_path):
+    _run_world(tmp_path, 4, 9, "peer", calls=3)
+
+
+def _timeout_main(rank, world, port, result_path):
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    try:
+        from tabby_b200 import synth
+        from tabby_b200._lib import OUTCOME_DTYPE
+        from tabby_b200.sharded import ShardedSampler
+
+        rows = 8
+        x, p, u = synth.config("c5", seed=3, rows=rows)
+        s = ShardedSampler(x.shape[1], device=rank, max_rows=rows, exchange="peer")
+        local = torch.from_numpy(np.ascontiguousarray(x[:, s.lo:s.hi])).cuda(rank)
+        s.local_into_exchange(local)
+        dev = torch.device("cuda", rank)
+        pd = torch.from_numpy(p.view(np.uint8).copy()).to(dev)
+        ud = torch.from_numpy(u).to(dev)
+        out = torch.zeros(rows * OUTCOME_DTYPE.itemsize, dtype=torch.uint8, device=dev)
+        t0 = time.perf_counter()
+        if rank == 0:  # rank 1 never joins the merge: rank 0's waits run out
+            s.exchange_merge_async(rows, pd, ud, out)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        status = out.cpu().numpy().view(OUTCOME_DTYPE)["status"]
+        np.savez(f"{result_path}.{rank}.npz", status=status, dt=np.array([dt]))
+        dist.barrier()  # rank 1 keeps its buffer mapped until rank 0's kernel has returned
+        s.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_exchange_wait_runs_out(tmp_path):
+    import torch
+
+    if not gpu_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    from tabby_b200._lib import TABBY_ETIMEOUT
+
+    path = str(tmp_path / "res")
+    mp.start_processes(_timeout_main, args=(2, _free_port(), path), nprocs=2, join=True,
+                       start_method="spawn")
+    r0 = np.load(f"{path}.0.npz")
+    assert (r0["status"] == TABBY_ETIMEOUT).all(), r0["status"]
+    assert r0["dt"][0] < 5.0
 
 
 def test_shard_merge_emulated_on_one_gpu():
