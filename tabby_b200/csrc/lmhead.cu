@@ -59,7 +59,6 @@ constexpr int kLmUnit = 16;        // CTAs own vocabulary ranges in units of 16 
                                    // smallest N), so the last tile of a range may be narrower
 constexpr int kTileBytes = kLmM * kLmK * 2;   // 16 KB: a hidden-state tile
 constexpr int kWTileBytes = kLmN * kLmK * 2;  // 32 KB: a weight stage
-constexpr int kStageBytes2 = 2 * kTileBytes;
 constexpr int kLmThreads = 320;    // TMA producer, MMA issuer, 8 epilogue warps
 constexpr int kEpiThreads = 256;   // two epilogue warps a TMEM lane quarter
 constexpr int kTmemCols = 2 * kLmN;
@@ -236,10 +235,6 @@ __device__ __forceinline__ uint32_t lm_key(float x) {
   uint32_t b = __float_as_uint(x);
   b = (b == 0x80000000u) ? 0u : b;
   return b ^ ((uint32_t)((int32_t)b >> 31) | 0x80000000u);
-}
-__device__ __forceinline__ uint64_t lm_comp(uint64_t raw_idx) {  // raw << 32 | idx
-  return ((uint64_t)lm_key(__uint_as_float((uint32_t)(raw_idx >> 32))) << 32) |
-         (uint64_t)(~(uint32_t)raw_idx);
 }
 
 // Index of (slot, row) in the candidate table. Rows are XOR-swizzled by the slot pair so

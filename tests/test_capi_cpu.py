@@ -127,3 +127,20 @@ def test_product_never_imports_the_oracle():
             if f.endswith((".py", ".cu", ".cuh", ".h", ".cpp")):
                 text = open(os.path.join(dirpath, f), errors="replace").read()
                 assert "oracle" not in re.sub(r"#.*|//.*", "", text).lower() or f == "__init__.py", f
+
+
+def test_exchange_rejects_bad_arguments_before_touching_the_device():
+    """tabby_exchange_create validates world, rank and max_rows first (no GPU needed)."""
+    import ctypes
+
+    from tabby_b200 import _lib
+
+    L = _lib.lib()
+    h = ctypes.c_void_p()
+    for world, rank, rows in ((0, 0, 8), (17, 0, 8), (2, 2, 8), (2, -1, 8), (2, 0, 0)):
+        assert L.tabby_exchange_create(0, world, rank, rows, ctypes.byref(h)) == _lib.TABBY_EINVAL
+        assert h.value is None
+    assert L.tabby_exchange_create(0, 1, 0, 8, None) == _lib.TABBY_EINVAL
+    assert L.tabby_exchange_merge_async(None, 1, None, None, None, None) == _lib.TABBY_EINVAL
+    assert b"exchange" in L.tabby_last_error()
+    assert L.tabby_exchange_destroy(None) == _lib.TABBY_OK
