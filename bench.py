@@ -524,6 +524,27 @@ def sweep_points(sampler, x, p, u, dev, steps):
 SWEEP_ROWS = (1, 2, 4, 8, 16, 32, 64, 128, 256)
 
 
+def run_sharded_only(args, rank, local_rank, world):
+    """`--sharded`: the vocab-sharded c5 step alone (NCCL all-gather, then peer exchange)."""
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    pg = None
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+        pg = dist
+    lines = [run_sharded(args, rank, local_rank, world, dev, pg),
+             run_sharded(args, rank, local_rank, world, dev, pg, "peer")]
+    if rank == 0:
+        for line in lines:
+            print(json.dumps(line), flush=True)
+    if pg is not None:
+        dist.destroy_process_group()
+    return 0
+
+
 def run_sweep(args):
     """Batch sweep on one GPU (one JSON line)."""
     import torch
@@ -697,6 +718,8 @@ def main():
     ap.add_argument("--softmax", action="store_true", help="softmax_rows shapes on one GPU")
     ap.add_argument("--lmhead", action="store_true", help="fused LM head + sampling on one GPU")
     ap.add_argument("--rows", default="", help="--lmhead: comma-separated batch sizes")
+    ap.add_argument("--sharded", action="store_true",
+                    help="only the vocab-sharded c5 step, both exchanges (one line each)")
     ap.add_argument("--profile", action="store_true",
                     help="only warm-up + timed steps (for ncu): no heat loop, e2e or CPU leg")
     args = ap.parse_args()
@@ -711,6 +734,8 @@ def main():
         return run_softmax(args) if rank == 0 else 0
     if args.lmhead:
         return run_lmhead(args) if rank == 0 else 0
+    if args.sharded:
+        return run_sharded_only(args, rank, local_rank, world)
     return run_ours(args, rank, local_rank, world)
 
 

@@ -27,7 +27,10 @@
 //                  estimate (falling back to an exact re-filter), keeps and sorts the k
 //                  best (binned ranking) and runs sampleFromTopK in float64
 //                  (finalize.cuh); with a device RNG state the draw is made here.
-//   merge_kernel   the vocab-sharded finish: merges all-gathered per-shard blocks.
+//   merge_kernel   the vocab-sharded finish: one warp a row merges the all-gathered
+//                  per-shard blocks (register bitonic merges) and runs finalize_warp.
+//   xmerge_kernel  the same merge with the exchange inside: peers' blocks read over
+//                  NVLink, each rank merging its share of the rows (exchange.cu).
 //
 // Selection works on the raw logits; temperature only enters the float64 finalize,
 // exactly as sampler.ts:144-146 and :170 do. Ties go to the lower index, as
@@ -58,8 +61,7 @@ constexpr int kFinishCap = (kStageBytes - 2048 * 4) / 8;
 constexpr int kBins = 2048;               // radix digit: 11 bits
 constexpr int kMaxChunks = 32;            // chunks of one row (warp stats: chunks x 16 <= 512)
 constexpr int kMinChunk = 8192;           // logits: below this a row is not split further
-constexpr int kMergeThreads = 512;
-constexpr int kMaxShards = 16;           // shards the merge takes (candidates <= 2 x kMergeThreads)
+constexpr int kMaxShards = 16;           // shards the merge takes (tabby_shard_merge_async's limit)
 static_assert(kRowGroups == kScratchGroups && kFinishCap >= 8192 &&
                   kRowGroups / (kMaxChunks * kWarps) >= 16 && kMaxChunks == kScratchChunks &&
                   kWarps == kScratchWarps && kMaxChunks * kWarps <= kThreads,
@@ -2094,101 +2096,113 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
 }
 
 // ------------------------------------------------------------------------------------
-// Vocab-sharded finish: one CTA per row over the all-gathered shard blocks.
+// Vocab-sharded finish: one warp per row over the shard blocks (all-gathered, or in peer memory).
 // ------------------------------------------------------------------------------------
-// One row of the vocab-sharded merge (block-uniform call): block s of the row is at
-// bases[s] + src_row * a.block_ld. Writes the outcome to *out (and *out2 unless NULL);
-// `status_in` (TABBY_OK or an
-// error found by the caller) overrides the outcome's status.
-__device__ __noinline__ void merge_row(const MergeLaunch &a, int row, int src_row,
-                                       const float *const *bases, uint32_t status_in,
-                                       tabby_sample_outcome *out, tabby_sample_outcome *out2,
-                                       unsigned char *smem_raw, Shared *sh) {
-  const int tid = threadIdx.x;
-  const int total = a.shards * TABBY_SHARD_TOP_K;
-  uint64_t *cand = reinterpret_cast<uint64_t *>(smem_raw);
-  double *exact = reinterpret_cast<double *>(cand + 2 * kMergeThreads);
-  double *scaled = exact + TABBY_SHARD_TOP_K;
-  double *cum = scaled + TABBY_SHARD_TOP_K;
-  int32_t *ids = reinterpret_cast<int32_t *>(cum + TABBY_SHARD_TOP_K);
-  float *vals = reinterpret_cast<float *>(ids + TABBY_SHARD_TOP_K);
+// One row of the vocab-sharded merge by one warp: block s of the row is at
+// bases[s] + src_row * a.block_ld. The shards' candidate lists (at most 64 each, sorted)
+// are merged into the row's best 64 in registers (lane l holds 2l and 2l + 1), the
+// (max, sum-exp) pairs are combined in shard order, and finalize_warp samples. Writes the
+// outcome to *out (and *out2 unless NULL); `status_in` (TABBY_OK or an error found by the
+// caller) overrides the outcome's status. `scratch`: 192 doubles of this warp.
+__device__ __noinline__ void merge_row_warp(const MergeLaunch &a, int row, int src_row,
+                                            const float *const *bases, uint32_t status_in,
+                                            tabby_sample_outcome *out,
+                                            tabby_sample_outcome *out2, double *scratch) {
+  const unsigned kAll = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
   const tabby_sampling_params p = a.params[row];
   auto blk = [&](int s) { return bases[s] + (int64_t)src_row * a.block_ld; };
-
-  if (tid == 0) {
-    // M = max m_s; S = sum s_s * exp(m_s - M), shards in rank order.
-    float mx = -3.40282347e38f;
-    uint32_t bad = 0;
+  // M = max m_s; S = sum s_s * exp(m_s - M), shards in rank order (lane 0).
+  float mx = -3.40282347e38f;
+  double S = 0.0;
+  uint32_t bad = 0;
+  if (lane == 0) {
     for (int s = 0; s < a.shards; s++) {
       const float ms = blk(s)[0];
       if (ms != ms) bad = kFlagBadInput;
       mx = fmaxf(mx, ms);
     }
-    double S = 0.0;
     for (int s = 0; s < a.shards; s++) {
       const float *b = blk(s);
       if (b[1] > 0.f)
         S = JS_ADD(S, JS_MUL((double)b[1], js_exp(JS_SUB((double)b[0], (double)mx))));
     }
     if (isnan(p.temperature) || isnan(p.top_p)) bad |= kFlagBadParams;
-    sh->merge_max = mx;
-    sh->merge_sum = (float)S;
-    sh->flags = bad;
-    sh->count = 0;
   }
-  __syncthreads();
-  for (int i = tid; i < total; i += kMergeThreads) {
-    const int s = i / TABBY_SHARD_TOP_K, j = i % TABBY_SHARD_TOP_K;
-    const float *b = blk(s);
-    const uint32_t gi = __float_as_uint(b[3 + 2 * j]);
-    if (gi != 0xffffffffu) cand[atomicAdd(&sh->count, 1u)] = composite(key_of(b[2 + 2 * j]), gi);
+  mx = __shfl_sync(kAll, mx, 0);
+  S = __shfl_sync(kAll, S, 0);
+  bad = __shfl_sync(kAll, bad, 0);
+  // The best 64 composites of all shards (0 = empty slot).
+  uint64_t v0 = 0, v1 = 0;
+  for (int s = 0; s < a.shards; s++) {
+    const float *b = blk(s) + 2;
+    uint64_t c0 = 0, c1 = 0;
+    const uint32_t g0 = __float_as_uint(b[4 * lane + 1]), g1 = __float_as_uint(b[4 * lane + 3]);
+    if (g0 != 0xffffffffu) c0 = composite(key_of(b[4 * lane]), g0);
+    if (g1 != 0xffffffffu) c1 = composite(key_of(b[4 * lane + 2]), g1);
+    warp_sort64_desc(c0, c1);
+    if (s == 0) {
+      v0 = c0;
+      v1 = c1;
+    } else {
+      warp_merge64_desc(v0, v1, c0, c1);
+    }
   }
-  __syncthreads();
-  const int nc = (int)sh->count;
-  block_sort_desc(cand, nc);
+  const int nc = __popc(__ballot_sync(kAll, v0 != 0)) + __popc(__ballot_sync(kAll, v1 != 0));
   const int k = pool_rule(p.temperature, p.top_k, TABBY_SHARD_TOP_K);
   const int kk = min(k, nc);
-  for (int i = tid; i < kk; i += kMergeThreads) {
-    const uint64_t e = cand[i];
-    const uint32_t key = (uint32_t)(e >> 32);
-    const uint32_t gi = ~(uint32_t)e;
-    float v = float_of_key(key);
-    if (key == 0x80000000u) {
-      // Recover the sign of a zero from the shard block that holds it.
+  const int32_t id0 = (int32_t)~(uint32_t)v0, id1 = (int32_t)~(uint32_t)v1;
+  float x0 = float_of_key((uint32_t)(v0 >> 32)), x1 = float_of_key((uint32_t)(v1 >> 32));
+  // Recover the sign of a zero logit from the shard block that holds it (rare).
+  for (int e = 0; e < 2; e++) {
+    const uint64_t c = e ? v1 : v0;
+    if (2 * lane + e < kk && (uint32_t)(c >> 32) == 0x80000000u) {
+      const uint32_t gi = ~(uint32_t)c;
       for (int s = 0; s < a.shards; s++) {
         const float *b = blk(s);
         for (int j = 0; j < TABBY_SHARD_TOP_K; j++)
-          if (__float_as_uint(b[3 + 2 * j]) == gi) v = b[2 + 2 * j];
+          if (__float_as_uint(b[3 + 2 * j]) == gi) {
+            if (e)
+              x1 = b[2 + 2 * j];
+            else
+              x0 = b[2 + 2 * j];
+          }
       }
     }
-    ids[i] = (int32_t)gi;
-    vals[i] = v;
   }
-  __syncthreads();
-  const float max_logit = kk > 0 ? vals[0] : sh->merge_max;
-  const uint32_t flags = sh->flags;
-  const uint32_t status = status_in != TABBY_OK          ? status_in
-                          : (flags & kFlagBadInput)    ? (uint32_t)TABBY_EINPUT
-                          : (flags & kFlagBadParams) ? (uint32_t)TABBY_EINVAL
-                                                     : (uint32_t)TABBY_OK;
-  if (a.topk_ids)
-    for (int i = tid; i < kk; i += kMergeThreads) a.topk_ids[(int64_t)row * a.topk_ld + i] = ids[i];
-  if (a.topk_values)
-    for (int i = tid; i < kk; i += kMergeThreads)
-      a.topk_values[(int64_t)row * a.topk_ld + i] = vals[i];
-  finalize_sample(ids, vals, kk, max_logit, sh->merge_sum, p, a.uniforms[row], cum, scaled,
-                  sh, out, status, out2);
+  const float max_logit = kk > 0 ? __shfl_sync(kAll, x0, 0) : mx;
+  const uint32_t status = status_in != TABBY_OK        ? status_in
+                          : (bad & kFlagBadInput)    ? (uint32_t)TABBY_EINPUT
+                          : (bad & kFlagBadParams) ? (uint32_t)TABBY_EINVAL
+                                                   : (uint32_t)TABBY_OK;
+  if (a.topk_ids) {
+    if (2 * lane < kk) a.topk_ids[(int64_t)row * a.topk_ld + 2 * lane] = id0;
+    if (2 * lane + 1 < kk) a.topk_ids[(int64_t)row * a.topk_ld + 2 * lane + 1] = id1;
+  }
+  if (a.topk_values) {
+    if (2 * lane < kk) a.topk_values[(int64_t)row * a.topk_ld + 2 * lane] = x0;
+    if (2 * lane + 1 < kk) a.topk_values[(int64_t)row * a.topk_ld + 2 * lane + 1] = x1;
+  }
+  finalize_warp(id0, id1, x0, x1, kk, max_logit, (float)S, p, a.uniforms[row], scratch, out,
+                status);
+  if (out2) {
+    __syncwarp();
+    if (lane == 0) *out2 = *out;  // lane 0 wrote *out
+  }
 }
 
-__global__ void __launch_bounds__(kMergeThreads) merge_kernel(MergeLaunch a) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  __shared__ Shared sh_s;
+constexpr int kMergeWarps = 4;  // rows a merge CTA (one warp a row)
+
+__global__ void __launch_bounds__(32 * kMergeWarps) merge_kernel(MergeLaunch a) {
   __shared__ const float *bases[kMaxShards];
+  __shared__ double scratch[kMergeWarps][192];
   if (threadIdx.x < a.shards)
     bases[threadIdx.x] = a.gathered + (int64_t)threadIdx.x * a.rows * a.block_ld;
   __syncthreads();
-  const int row = blockIdx.x;
-  merge_row(a, row, row, bases, TABBY_OK, &a.out[row], nullptr, smem_raw, &sh_s);
+  const int warp = threadIdx.x >> 5;
+  const int row = blockIdx.x * kMergeWarps + warp;
+  if (row < a.rows)
+    merge_row_warp(a, row, row, bases, TABBY_OK, &a.out[row], nullptr, scratch[warp]);
 }
 
 // ------------------------------------------------------------------------------------
@@ -2251,11 +2265,10 @@ __device__ __forceinline__ T pick(const T (&arr)[TABBY_EXCHANGE_MAX_WORLD], int 
   return v;
 }
 
-__global__ void __launch_bounds__(kMergeThreads) xmerge_kernel(const __grid_constant__ XMergeLaunch x) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  __shared__ Shared sh_s;
+__global__ void __launch_bounds__(32 * kMergeWarps) xmerge_kernel(const __grid_constant__ XMergeLaunch x) {
   __shared__ const float *bases[kMaxShards];
-  __shared__ uint32_t missing;
+  __shared__ double scratch[kMergeWarps][192];
+  __shared__ uint32_t missing, last;
   const MergeLaunch &a = x.m;
   const int tid = threadIdx.x;
   if (tid < x.world) bases[tid] = pick(x.peer_blocks, tid);
@@ -2268,19 +2281,21 @@ __global__ void __launch_bounds__(kMergeThreads) xmerge_kernel(const __grid_cons
   if (tid == 0) missing = wait_flags(x.flags, x.world, x.rank, x.epoch, x.timeout_ns);
   __syncthreads();
   const int nloc = xrow0(a.rows, x.world, x.rank + 1) - xrow0(a.rows, x.world, x.rank);
-  if ((int)blockIdx.x < nloc) {
-    const int row = xrow0(a.rows, x.world, x.rank) + blockIdx.x;
+  const int warp = tid >> 5;
+  const int li = (int)blockIdx.x * kMergeWarps + warp;  // this warp's row among this rank's
+  if (li < nloc) {
+    const int row = xrow0(a.rows, x.world, x.rank) + li;
     // The outcome to this rank's buffer (for the peers) and to the caller's.
-    merge_row(a, row, row, bases, missing ? (uint32_t)TABBY_ETIMEOUT : (uint32_t)TABBY_OK,
-              &x.outs[row], &a.out[row], smem_raw, &sh_s);
+    merge_row_warp(a, row, row, bases, missing ? (uint32_t)TABBY_ETIMEOUT : (uint32_t)TABBY_OK,
+                   &x.outs[row], &a.out[row], scratch[warp]);
   }
   __syncthreads();
   if (tid == 0) {
-    __threadfence();  // this CTA's outcome is written before it is counted
-    sh_s.last = atomicAdd(x.counter, 1u) == gridDim.x - 1 ? 1u : 0u;
+    __threadfence();  // this CTA's outcomes are written before they are counted
+    last = atomicAdd(x.counter, 1u) == gridDim.x - 1 ? 1u : 0u;
   }
   __syncthreads();
-  if (!sh_s.last) return;
+  if (!last) return;
   // The last CTA: every outcome of this rank is written; say so to every rank, wait for
   // every rank's word, then read each row's outcome from the rank that owns it.
   if (tid == 0) *x.counter = 0u;
@@ -2293,7 +2308,7 @@ __global__ void __launch_bounds__(kMergeThreads) xmerge_kernel(const __grid_cons
   __syncthreads();
   const uint32_t late = missing;
   const int mine0 = xrow0(a.rows, x.world, x.rank), mine1 = xrow0(a.rows, x.world, x.rank + 1);
-  for (int i = tid; i < a.rows; i += kMergeThreads) {
+  for (int i = tid; i < a.rows; i += blockDim.x) {
     if (i >= mine0 && i < mine1) continue;  // written by this rank's CTAs
     int owner = 0;
     while (owner + 1 < x.world && xrow0(a.rows, x.world, owner + 1) <= i) owner++;
@@ -2439,18 +2454,15 @@ cudaError_t launch_rows(const RowLaunch &l, const RowGeometry &geo, const Scratc
 }
 
 cudaError_t launch_xmerge(const XMergeLaunch &l, cudaStream_t stream) {
-  const size_t smem =
-      (size_t)2 * kMergeThreads * 8 + (size_t)TABBY_SHARD_TOP_K * (3 * 8 + 4 + 4);
   const int nloc = xrow0(l.m.rows, l.world, l.rank + 1) - xrow0(l.m.rows, l.world, l.rank);
-  xmerge_kernel<<<std::max(nloc, 1), kMergeThreads, smem, stream>>>(l);
+  const int grid = std::max((nloc + kMergeWarps - 1) / kMergeWarps, 1);
+  xmerge_kernel<<<grid, 32 * kMergeWarps, 0, stream>>>(l);
   return cudaGetLastError();
 }
 
 cudaError_t launch_merge(const MergeLaunch &l, cudaStream_t stream) {
   if (l.rows == 0) return cudaSuccess;
-  const size_t smem =
-      (size_t)2 * kMergeThreads * 8 + (size_t)TABBY_SHARD_TOP_K * (3 * 8 + 4 + 4);
-  merge_kernel<<<l.rows, kMergeThreads, smem, stream>>>(l);
+  merge_kernel<<<(l.rows + kMergeWarps - 1) / kMergeWarps, 32 * kMergeWarps, 0, stream>>>(l);
   return cudaGetLastError();
 }
 
