@@ -191,15 +191,14 @@ TABBY_API int tabby_shard_merge_async(tabby_sampler *sampler, const float *d_gat
  *   1. tabby_exchange_create; tabby_exchange_ipc_handle gives this rank's
  *      TABBY_EXCHANGE_HANDLE_BYTES-byte CUDA IPC handle; the caller moves the handles
  *      between processes (rank-major) and passes all of them to tabby_exchange_open;
- *   2. every call: tabby_shard_local_async writes this rank's blocks into the buffer
- *      tabby_exchange_blocks returns; then tabby_exchange_merge_async on the same stream.
- *      It publishes this rank's blocks, waits for every rank's, merges the rows this rank
- *      owns (rows [r * rows / world, (r + 1) * rows / world)) into its own buffer, waits
- *      for every rank's rows and reads them from their owners' buffers, and writes all
+ *   2. every step: tabby_shard_local_async writes this rank's blocks into the buffer
+ *      tabby_exchange_blocks returns (ask before every step: two buffers alternate), then
+ *      tabby_exchange_merge_async on the same stream. It announces this rank's blocks to
+ *      every peer (a release store into the peer's flag word), waits for every peer's
+ *      word, then merges every row reading the peers' blocks over NVLink, and writes all
  *      `rows` outcomes to d_out, the same on every rank. Every rank must make the same
  *      calls in the same order with the same `rows`, params and uniforms. A wait that
- *      runs out (0.5 s) gives the affected rows status TABBY_ETIMEOUT; the kernel always
- *      returns.
+ *      runs out (0.5 s) gives every row status TABBY_ETIMEOUT; the kernel always returns.
  *   3. tabby_exchange_destroy only after every rank's last merge has completed (e.g. after
  *      a device synchronize and a barrier between the processes).
  * 1 <= world <= TABBY_EXCHANGE_MAX_WORLD; pool sizes above TABBY_SHARD_TOP_K are clipped.

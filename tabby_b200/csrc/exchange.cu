@@ -4,12 +4,12 @@
 // through a CUDA IPC handle (the caller moves the 64-byte handles between processes, e.g.
 // with torch.distributed.all_gather_object). After tabby_exchange_open every rank holds
 // device pointers to every rank's buffer, and tabby_exchange_merge_async runs the merge
-// with the exchange inside the kernel: peer loads of the blocks and peer stores of the
-// outcomes over NVLink, ordered by release/acquire flag words (xmerge_kernel). No
-// collective library is involved and nothing uses multicast.
+// with the exchange inside the kernel: one release/acquire handshake on flag words, then
+// peer loads of the blocks over NVLink (xmerge_kernel). No collective library is involved
+// and nothing uses multicast.
 //
-// Buffer layout (each section 256-byte aligned): blocks [max_rows][kBlockLd] f32, outcomes
-// [max_rows], flags [2 * world] u32 (arrive, done), the CTA counter.
+// Buffer layout (each section 256-byte aligned): two block buffers [max_rows][kBlockLd]
+// f32 (step e writes and reads the one of parity e & 1), arrive words [world] u32.
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -27,13 +27,12 @@ constexpr uint64_t kTimeoutNs = 500ull * 1000ull * 1000ull;  // bounded waits: 0
 size_t section(size_t b) { return (b + 255) / 256 * 256; }
 
 struct Layout {
-  size_t blocks, outs, flags, counter, bytes;
+  size_t blocks, block_bytes, flags, bytes;
   explicit Layout(int max_rows, int world) {
     blocks = 0;
-    outs = blocks + section((size_t)max_rows * kBlockLd * 4);
-    flags = outs + section((size_t)max_rows * sizeof(tabby_sample_outcome));
-    counter = flags + section((size_t)2 * world * 4);
-    bytes = counter + section(4);
+    block_bytes = section((size_t)max_rows * kBlockLd * 4);
+    flags = blocks + 2 * block_bytes;
+    bytes = flags + section((size_t)world * 4);
   }
 };
 
@@ -153,7 +152,9 @@ int tabby_exchange_open(tabby_exchange *x, const void *handles) {
 
 int tabby_exchange_blocks(tabby_exchange *x, float **d_blocks, int32_t *block_ld) {
   if (!x || !d_blocks || !block_ld) return xfail(TABBY_EINVAL, "arguments must not be NULL");
-  *d_blocks = reinterpret_cast<float *>(x->base + x->lay.blocks);
+  // The buffer the next merge reads: the parity of the next epoch.
+  const uint32_t next = x->epoch + 1u;
+  *d_blocks = reinterpret_cast<float *>(x->base + x->lay.blocks + (next & 1u) * x->lay.block_bytes);
   *block_ld = kBlockLd;
   return TABBY_OK;
 }
@@ -169,9 +170,10 @@ int tabby_exchange_merge_async(tabby_exchange *x, int32_t rows,
     return xfail(TABBY_EINVAL, "params, uniforms and out must not be NULL");
   DeviceScope scope(x->device);
   if (scope.err != cudaSuccess) return xcuda(scope.err, "cudaSetDevice");
-  // Every rank makes the same calls in the same order, so the epochs agree; 0 is skipped
-  // (the flag words start at 0).
-  if (++x->epoch == 0u) x->epoch = 1u;
+  // Every rank makes the same calls in the same order, so the epochs agree. The flag words
+  // start at 0 and the first epoch is 1; after a wrap to 0 they hold 0xffffffff, so no
+  // word ever matches an epoch its rank has not announced.
+  ++x->epoch;
   tabby::XMergeLaunch l;
   l.m.rows = rows;
   l.m.shards = x->world;
@@ -179,14 +181,12 @@ int tabby_exchange_merge_async(tabby_exchange *x, int32_t rows,
   l.m.params = d_params;
   l.m.uniforms = d_uniforms;
   l.m.out = d_out;
+  const size_t par = (x->epoch & 1u) * x->lay.block_bytes;
   for (int q = 0; q < x->world; q++) {
-    l.peer_blocks[q] = reinterpret_cast<const float *>(x->peer_base[q] + x->lay.blocks);
-    l.peer_outs[q] = reinterpret_cast<tabby_sample_outcome *>(x->peer_base[q] + x->lay.outs);
+    l.peer_blocks[q] = reinterpret_cast<const float *>(x->peer_base[q] + x->lay.blocks + par);
     l.peer_flags[q] = reinterpret_cast<uint32_t *>(x->peer_base[q] + x->lay.flags);
   }
   l.flags = reinterpret_cast<uint32_t *>(x->base + x->lay.flags);
-  l.counter = reinterpret_cast<uint32_t *>(x->base + x->lay.counter);
-  l.outs = reinterpret_cast<tabby_sample_outcome *>(x->base + x->lay.outs);
   l.rank = x->rank;
   l.world = x->world;
   l.epoch = x->epoch;

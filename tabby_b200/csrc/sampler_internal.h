@@ -52,18 +52,16 @@ struct MergeLaunch {
 };
 
 // The vocab-sharded merge with its exchange over peer memory (xmerge_kernel). Each rank's
-// exchange buffer holds its blocks [max_rows][block_ld], the outcomes of all rows
-// [max_rows] (each written by the rank that owns the row) and 2 * world flag words
-// (arrive, done: slot q written by rank q with the call's epoch).
+// exchange buffer holds two block buffers [max_rows][block_ld] (a step writes the one of
+// its epoch's parity) and `world` arrive words (slot q written by rank q with the epoch
+// of the step whose blocks it has published).
 struct XMergeLaunch {
-  MergeLaunch m;                             // rows = all rows; gathered unused; out = caller's
-  // Every rank's buffers, by rank (kernel parameters: no dependent load to find them).
+  MergeLaunch m;  // rows = all rows; gathered unused; out = the caller's
+  // Every rank's block buffer of this step, by rank (kernel parameters: no dependent load
+  // to find them).
   const float *peer_blocks[TABBY_EXCHANGE_MAX_WORLD] = {};
-  tabby_sample_outcome *peer_outs[TABBY_EXCHANGE_MAX_WORLD] = {};
-  uint32_t *peer_flags[TABBY_EXCHANGE_MAX_WORLD] = {};
-  uint32_t *flags = nullptr;                 // this rank's flag words
-  uint32_t *counter = nullptr;               // CTAs done (the last one resets it)
-  tabby_sample_outcome *outs = nullptr;      // this rank's outcome buffer
+  uint32_t *peer_flags[TABBY_EXCHANGE_MAX_WORLD] = {};  // every rank's arrive words
+  uint32_t *flags = nullptr;                            // this rank's arrive words
   int32_t rank = 0;
   int32_t world = 1;
   uint32_t epoch = 0;

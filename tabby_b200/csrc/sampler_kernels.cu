@@ -29,8 +29,8 @@
 //                  (finalize.cuh); with a device RNG state the draw is made here.
 //   merge_kernel   the vocab-sharded finish: one warp a row merges the all-gathered
 //                  per-shard blocks (register bitonic merges) and runs finalize_warp.
-//   xmerge_kernel  the same merge with the exchange inside: peers' blocks read over
-//                  NVLink, each rank merging its share of the rows (exchange.cu).
+//   xmerge_kernel  the same merge with the exchange inside: the peers' blocks read over
+//                  NVLink after one release/acquire handshake (exchange.cu).
 //
 // Selection works on the raw logits; temperature only enters the float64 finalize,
 // exactly as sampler.ts:144-146 and :170 do. Ties go to the lower index, as
@@ -616,13 +616,11 @@ __device__ __noinline__ uint64_t shrink_to(uint64_t *cand, int n, int k, int lim
 // exp(l - max) / sumExp of the chosen candidate, computed exactly (js_exp); poolMass is
 // the parallel sum (within 1e-12 relative of the reference's) unless the replay ran.
 // ------------------------------------------------------------------------------------
-template <bool kSecondOut>
-__device__ __noinline__ void finalize_sample_t(const int32_t *ids, const float *vals, int n,
+__device__ __noinline__ void finalize_sample(const int32_t *ids, const float *vals, int n,
                                              float max_logit, float sum_exp,
                                              tabby_sampling_params p, double u, double *cum,
                                              double *work, Shared *sh,
-                                             tabby_sample_outcome *out, uint32_t status,
-                                             tabby_sample_outcome *out2) {
+                                             tabby_sample_outcome *out, uint32_t status) {
   const int tid = threadIdx.x;
   if (status != TABBY_OK || n == 0) {
     if (tid == 0) {
@@ -638,7 +636,6 @@ __device__ __noinline__ void finalize_sample_t(const int32_t *ids, const float *
       o.status = status != TABBY_OK ? (int32_t)status : (int32_t)TABBY_EEMPTY;
       o.reserved = 0;
       *out = o;
-      if (kSecondOut) *out2 = o;
     }
     return;
   }
@@ -738,26 +735,9 @@ __device__ __noinline__ void finalize_sample_t(const int32_t *ids, const float *
     o.status = TABBY_OK;
     o.reserved = fallback ? 1 : 0;  // 1 when the sequential replay decided
     *out = o;
-    if (kSecondOut) *out2 = o;
   }
 }
 
-
-// sampleFromTopK writing one outcome (the row pass), or two (the exchange merge: the
-// peers' copy and the caller's).
-__device__ __forceinline__ void finalize_sample(const int32_t *ids, const float *vals, int n,
-                                                float max_logit, float sum_exp,
-                                                tabby_sampling_params p, double u, double *cum,
-                                                double *work, Shared *sh,
-                                                tabby_sample_outcome *out, uint32_t status,
-                                                tabby_sample_outcome *out2 = nullptr) {
-  if (out2)
-    finalize_sample_t<true>(ids, vals, n, max_logit, sum_exp, p, u, cum, work, sh, out, status,
-                            out2);
-  else
-    finalize_sample_t<false>(ids, vals, n, max_logit, sum_exp, p, u, cum, work, sh, out, status,
-                             nullptr);
-}
 
 // The min(64, n) largest of cand[0, n), sorted descending, into cand[0, 64) (zeros past
 // n). Block-uniform call. Every warp keeps a running top 64 of its share in registers
@@ -2102,52 +2082,63 @@ __global__ void __launch_bounds__(kThreads, 2) row_kernel(const __grid_constant_
 // bases[s] + src_row * a.block_ld. The shards' candidate lists (at most 64 each, sorted)
 // are merged into the row's best 64 in registers (lane l holds 2l and 2l + 1), the
 // (max, sum-exp) pairs are combined in shard order, and finalize_warp samples. Writes the
-// outcome to *out (and *out2 unless NULL); `status_in` (TABBY_OK or an error found by the
+// outcome to *out; `status_in` (TABBY_OK or an error found by the
 // caller) overrides the outcome's status. `scratch`: 192 doubles of this warp.
 __device__ __noinline__ void merge_row_warp(const MergeLaunch &a, int row, int src_row,
                                             const float *const *bases, uint32_t status_in,
-                                            tabby_sample_outcome *out,
-                                            tabby_sample_outcome *out2, double *scratch) {
+                                            tabby_sample_outcome *out, double *scratch) {
   const unsigned kAll = 0xffffffffu;
   const int lane = threadIdx.x & 31;
   const tabby_sampling_params p = a.params[row];
   auto blk = [&](int s) { return bases[s] + (int64_t)src_row * a.block_ld; };
-  // M = max m_s; S = sum s_s * exp(m_s - M), shards in rank order (lane 0).
+  // Every load of the row's blocks is issued before any result is used (the blocks may
+  // be in a peer's memory, a round trip over NVLink): lane s takes shard s's (max,
+  // sum-exp); the candidates come four shards at a time, two a lane.
+  float2 stat = make_float2(-3.40282347e38f, 0.f);
+  if (lane < a.shards) stat = *reinterpret_cast<const float2 *>(blk(lane));
+  uint64_t v0 = 0, v1 = 0;  // the best 64 composites of all shards so far (0 = empty slot)
+  for (int s0 = 0; s0 < a.shards; s0 += 4) {
+    float2 lo[4], hi[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      if (s0 + j < a.shards) {
+        const float2 *q = reinterpret_cast<const float2 *>(blk(s0 + j) + 2) + 2 * lane;
+        lo[j] = q[0];  // (value, index bits) of candidate 2l
+        hi[j] = q[1];  // ... of candidate 2l + 1
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      if (s0 + j < a.shards) {
+        uint64_t c0 = 0, c1 = 0;
+        const uint32_t g0 = __float_as_uint(lo[j].y), g1 = __float_as_uint(hi[j].y);
+        if (g0 != 0xffffffffu) c0 = composite(key_of(lo[j].x), g0);
+        if (g1 != 0xffffffffu) c1 = composite(key_of(hi[j].x), g1);
+        warp_sort64_desc(c0, c1);
+        if (s0 + j == 0) {
+          v0 = c0;
+          v1 = c1;
+        } else {
+          warp_merge64_desc(v0, v1, c0, c1);
+        }
+      }
+    }
+  }
+  // M = max m_s; S = sum s_s * exp(m_s - M), shards in rank order (every lane computes
+  // the same values from the pairs the lanes hold).
   float mx = -3.40282347e38f;
   double S = 0.0;
   uint32_t bad = 0;
-  if (lane == 0) {
-    for (int s = 0; s < a.shards; s++) {
-      const float ms = blk(s)[0];
-      if (ms != ms) bad = kFlagBadInput;
-      mx = fmaxf(mx, ms);
-    }
-    for (int s = 0; s < a.shards; s++) {
-      const float *b = blk(s);
-      if (b[1] > 0.f)
-        S = JS_ADD(S, JS_MUL((double)b[1], js_exp(JS_SUB((double)b[0], (double)mx))));
-    }
-    if (isnan(p.temperature) || isnan(p.top_p)) bad |= kFlagBadParams;
-  }
-  mx = __shfl_sync(kAll, mx, 0);
-  S = __shfl_sync(kAll, S, 0);
-  bad = __shfl_sync(kAll, bad, 0);
-  // The best 64 composites of all shards (0 = empty slot).
-  uint64_t v0 = 0, v1 = 0;
   for (int s = 0; s < a.shards; s++) {
-    const float *b = blk(s) + 2;
-    uint64_t c0 = 0, c1 = 0;
-    const uint32_t g0 = __float_as_uint(b[4 * lane + 1]), g1 = __float_as_uint(b[4 * lane + 3]);
-    if (g0 != 0xffffffffu) c0 = composite(key_of(b[4 * lane]), g0);
-    if (g1 != 0xffffffffu) c1 = composite(key_of(b[4 * lane + 2]), g1);
-    warp_sort64_desc(c0, c1);
-    if (s == 0) {
-      v0 = c0;
-      v1 = c1;
-    } else {
-      warp_merge64_desc(v0, v1, c0, c1);
-    }
+    const float ms = __shfl_sync(kAll, stat.x, s);
+    if (ms != ms) bad = kFlagBadInput;
+    mx = fmaxf(mx, ms);
   }
+  for (int s = 0; s < a.shards; s++) {
+    const float ms = __shfl_sync(kAll, stat.x, s), ss = __shfl_sync(kAll, stat.y, s);
+    if (ss > 0.f) S = JS_ADD(S, JS_MUL((double)ss, js_exp(JS_SUB((double)ms, (double)mx))));
+  }
+  if (isnan(p.temperature) || isnan(p.top_p)) bad |= kFlagBadParams;
   const int nc = __popc(__ballot_sync(kAll, v0 != 0)) + __popc(__ballot_sync(kAll, v1 != 0));
   const int k = pool_rule(p.temperature, p.top_k, TABBY_SHARD_TOP_K);
   const int kk = min(k, nc);
@@ -2185,10 +2176,6 @@ __device__ __noinline__ void merge_row_warp(const MergeLaunch &a, int row, int s
   }
   finalize_warp(id0, id1, x0, x1, kk, max_logit, (float)S, p, a.uniforms[row], scratch, out,
                 status);
-  if (out2) {
-    __syncwarp();
-    if (lane == 0) *out2 = *out;  // lane 0 wrote *out
-  }
 }
 
 constexpr int kMergeWarps = 4;  // rows a merge CTA (one warp a row)
@@ -2202,24 +2189,23 @@ __global__ void __launch_bounds__(32 * kMergeWarps) merge_kernel(MergeLaunch a) 
   const int warp = threadIdx.x >> 5;
   const int row = blockIdx.x * kMergeWarps + warp;
   if (row < a.rows)
-    merge_row_warp(a, row, row, bases, TABBY_OK, &a.out[row], nullptr, scratch[warp]);
+    merge_row_warp(a, row, row, bases, TABBY_OK, &a.out[row], scratch[warp]);
 }
 
 // ------------------------------------------------------------------------------------
 // Vocab-sharded merge with the exchange over NVLink peer memory (one launch a rank).
 //
-// Every rank's local pass has written its blocks into its own exchange buffer. This
-// kernel (1) tells every rank that this rank's blocks of this call are ready (a release
-// store of the call's epoch into each rank's arrive slot for this rank), (2) waits until
-// every rank's arrive slot here holds the epoch, (3) merges the rows this rank owns
-// (rows [row0, row0 + nloc)), reading the blocks straight from the peers' buffers and
-// writing the outcomes into its own buffer, and (4) in the CTA that ends last, tells
-// every rank that this rank's outcomes are written, waits for every rank's word and
-// reads each row's outcome from the buffer of the rank that owns it into the caller's
-// buffer. A rank overwrites its blocks and outcomes only in its next call, after every
-// rank has said it is done with this one. Every wait polls at most `timeout_ns` of
-// %globaltimer; rows whose blocks or outcomes did not arrive in time report
-// TABBY_ETIMEOUT.
+// Every rank's local pass has written its blocks into its own exchange buffer (the one
+// of the step's parity). This kernel (1) tells every peer that this rank's blocks of the
+// step are ready (a system-scope fence, then a release store of the step's epoch into
+// the peer's arrive word for this rank), (2) waits until every peer's arrive word here
+// holds the epoch, and (3) merges every row, one warp a row, reading the peers' blocks
+// straight from their buffers over NVLink. Every rank computes the same outcomes, so
+// nothing else is exchanged. A rank rewrites a block buffer two steps later; by then
+// every peer has announced the step in between, which it does only after its merge of
+// this step has returned, so nobody still reads it. Every wait polls at most
+// `timeout_ns` of %globaltimer; when a peer's word does not arrive in time every row
+// reports TABBY_ETIMEOUT.
 // ------------------------------------------------------------------------------------
 __device__ __forceinline__ void st_release_sys_u32(uint32_t *p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -2250,9 +2236,6 @@ __device__ uint32_t wait_flags(const uint32_t *flags, int n, int skip, uint32_t 
   }
 }
 
-__host__ __device__ __forceinline__ int32_t xrow0(int32_t rows, int32_t world, int32_t r) {
-  return (int32_t)(((int64_t)r * rows) / world);
-}
 
 // Element q of a per-rank pointer array held in the kernel parameters, selected with
 // constant indices (a dynamic index into the parameters would copy them to local memory).
@@ -2268,7 +2251,7 @@ __device__ __forceinline__ T pick(const T (&arr)[TABBY_EXCHANGE_MAX_WORLD], int 
 __global__ void __launch_bounds__(32 * kMergeWarps) xmerge_kernel(const __grid_constant__ XMergeLaunch x) {
   __shared__ const float *bases[kMaxShards];
   __shared__ double scratch[kMergeWarps][192];
-  __shared__ uint32_t missing, last;
+  __shared__ uint32_t missing;
   const MergeLaunch &a = x.m;
   const int tid = threadIdx.x;
   if (tid < x.world) bases[tid] = pick(x.peer_blocks, tid);
@@ -2280,51 +2263,11 @@ __global__ void __launch_bounds__(32 * kMergeWarps) xmerge_kernel(const __grid_c
   // This rank's own blocks are ready by stream order; only the peers' are waited for.
   if (tid == 0) missing = wait_flags(x.flags, x.world, x.rank, x.epoch, x.timeout_ns);
   __syncthreads();
-  const int nloc = xrow0(a.rows, x.world, x.rank + 1) - xrow0(a.rows, x.world, x.rank);
   const int warp = tid >> 5;
-  const int li = (int)blockIdx.x * kMergeWarps + warp;  // this warp's row among this rank's
-  if (li < nloc) {
-    const int row = xrow0(a.rows, x.world, x.rank) + li;
-    // The outcome to this rank's buffer (for the peers) and to the caller's.
+  const int row = (int)blockIdx.x * kMergeWarps + warp;
+  if (row < a.rows)
     merge_row_warp(a, row, row, bases, missing ? (uint32_t)TABBY_ETIMEOUT : (uint32_t)TABBY_OK,
-                   &x.outs[row], &a.out[row], scratch[warp]);
-  }
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();  // this CTA's outcomes are written before they are counted
-    last = atomicAdd(x.counter, 1u) == gridDim.x - 1 ? 1u : 0u;
-  }
-  __syncthreads();
-  if (!last) return;
-  // The last CTA: every outcome of this rank is written; say so to every rank, wait for
-  // every rank's word, then read each row's outcome from the rank that owns it.
-  if (tid == 0) *x.counter = 0u;
-  if (x.world == 1) return;
-  if (tid < x.world && tid != x.rank) {
-    __threadfence_system();
-    st_release_sys_u32(pick(x.peer_flags, tid) + x.world + x.rank, x.epoch);
-  }
-  if (tid == 0) missing = wait_flags(x.flags + x.world, x.world, x.rank, x.epoch, x.timeout_ns);
-  __syncthreads();
-  const uint32_t late = missing;
-  const int mine0 = xrow0(a.rows, x.world, x.rank), mine1 = xrow0(a.rows, x.world, x.rank + 1);
-  for (int i = tid; i < a.rows; i += blockDim.x) {
-    if (i >= mine0 && i < mine1) continue;  // written by this rank's CTAs
-    int owner = 0;
-    while (owner + 1 < x.world && xrow0(a.rows, x.world, owner + 1) <= i) owner++;
-    tabby_sample_outcome o;
-    const unsigned long long *src =
-        reinterpret_cast<const unsigned long long *>(pick(x.peer_outs, owner) + i);
-    unsigned long long *dst = reinterpret_cast<unsigned long long *>(&o);
-#pragma unroll
-    for (int w = 0; w < 6; w++) dst[w] = __ldcv(src + w);
-    if ((late >> owner) & 1u) {
-      o.id = -1;
-      o.considered_count = 0;
-      o.status = TABBY_ETIMEOUT;
-    }
-    a.out[i] = o;
-  }
+                   &a.out[row], scratch[warp]);
 }
 
 // ------------------------------------------------------------------------------------
@@ -2454,8 +2397,7 @@ cudaError_t launch_rows(const RowLaunch &l, const RowGeometry &geo, const Scratc
 }
 
 cudaError_t launch_xmerge(const XMergeLaunch &l, cudaStream_t stream) {
-  const int nloc = xrow0(l.m.rows, l.world, l.rank + 1) - xrow0(l.m.rows, l.world, l.rank);
-  const int grid = std::max((nloc + kMergeWarps - 1) / kMergeWarps, 1);
+  const int grid = std::max((l.m.rows + kMergeWarps - 1) / kMergeWarps, 1);
   xmerge_kernel<<<grid, 32 * kMergeWarps, 0, stream>>>(l);
   return cudaGetLastError();
 }

@@ -17,11 +17,10 @@ merge is deterministic), so no broadcast is needed either. Pool sizes are capped
 64 (TABBY_SHARD_TOP_K), the reference's MAX_TOP_K (kernels.ts:448).
 
 With ``exchange="peer"`` steps 2 and 3 are one kernel instead: each rank's blocks stay in
-its own CUDA-IPC-shared buffer, and tabby_exchange_merge_async reads the peers' blocks
-over NVLink, merges only the rows this rank owns into its own buffer and then reads the
-other rows' outcomes from the ranks that own them (release/acquire flag words order the
-exchange), so the merge work is split across the ranks and no collective library call
-is on the path.
+its own CUDA-IPC-shared buffer (two, used in turn), and tabby_exchange_merge_async
+announces them with a release store into every peer's flag word, waits for the peers'
+words and merges every row reading the peers' blocks over NVLink, so no collective
+library call is on the path.
 
 Row-split data parallelism (independent rows per GPU) needs nothing from this module:
 each rank runs Sampler.sample_batch on its own rows with no collective.
@@ -95,12 +94,18 @@ class PeerExchange:
                 allh = [mine.raw]
             blob = ctypes.create_string_buffer(b"".join(allh), len(allh) * len(mine.raw))
             check(lib().tabby_exchange_open(h, blob))
-            ptr, ld = ctypes.c_void_p(), ctypes.c_int32()
-            check(lib().tabby_exchange_blocks(h, ctypes.byref(ptr), ctypes.byref(ld)))
-            self.blocks_ptr, self.block_ld = ptr.value, ld.value
         except Exception:
             lib().tabby_exchange_destroy(h)
             raise
+
+    def next_blocks(self):
+        """(device pointer, row stride in words) of the block buffer the next merge reads
+        (the two buffers alternate from step to step)."""
+        import ctypes
+
+        ptr, ld = ctypes.c_void_p(), ctypes.c_int32()
+        check(lib().tabby_exchange_blocks(self.handle, ctypes.byref(ptr), ctypes.byref(ld)))
+        return ptr.value, ld.value
 
     def close(self) -> None:
         """Frees the buffer; call on every rank after a barrier that follows the last merge."""
@@ -113,8 +118,8 @@ class ShardedSampler:
     """Sampling of vocab-sharded rows on this rank's GPU; one instance per rank.
 
     exchange: "gather" (NCCL all-gather of the blocks, then every rank merges every row)
-    or "peer" (PeerExchange: the merge kernel exchanges over peer memory itself; every
-    rank merges its share of the rows and reads the rest from their owners)."""
+    or "peer" (PeerExchange: the merge kernel reads the peers' blocks over peer memory
+    itself after one flag handshake)."""
 
     def __init__(self, vocab: int, device: Optional[int] = None, group=None,
                  max_rows: int = 512, exchange: str = "gather"):
@@ -146,13 +151,14 @@ class ShardedSampler:
             raise ValueError(f"rank {self.rank} holds {self.hi - self.lo} columns, got {sv}")
         if rows > self.exchange.max_rows:
             raise ValueError(f"{rows} rows exceed the exchange's {self.exchange.max_rows}")
+        blocks, ld = self.exchange.next_blocks()
         check(lib().tabby_shard_local_async(self.sampler.handle, x.data_ptr(), x.stride(0), rows,
-                                            sv, self.lo, self.exchange.blocks_ptr,
-                                            self.exchange.block_ld, self.sampler._stream()))
+                                            sv, self.lo, blocks, ld, self.sampler._stream()))
         return rows
 
     def exchange_merge_async(self, rows: int, params_dev, uniforms_dev, out_dev) -> None:
-        """Steps 2-3 in one kernel over peer memory (device tensors, no sync)."""
+        """Steps 2-3 in one kernel over peer memory (device tensors, no sync); every rank
+        must call it once per local_into_exchange, in the same order."""
         check(lib().tabby_exchange_merge_async(self.exchange.handle, rows, params_dev.data_ptr(),
                                                uniforms_dev.data_ptr(), out_dev.data_ptr(),
                                                self.sampler._stream()))
