@@ -20,6 +20,7 @@ using tabby::MergeLaunch;
 using tabby::RowGeometry;
 using tabby::RowLaunch;
 using tabby::Scratch;
+using tabby::DeviceScope;
 
 struct tabby_sampler {
   int32_t device;
@@ -54,19 +55,6 @@ int cuda_fail(cudaError_t err, const char *what) {
   return fail(TABBY_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(err), cudaGetErrorString(err));
 }
 
-// Makes the handle's device current for the scope of a call and restores the caller's.
-struct DeviceScope {
-  int prev = -1;
-  cudaError_t err = cudaSuccess;
-  explicit DeviceScope(int dev) {
-    err = cudaGetDevice(&prev);
-    if (err == cudaSuccess && prev != dev) err = cudaSetDevice(dev);
-  }
-  ~DeviceScope() {
-    int cur = -1;
-    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
-  }
-};
 
 bool aligned4(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
 

@@ -18,6 +18,8 @@
 #include "sampler_internal.h"
 #include "tabby_sample.h"
 
+using tabby::DeviceScope;
+
 namespace {
 
 constexpr int kBlockLd = 2 + 2 * TABBY_SHARD_TOP_K;
@@ -50,18 +52,6 @@ int xcuda(cudaError_t err, const char *what) {
   return xfail(TABBY_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(err), cudaGetErrorString(err));
 }
 
-struct DeviceScope {
-  int prev = -1;
-  cudaError_t err = cudaSuccess;
-  explicit DeviceScope(int dev) {
-    err = cudaGetDevice(&prev);
-    if (err == cudaSuccess && prev != dev) err = cudaSetDevice(dev);
-  }
-  ~DeviceScope() {
-    int cur = -1;
-    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
-  }
-};
 
 }  // namespace
 

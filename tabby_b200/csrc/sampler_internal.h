@@ -178,6 +178,20 @@ cudaError_t launch_rows(const RowLaunch &a, const RowGeometry &geo, const Scratc
                         cudaStream_t stream);
 cudaError_t launch_merge(const MergeLaunch &a, cudaStream_t stream);
 
+// Makes a device current for the scope of a C-ABI call and restores the caller's.
+struct DeviceScope {
+  int prev = -1;
+  cudaError_t err = cudaSuccess;
+  explicit DeviceScope(int dev) {
+    err = cudaGetDevice(&prev);
+    if (err == cudaSuccess && prev != dev) err = cudaSetDevice(dev);
+  }
+  ~DeviceScope() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
 // Records `msg` as the calling thread's tabby_last_error() and returns `status`.
 int set_error(int status, const char *msg);
 
