@@ -56,6 +56,62 @@ def bench_config(world):
                   f"({ROTATE * ROWS * VOCAB * 4 / 1e6:.0f} MB > 126 MB L2)"}
 
 
+def parse_cpulist(text):
+    """'0-3,8,10-11' -> {0, 1, 2, 3, 8, 10, 11} (the sysfs cpulist format)."""
+    cpus = set()
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        lo, _, hi = part.partition("-")
+        cpus.update(range(int(lo), int(hi or lo) + 1))
+    return cpus
+
+
+def gpu_numa_cpus(device_index):
+    """(NUMA node, CPUs of that node this process may run on) for the PCI slot of CUDA
+    device `device_index`, or (None, None) when the host does not say (no sysfs entry,
+    node -1, or none of the node's CPUs in this process's affinity mask)."""
+    try:
+        import torch
+
+        pr = torch.cuda.get_device_properties(device_index)
+        slot = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{slot}/numa_node") as f:
+            node = int(f.read().strip())
+        if node < 0:
+            return None, None
+        with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+            cpus = parse_cpulist(f.read()) & os.sched_getaffinity(0)
+        return (node, cpus) if cpus else (None, None)
+    except (OSError, ValueError, AttributeError, RuntimeError):
+        return None, None
+
+
+class NumaLocal:
+    """Runs the enclosed block on the CPUs of the GPU's NUMA node, so host buffers first
+    touched inside it get pages on the node whose PCIe root holds the GPU (a pinned
+    buffer on the other socket crosses the inter-socket link on every H2D copy); restores
+    the previous affinity on exit. A no-op where the node is unknown."""
+
+    def __init__(self, device_index):
+        self.node, self.cpus = gpu_numa_cpus(device_index)
+        self.prev = None
+
+    def __enter__(self):
+        if self.cpus:
+            try:
+                self.prev = os.sched_getaffinity(0)
+                os.sched_setaffinity(0, self.cpus)
+            except OSError:
+                self.prev = None
+                self.node = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            os.sched_setaffinity(0, self.prev)
+
+
 def cpu_model():
     try:
         with open("/proc/cpuinfo") as f:
@@ -290,20 +346,28 @@ def run_ours(args, rank, local_rank, world):
     # End-to-end through the public host-buffer API: pinned host logits in, outcomes out.
     e2e_steps = 0 if args.profile else max(3, min(args.steps, 50))
     e2e_value = None
+    e2e_node = None
     hout = np.zeros(ROWS, OUTCOME_DTYPE)
     if e2e_steps:
-        host = torch.from_numpy(x).pin_memory()
-        hp = p.copy()
-        hu = u.copy()
-        for _ in range(2):
-            check(L.tabby_sample_rows(h, host.data_ptr(), VOCAB, ROWS, VOCAB, hp.ctypes.data,
-                                      hu.ctypes.data, hout.ctypes.data, None, None, 0))
-        barrier()
-        t0 = time.perf_counter()
-        for _ in range(e2e_steps):
-            check(L.tabby_sample_rows(h, host.data_ptr(), VOCAB, ROWS, VOCAB, hp.ctypes.data,
-                                      hu.ctypes.data, hout.ctypes.data, None, None, 0))
-        e2e_s = time.perf_counter() - t0
+        # Host buffers are allocated and first touched on the GPU's NUMA node.
+        with NumaLocal(local_rank) as numa:
+            e2e_node = numa.node
+            host = torch.empty((ROWS, VOCAB), dtype=torch.float32, pin_memory=True)
+            host.copy_(torch.from_numpy(x))
+            hp = p.copy()
+            hu = u.copy()
+            hout = np.zeros(ROWS, OUTCOME_DTYPE)
+            for _ in range(2):
+                check(L.tabby_sample_rows(h, host.data_ptr(), VOCAB, ROWS, VOCAB,
+                                          hp.ctypes.data, hu.ctypes.data, hout.ctypes.data,
+                                          None, None, 0))
+            barrier()
+            t0 = time.perf_counter()
+            for _ in range(e2e_steps):
+                check(L.tabby_sample_rows(h, host.data_ptr(), VOCAB, ROWS, VOCAB,
+                                          hp.ctypes.data, hu.ctypes.data, hout.ctypes.data,
+                                          None, None, 0))
+            e2e_s = time.perf_counter() - t0
         if pg is not None:
             t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
             pg.all_reduce(t, op=pg.ReduceOp.MAX)
@@ -342,7 +406,8 @@ def run_ours(args, rank, local_rank, world):
             "e2e": {"value": e2e_value, "unit": "rows/s",
                     "h2d_bytes_per_step": ROWS * VOCAB * 4 + p.nbytes + u.nbytes,
                     "d2h_bytes_per_step": hout.nbytes, "steps": e2e_steps,
-                    "call": "tabby_sample_rows (pinned host buffers, synchronous)"},
+                    "call": "tabby_sample_rows (pinned host buffers, synchronous)",
+                    "host_numa_node": e2e_node},
             "gpu_launches": args.steps,  # one cooperative row_kernel launch per call
             "clocks": clocks.summary(),
         }
@@ -383,9 +448,9 @@ def run_sharded(args, rank, local_rank, world, dev, pg, exchange="gather"):
     """Vocab-sharded sampling (c5): every rank holds columns [r*V/N, (r+1)*V/N) of 512
     rows; a step is the local top-64 blocks (row_kernel), then either one NCCL all-gather
     of the blocks (none at N=1) and the merge of every row on every rank (merge_kernel),
-    or (exchange="peer") one xmerge_kernel that reads the peers' blocks over NVLink,
-    merges this rank's rows and stores their outcomes into every rank's buffer. Every
-    rank ends with the same tokens. Strong scaling: the job is 512 rows of the full
+    or (exchange="peer") one xmerge_kernel that announces this rank's blocks, waits for
+    the peers' announcements and merges every row reading the peers' blocks over NVLink.
+    Every rank ends with the same tokens. Strong scaling: the job is 512 rows of the full
     vocabulary whatever N is. Device-timed with CUDA events on the launch stream, max
     over ranks, also per phase."""
     import torch
@@ -460,7 +525,7 @@ def run_sharded(args, rank, local_rank, world, dev, pg, exchange="gather"):
                 "value": SHARD_ROWS / (total / 1e3), "unit": "rows/s", "ms_per_step": total,
                 "steps": steps, "scaling": "strong", "n_gpus": world,
                 "phases_us": {"local_row_kernel": 1e3 * phase[0],
-                              "xmerge_kernel (exchange + merge of this rank's rows)":
+                              "xmerge_kernel (handshake + merge of every row)":
                                   1e3 * phase[2]},
                 "local_columns": s.hi - s.lo,
                 "launches_per_step": "row_kernel + xmerge_kernel (no collective library call)"}
