@@ -182,7 +182,11 @@ int tabby_exchange_merge_async(tabby_exchange *x, int32_t rows,
   l.epoch = x->epoch;
   l.timeout_ns = kTimeoutNs;
   cudaError_t err = tabby::launch_xmerge(l, (cudaStream_t)stream);
-  if (err != cudaSuccess) return xcuda(err, "xmerge_kernel launch");
+  if (err != cudaSuccess) {
+    // Nothing was announced: keep this rank's epoch where the peers expect it.
+    --x->epoch;
+    return xcuda(err, "xmerge_kernel launch");
+  }
   return TABBY_OK;
 }
 
