@@ -300,3 +300,36 @@ def test_batch_uniforms_draw_only_for_sampling_rows():
     want = [nxt() if t > 0 else 0.0 for t in temps]
     assert list(u) == want
     assert rng.next() == nxt()
+
+
+# --- exact decision boundaries -------------------------------------------------------
+# Pools of m equal logits at the row maximum have weights of exactly 1/m (m a power of
+# two), so the cumulative sums hit top_p and u * total exactly. sampler.ts:181 keeps the
+# first i with cumulative >= topP and :199 the first i with target < running: these
+# cases pin both comparisons on the three implementations. Cases are (m, T, top_p, u,
+# expected cut, expected chosen index).
+BOUNDARY_CASES = [
+    (4, 1.0, 0.5, 0.5, 2, 1),      # cumulative == topP at i=1; target == running at i=0
+    (4, 1.0, 1.0, 0.25, 4, 1),     # no nucleus; target == cum[0]
+    (4, 0.7, 0.75, 0.0, 3, 0),     # u = 0 takes the first candidate
+    (2, 1.0, 0.5, 0.9999999, 1, 0),
+    (4, 1.0, 0.5000000000000001, 0.5, 3, 1),  # topP one ulp above cum[1]
+    (4, 1.0, 1.0, 1.0 - 2.0 ** -53, 4, 3),    # largest u below 1: the last candidate
+    (8, 1.3, 0.375, 2.0 / 3.0, 3, 2),  # target rounds to 0.25 == cum[1]
+    (128, 1.0, 0.5, 0.5, 64, 32),  # target == cum[31]
+]
+
+
+def boundary_pool(m):
+    return dict(maxLogit=4.0, sumExp=float(m), ids=[3 * i + 1 for i in range(m)],
+                logits=[4.0] * m)
+
+
+@pytest.mark.parametrize("case", BOUNDARY_CASES)
+def test_exact_boundaries_three_ways(oracle, case):
+    m, t, p, u, cut, chosen = case
+    top = boundary_pool(m)
+    a = py_sample_from_topk(top, t, p, u)
+    assert (a["consideredCount"], a["id"]) == (cut, top["ids"][chosen]), a
+    b, c = _oracle_impl(oracle)(top, t, p, u), _lib_impl()(top, t, p, u)
+    assert a == b == c
