@@ -237,6 +237,18 @@ def test_oracle_argmax_lowest_index_on_ties(oracle):
     assert oracle.topk(row, 1)[0][0] == 17
 
 
+def test_oracle_signed_zeros_tie_on_the_index(oracle):
+    """sampler.ts:28 sorts by `b.value - a.value || a.id - b.id`: +0 and -0 differ by 0,
+    so they tie and the lower id comes first; the values keep their sign bits."""
+    row = np.full(64, -1.0, np.float32)
+    row[[5, 9, 40]] = [-0.0, 0.0, -0.0]
+    ids, vals = oracle.topk(row, 4)
+    np.testing.assert_array_equal(ids, [5, 9, 40, 0])
+    np.testing.assert_array_equal(np.asarray(vals, np.float32).view(np.uint32),
+                                  np.array([-0.0, 0.0, -0.0, -1.0], np.float32).view(np.uint32))
+    assert oracle.argmax(row) == 5  # strictly greater scan: -0 is not above +0
+
+
 @pytest.mark.parametrize("t,k,cap,want", [
     (0.0, 40, 64, 1), (-1.0, 0, 64, 1), (0.7, 0, 64, 64), (0.7, 40, 64, 40),
     (0.7, 100, 64, 64), (0.7, -5, 64, 1), (1.0, 0, 1024, 1024), (1.0, 1000, 1024, 1000),
